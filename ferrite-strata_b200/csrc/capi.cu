@@ -1,0 +1,110 @@
+// Kernel-level C entry points declared in include/strata_b200.h.
+#include "../../include/strata_b200.h"
+#include "k_elem.cuh"
+
+namespace sb {
+std::atomic<uint64_t> g_launches{0};
+}
+
+using namespace sb;
+
+static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+int32_t strata_b200_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed,
+                                uint16_t* scale_bf16, void* stream) {
+  return launch_quant_w4g32(w, n, k, packed, scale_bf16, S(stream));
+}
+
+int32_t strata_b200_quant_w8pc(const float* w, int64_t n, int64_t k, int8_t* q, float* scale,
+                               void* stream) {
+  return launch_quant_w8pc(w, n, k, q, scale, S(stream));
+}
+
+int32_t strata_b200_dequant_w4g32(const uint8_t* packed, const uint16_t* scale_bf16, int64_t n,
+                                  int64_t k, float* w, void* stream) {
+  return launch_dequant_w4g32(packed, scale_bf16, n, k, w, S(stream));
+}
+
+int32_t strata_b200_dequant_w8pc(const int8_t* q, const float* scale, int64_t n, int64_t k,
+                                 float* w, void* stream) {
+  return launch_dequant_w8pc(q, scale, n, k, w, S(stream));
+}
+
+static int32_t linear_common(WFormat fmt, const uint16_t* x, int64_t m, int64_t k, const void* w,
+                             const void* s, int64_t n, const uint16_t* residual, uint16_t* y,
+                             void* stream) {
+  if (m < 0 || k <= 0 || n < 0 || m > INT32_MAX || k > INT32_MAX || n > INT32_MAX)
+    return SB_INVALID_ARGUMENT;
+  LinearBatch b{};
+  b.x = x;
+  b.m = int(m);
+  b.k = int(k);
+  b.fmt = fmt;
+  b.epi = residual ? Epilogue::Residual : Epilogue::None;
+  b.njobs = 1;
+  b.jobs[0] = LinearJob{w, s, int(n), y, int(n), residual, int(n)};
+  return launch_linear(b, S(stream));
+}
+
+int32_t strata_b200_linear_w4g32(const uint16_t* x, int64_t m, int64_t k, const uint8_t* packed,
+                                 const uint16_t* scale_bf16, int64_t n, const uint16_t* residual,
+                                 uint16_t* y, void* stream) {
+  return linear_common(WFormat::W4G32, x, m, k, packed, scale_bf16, n, residual, y, stream);
+}
+
+int32_t strata_b200_linear_w8pc(const uint16_t* x, int64_t m, int64_t k, const int8_t* q,
+                                const float* scale, int64_t n, const uint16_t* residual,
+                                uint16_t* y, void* stream) {
+  return linear_common(WFormat::W8PC, x, m, k, q, scale, n, residual, y, stream);
+}
+
+int32_t strata_b200_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int64_t rows,
+                                  int64_t cols, float eps, uint16_t* y, void* stream) {
+  return launch_rms_norm<uint16_t>(x, gamma, rows, cols, eps, y, S(stream));
+}
+
+int32_t strata_b200_rope_bf16(const uint16_t* x, const int32_t* pos, int64_t rows, int64_t heads,
+                              int64_t head_dim, float theta, uint16_t* y, void* stream) {
+  return launch_rope<uint16_t>(x, pos, rows, heads, head_dim, double(theta), y, S(stream));
+}
+
+int32_t strata_b200_swiglu_bf16(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* y,
+                                void* stream) {
+  return launch_swiglu<uint16_t>(gate, up, n, y, S(stream));
+}
+
+uint64_t strata_b200_attention_decode_scratch_bytes(int64_t batch, int64_t heads,
+                                                    int64_t head_dim, int64_t max_len) {
+  // The split count depends on the kv-head count only through the grid size;
+  // size for the worst case (one kv head per query head).
+  return attention_scratch_bytes(batch, heads, heads, head_dim, max_len) +
+         attention_scratch_bytes(batch, heads, 1, head_dim, max_len);
+}
+
+int32_t strata_b200_attention_decode_bf16(const uint16_t* q, const uint16_t* k_new,
+                                          const uint16_t* v_new, uint16_t* k_cache,
+                                          uint16_t* v_cache, const int32_t* pos, int64_t batch,
+                                          int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                          int64_t max_len, void* scratch, uint16_t* out,
+                                          void* stream) {
+  int rc = launch_kv_append<uint16_t>(k_new, v_new, k_cache, v_cache, pos, batch, 1, kv_heads,
+                                      head_dim, max_len, nullptr, S(stream));
+  if (rc) return rc;
+  return launch_attention<uint16_t>(q, k_cache, v_cache, pos, batch, 1, heads, kv_heads,
+                                    head_dim, max_len, static_cast<float*>(scratch), out, nullptr,
+                                    S(stream));
+}
+
+int32_t strata_b200_embed_bf16(const int32_t* ids, int64_t rows, const uint16_t* table,
+                               int64_t vocab, int64_t dim, uint16_t* out, void* stream) {
+  return launch_embed<uint16_t>(ids, rows, table, vocab, dim, out, nullptr, S(stream));
+}
+
+int32_t strata_b200_argmax_bf16(const uint16_t* x, int64_t rows, int64_t cols, int32_t* out,
+                                void* stream) {
+  return launch_argmax<uint16_t>(x, rows, cols, out, S(stream));
+}
+
+}  // extern "C"

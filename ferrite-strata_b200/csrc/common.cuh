@@ -1,0 +1,79 @@
+// Shared device helpers for the B200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+
+namespace sb {
+
+// Host-side count of kernel launches enqueued by this library.  Launches
+// recorded into a CUDA graph are counted once per replay by the executor.
+extern std::atomic<uint64_t> g_launches;
+
+inline void count_launch(uint64_t n = 1) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
+
+inline int ceil_div(int64_t a, int64_t b) { return int((a + b - 1) / b); }
+
+#if defined(__CUDACC__)
+
+__device__ __forceinline__ float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
+
+// Round-to-nearest-even f32 -> bf16, matching the oracle bit for bit on
+// finite values.
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  return uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 128-bit read-only load that does not allocate in L1 (streamed weights).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+#endif  // __CUDACC__
+
+}  // namespace sb
+
+// Status codes shared with strata_plugin.h.
+#define SB_OK 0
+#define SB_INVALID_ARGUMENT (-3)
+#define SB_RESOURCE_EXHAUSTED (-5)
+#define SB_INTERNAL (-6)
+
+#define SB_LAUNCH_CHECK()                                   \
+  do {                                                      \
+    cudaError_t e_ = cudaGetLastError();                    \
+    if (e_ != cudaSuccess) return SB_INTERNAL;              \
+    sb::count_launch();                                     \
+  } while (0)

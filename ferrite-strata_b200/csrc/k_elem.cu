@@ -1,0 +1,463 @@
+// Row-wise and elementwise kernels: RMSNorm, RoPE, SwiGLU, broadcast add/mul,
+// unary maps, softmax, LayerNorm, transpose/slice/broadcast copies, embedding
+// gather, argmax, and the small f32 contractions the reference's own op set
+// needs (Linear, MatMul).  Templated on the element type: f32 or bf16 (stored
+// as uint16_t), always computing in f32.
+#include "k_elem.cuh"
+
+namespace sb {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld(const T* p, int64_t i);
+template <>
+__device__ __forceinline__ float ld<float>(const float* p, int64_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ld<uint16_t>(const uint16_t* p, int64_t i) { return bf2f(p[i]); }
+
+template <typename T>
+__device__ __forceinline__ void st(T* p, int64_t i, float v);
+template <>
+__device__ __forceinline__ void st<float>(float* p, int64_t i, float v) { p[i] = v; }
+template <>
+__device__ __forceinline__ void st<uint16_t>(uint16_t* p, int64_t i, float v) { p[i] = f2bf(v); }
+
+// Block-wide sum for blockDim.x <= 1024; all threads get the result.
+__device__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : 0.0f;
+  return warp_sum(t);
+}
+
+__device__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : -INFINITY;
+  return warp_max(t);
+}
+
+template <typename T>
+__global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g, int64_t cols,
+                                float eps, T* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  float ss = 0.0f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float v = ld(xr, c);
+    ss = fmaf(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / float(cols) + eps);
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    st(y, row * cols + c, (ld(xr, c) * inv) * ld(g, c));
+}
+
+// Rotate-half RoPE; angles in double, as the oracle computes them.
+template <typename T>
+__global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__ pos, int64_t rows,
+                            int heads, int head_dim, double theta, T* __restrict__ y) {
+  const int half = head_dim / 2;
+  const int64_t total = rows * heads * half;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int j = int(i % half);
+    const int64_t rh = i / half;
+    const int64_t row = rh / heads;
+    const int64_t base = rh * head_dim;
+    const double inv = pow(theta, -2.0 * double(j) / double(head_dim));
+    double s, c;
+    sincos(double(pos[row]) * inv, &s, &c);
+    const double x1 = ld(x, base + j), x2 = ld(x, base + j + half);
+    st(y, base + j, float(x1 * c - x2 * s));
+    st(y, base + j + half, float(x2 * c + x1 * s));
+  }
+}
+
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ gate, const T* __restrict__ up, int64_t n,
+                              T* __restrict__ y) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float gv = ld(gate, i);
+    st(y, i, (gv / (1.0f + expf(-gv))) * ld(up, i));
+  }
+}
+
+// NumPy broadcasting through per-axis strides (0 on broadcast axes).
+template <typename T>
+__global__ void binary_kernel(int op, const T* __restrict__ a, const T* __restrict__ b,
+                              T* __restrict__ out, BcastShape sh) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < sh.total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = i, ia = 0, ib = 0;
+    for (int ax = sh.rank - 1; ax >= 0; --ax) {
+      const int64_t idx = rem % sh.dims[ax];
+      rem /= sh.dims[ax];
+      ia += idx * sh.sa[ax];
+      ib += idx * sh.sb[ax];
+    }
+    const float va = ld(a, ia), vb = ld(b, ib);
+    st(out, i, op == 0 ? va + vb : va * vb);
+  }
+}
+
+__device__ __forceinline__ float erf_as(float x) {
+  // Abramowitz & Stegun 7.1.26, the form the reference CPU backend uses.
+  const float sign = x < 0.0f ? -1.0f : 1.0f;
+  const float ax = fabsf(x);
+  const float t = 1.0f / (1.0f + 0.3275911f * ax);
+  const float poly =
+      ((((1.0614054f * t - 1.4531521f) * t) + 1.4214138f) * t - 0.28449672f) * t + 0.2548296f;
+  return sign * (1.0f - poly * t * expf(-ax * ax));
+}
+
+template <typename T>
+__global__ void unary_kernel(int op, const T* __restrict__ x, int64_t n, T* __restrict__ y) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float v = ld(x, i);
+    float r;
+    if (op == 0) r = 0.5f * v * (1.0f + erf_as(v / 1.41421356237309504880f));
+    else if (op == 1) r = expf(v);
+    else r = logf(v);
+    st(y, i, r);
+  }
+}
+
+template <typename T>
+__global__ void softmax_kernel(const T* __restrict__ x, int64_t cols, T* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  float mx = -INFINITY;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) mx = fmaxf(mx, ld(xr, c));
+  mx = block_max(mx, red);
+  float sum = 0.0f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) sum += expf(ld(xr, c) - mx);
+  sum = block_sum(sum, red);
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    st(y, row * cols + c, expf(ld(xr, c) - mx) / sum);
+}
+
+template <typename T>
+__global__ void layer_norm_kernel(const T* __restrict__ x, const T* __restrict__ gamma,
+                                  const T* __restrict__ beta, int64_t cols, float eps,
+                                  T* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  float s = 0.0f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += ld(xr, c);
+  const float mean = block_sum(s, red) / float(cols);
+  float v = 0.0f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float d = ld(xr, c) - mean;
+    v = fmaf(d, d, v);
+  }
+  const float var = block_sum(v, red) / float(cols);
+  const float den = sqrtf(var + eps);
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    st(y, row * cols + c, ((ld(xr, c) - mean) / den) * ld(gamma, c) + ld(beta, c));
+}
+
+template <typename T>
+__global__ void transpose2_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                  T* __restrict__ y) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * cols;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    y[c * rows + r] = x[i];
+  }
+}
+
+template <typename T>
+__global__ void slice_cols_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                  int64_t start, int64_t stride, int64_t out_cols,
+                                  T* __restrict__ y) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * out_cols;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / out_cols, j = i % out_cols;
+    y[i] = x[r * cols + start + j * stride];
+  }
+}
+
+template <typename T>
+__global__ void broadcast_kernel(const T* __restrict__ a, T* __restrict__ out, BcastShape sh) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < sh.total;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    int64_t rem = i, ia = 0;
+    for (int ax = sh.rank - 1; ax >= 0; --ax) {
+      const int64_t idx = rem % sh.dims[ax];
+      rem /= sh.dims[ax];
+      ia += idx * sh.sa[ax];
+    }
+    out[i] = a[ia];
+  }
+}
+
+template <typename T>
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ table,
+                             int64_t vocab, int64_t dim, T* __restrict__ out, int* err) {
+  const int64_t row = blockIdx.x;
+  const int32_t id = ids[row];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0 && err) atomicExch(err, 3);
+    for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) out[row * dim + c] = T(0);
+    return;
+  }
+  const T* src = table + int64_t(id) * dim;
+  for (int64_t c = threadIdx.x; c < dim; c += blockDim.x) out[row * dim + c] = src[c];
+}
+
+// Lowest index among the maxima; NaN never wins; an all-NaN row gives 0.
+template <typename T>
+__global__ void argmax_kernel(const T* __restrict__ x, int64_t cols, int32_t* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int32_t si[32];
+  const int64_t row = blockIdx.x;
+  float bv = -INFINITY;
+  int32_t bi = INT32_MAX;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float v = ld(x, row * cols + c);
+    if (v != v) continue;
+    if (bi == INT32_MAX || v > bv) bv = v, bi = int32_t(c);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (oi != INT32_MAX && (bi == INT32_MAX || ov > bv || (ov == bv && oi < bi))) bv = ov, bi = oi;
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sv[warp] = bv, si[warp] = bi;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : INT32_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi != INT32_MAX && (bi == INT32_MAX || ov > bv || (ov == bv && oi < bi)))
+        bv = ov, bi = oi;
+    }
+    if (lane == 0) out[row] = bi == INT32_MAX ? 0 : bi;
+  }
+}
+
+// Tiled f32 GEMM for the reference's own Linear/MatMul ops (small shapes):
+// C[m, n] = sum_k A[m, k] * B(k, n), B read through strides so that Linear's
+// [out, in] weight and MatMul's [k, n] operand share one kernel.
+constexpr int kT = 32;
+__global__ void gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                const float* __restrict__ bias, int64_t m, int64_t k, int64_t n,
+                                int64_t b_sk, int64_t b_sn, float* __restrict__ c) {
+  __shared__ float as[kT][kT + 1];
+  __shared__ float bs[kT][kT + 1];
+  const int tx = threadIdx.x % kT, ty = threadIdx.x / kT;  // 32 x 8 threads
+  const int64_t row0 = int64_t(blockIdx.y) * kT, col0 = int64_t(blockIdx.x) * kT;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int64_t k0 = 0; k0 < k; k0 += kT) {
+    for (int r = ty; r < kT; r += 8) {
+      const int64_t ar = row0 + r, ac = k0 + tx;
+      as[r][tx] = (ar < m && ac < k) ? a[ar * k + ac] : 0.0f;
+      const int64_t bk = k0 + r, bn = col0 + tx;
+      bs[r][tx] = (bk < k && bn < n) ? b[bk * b_sk + bn * b_sn] : 0.0f;
+    }
+    __syncthreads();
+    for (int kk = 0; kk < kT; ++kk) {
+      const float bv = bs[kk][tx];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = fmaf(as[ty + 8 * i][kk], bv, acc[i]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t r = row0 + ty + 8 * i, cc = col0 + tx;
+    if (r < m && cc < n) c[r * n + cc] = acc[i] + (bias ? bias[cc] : 0.0f);
+  }
+}
+
+__global__ void convert_kernel(int dir, const void* __restrict__ x, int64_t n, void* __restrict__ y) {
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    if (dir == 0)
+      static_cast<uint16_t*>(y)[i] = f2bf(static_cast<const float*>(x)[i]);
+    else
+      static_cast<float*>(y)[i] = bf2f(static_cast<const uint16_t*>(x)[i]);
+  }
+}
+
+inline unsigned grid_for(int64_t n, int threads = 256) {
+  int64_t b = (n + threads - 1) / threads;
+  const int64_t cap = int64_t(kNumSMs) * 16;
+  if (b > cap) b = cap;
+  return unsigned(b < 1 ? 1 : b);
+}
+
+inline int row_threads(int64_t cols) {
+  if (cols >= 1024) return 512;
+  if (cols >= 256) return 256;
+  return 128;
+}
+
+}  // namespace
+
+template <typename T>
+int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float eps, T* y,
+                    cudaStream_t st) {
+  if (rows == 0 || cols == 0) return SB_OK;
+  rms_norm_kernel<T><<<unsigned(rows), row_threads(cols), 0, st>>>(x, g, cols, eps, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int64_t head_dim,
+                double theta, T* y, cudaStream_t st) {
+  if (head_dim % 2) return SB_INVALID_ARGUMENT;
+  const int64_t n = rows * heads * (head_dim / 2);
+  if (n == 0) return SB_OK;
+  rope_kernel<T><<<grid_for(n), 256, 0, st>>>(x, pos, rows, int(heads), int(head_dim), theta, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_swiglu(const T* gate, const T* up, int64_t n, T* y, cudaStream_t st) {
+  if (n == 0) return SB_OK;
+  swiglu_kernel<T><<<grid_for(n), 256, 0, st>>>(gate, up, n, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_binary(int op, const T* a, const T* b, T* out, const BcastShape& sh, cudaStream_t st) {
+  if (sh.total == 0) return SB_OK;
+  binary_kernel<T><<<grid_for(sh.total), 256, 0, st>>>(op, a, b, out, sh);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_unary(int op, const T* x, int64_t n, T* y, cudaStream_t st) {
+  if (n == 0) return SB_OK;
+  unary_kernel<T><<<grid_for(n), 256, 0, st>>>(op, x, n, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_softmax(const T* x, int64_t rows, int64_t cols, T* y, cudaStream_t st) {
+  if (rows == 0 || cols == 0) return SB_OK;
+  softmax_kernel<T><<<unsigned(rows), row_threads(cols), 0, st>>>(x, cols, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_layer_norm(const T* x, const T* gamma, const T* beta, int64_t rows, int64_t cols,
+                      float eps, T* y, cudaStream_t st) {
+  if (rows == 0 || cols == 0) return SB_OK;
+  layer_norm_kernel<T><<<unsigned(rows), row_threads(cols), 0, st>>>(x, gamma, beta, cols, eps, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_transpose2(const T* x, int64_t rows, int64_t cols, T* y, cudaStream_t st) {
+  if (rows * cols == 0) return SB_OK;
+  transpose2_kernel<T><<<grid_for(rows * cols), 256, 0, st>>>(x, rows, cols, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_slice_cols(const T* x, int64_t rows, int64_t cols, int64_t start, int64_t stride,
+                      int64_t out_cols, T* y, cudaStream_t st) {
+  if (rows * out_cols == 0) return SB_OK;
+  slice_cols_kernel<T><<<grid_for(rows * out_cols), 256, 0, st>>>(x, rows, cols, start, stride,
+                                                                  out_cols, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_broadcast(const T* a, T* out, const BcastShape& sh, cudaStream_t st) {
+  if (sh.total == 0) return SB_OK;
+  broadcast_kernel<T><<<grid_for(sh.total), 256, 0, st>>>(a, out, sh);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_embed(const int32_t* ids, int64_t rows, const T* table, int64_t vocab, int64_t dim,
+                 T* out, int* err, cudaStream_t st) {
+  if (rows == 0 || dim == 0) return SB_OK;
+  embed_kernel<T><<<unsigned(rows), 256, 0, st>>>(ids, table, vocab, dim, out, err);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+template <typename T>
+int launch_argmax(const T* x, int64_t rows, int64_t cols, int32_t* out, cudaStream_t st) {
+  if (rows == 0) return SB_OK;
+  argmax_kernel<T><<<unsigned(rows), 512, 0, st>>>(x, cols, out);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+int launch_gemm_f32(const float* a, const float* b, const float* bias, int64_t m, int64_t k,
+                    int64_t n, bool b_is_nk, float* c, cudaStream_t st) {
+  if (m == 0 || n == 0) return SB_OK;
+  const dim3 grid(unsigned((n + kT - 1) / kT), unsigned((m + kT - 1) / kT));
+  // b_is_nk: B stored [n, k] (Linear weight); else [k, n] (MatMul).
+  const int64_t sk = b_is_nk ? 1 : n, sn = b_is_nk ? k : 1;
+  gemm_f32_kernel<<<grid, 256, 0, st>>>(a, b, bias, m, k, n, sk, sn, c);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+int launch_convert(int dir, const void* x, int64_t n, void* y, cudaStream_t st) {
+  if (n == 0) return SB_OK;
+  convert_kernel<<<grid_for(n), 256, 0, st>>>(dir, x, n, y);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
+#define SB_INST(T)                                                                              \
+  template int launch_rms_norm<T>(const T*, const T*, int64_t, int64_t, float, T*, cudaStream_t); \
+  template int launch_rope<T>(const T*, const int32_t*, int64_t, int64_t, int64_t, double, T*,  \
+                              cudaStream_t);                                                   \
+  template int launch_swiglu<T>(const T*, const T*, int64_t, T*, cudaStream_t);                 \
+  template int launch_binary<T>(int, const T*, const T*, T*, const BcastShape&, cudaStream_t);  \
+  template int launch_unary<T>(int, const T*, int64_t, T*, cudaStream_t);                       \
+  template int launch_softmax<T>(const T*, int64_t, int64_t, T*, cudaStream_t);                 \
+  template int launch_layer_norm<T>(const T*, const T*, const T*, int64_t, int64_t, float, T*,  \
+                                    cudaStream_t);                                             \
+  template int launch_transpose2<T>(const T*, int64_t, int64_t, T*, cudaStream_t);              \
+  template int launch_slice_cols<T>(const T*, int64_t, int64_t, int64_t, int64_t, int64_t, T*,  \
+                                    cudaStream_t);                                             \
+  template int launch_broadcast<T>(const T*, T*, const BcastShape&, cudaStream_t);              \
+  template int launch_embed<T>(const int32_t*, int64_t, const T*, int64_t, int64_t, T*, int*,   \
+                               cudaStream_t);                                                  \
+  template int launch_argmax<T>(const T*, int64_t, int64_t, int32_t*, cudaStream_t);
+
+SB_INST(float)
+SB_INST(uint16_t)
+#undef SB_INST
+
+}  // namespace sb

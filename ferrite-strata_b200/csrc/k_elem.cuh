@@ -1,0 +1,80 @@
+// Launcher declarations for every kernel family, used by the executor and the
+// kernel-level C entry points.
+#pragma once
+
+#include "common.cuh"
+#include "k_linear.cuh"
+
+namespace sb {
+
+// Output shape plus per-axis element strides of the operands (0 where an
+// operand is broadcast along that axis).
+struct BcastShape {
+  int rank;
+  int64_t total;
+  int64_t dims[8];
+  int64_t sa[8];
+  int64_t sb[8];
+};
+
+template <typename T>
+int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float eps, T* y,
+                    cudaStream_t st);
+template <typename T>
+int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int64_t head_dim,
+                double theta, T* y, cudaStream_t st);
+template <typename T>
+int launch_swiglu(const T* gate, const T* up, int64_t n, T* y, cudaStream_t st);
+// op: 0 = add, 1 = mul
+template <typename T>
+int launch_binary(int op, const T* a, const T* b, T* out, const BcastShape& sh, cudaStream_t st);
+// op: 0 = gelu (exact), 1 = exp, 2 = log
+template <typename T>
+int launch_unary(int op, const T* x, int64_t n, T* y, cudaStream_t st);
+template <typename T>
+int launch_softmax(const T* x, int64_t rows, int64_t cols, T* y, cudaStream_t st);
+template <typename T>
+int launch_layer_norm(const T* x, const T* gamma, const T* beta, int64_t rows, int64_t cols,
+                      float eps, T* y, cudaStream_t st);
+template <typename T>
+int launch_transpose2(const T* x, int64_t rows, int64_t cols, T* y, cudaStream_t st);
+template <typename T>
+int launch_slice_cols(const T* x, int64_t rows, int64_t cols, int64_t start, int64_t stride,
+                      int64_t out_cols, T* y, cudaStream_t st);
+template <typename T>
+int launch_broadcast(const T* a, T* out, const BcastShape& sh, cudaStream_t st);
+template <typename T>
+int launch_embed(const int32_t* ids, int64_t rows, const T* table, int64_t vocab, int64_t dim,
+                 T* out, int* err, cudaStream_t st);
+template <typename T>
+int launch_argmax(const T* x, int64_t rows, int64_t cols, int32_t* out, cudaStream_t st);
+int launch_gemm_f32(const float* a, const float* b, const float* bias, int64_t m, int64_t k,
+                    int64_t n, bool b_is_nk, float* c, cudaStream_t st);
+// dir 0: f32 -> bf16, dir 1: bf16 -> f32
+int launch_convert(int dir, const void* x, int64_t n, void* y, cudaStream_t st);
+
+// Attention (k_attention.cu).
+int attention_splits(int64_t rows, int64_t kv_heads, int64_t max_len);
+uint64_t attention_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                 int64_t max_len);
+template <typename T>
+int launch_kv_append(const T* k_new, const T* v_new, T* k_cache, T* v_cache, const int32_t* pos,
+                     int64_t rows, int64_t tokens_per_seq, int64_t kv_heads, int64_t head_dim,
+                     int64_t max_len, int* err, cudaStream_t st);
+template <typename T>
+int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32_t* pos,
+                     int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads,
+                     int64_t head_dim, int64_t max_len, float* scratch, T* out, int* err,
+                     cudaStream_t st);
+
+// Quantisation (k_quant.cu).
+int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, uint16_t* scale,
+                       cudaStream_t st);
+int launch_quant_w8pc(const float* w, int64_t n, int64_t k, int8_t* q, float* scale,
+                      cudaStream_t st);
+int launch_dequant_w4g32(const uint8_t* packed, const uint16_t* scale, int64_t n, int64_t k,
+                         float* w, cudaStream_t st);
+int launch_dequant_w8pc(const int8_t* q, const float* scale, int64_t n, int64_t k, float* w,
+                        cudaStream_t st);
+
+}  // namespace sb

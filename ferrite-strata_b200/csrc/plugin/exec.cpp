@@ -1,0 +1,914 @@
+// Lowering a decoded subgraph to a list of kernel launches, planning the
+// device workspace, and enqueueing the launches (optionally as a CUDA graph).
+//
+// The reference CPU backend compiles one Step per node and runs them in order
+// (crates/ferrite-strata-cpu/src/backend.rs:883-1012, 187-304), publishing
+// only the declared outputs.  This lowering keeps those semantics and adds
+// the fusions a decoder block needs on the GPU:
+//   * linears that share their input x run as one launch (q/k/v);
+//   * gate and up linears feeding fused::swiglu become one launch whose
+//     epilogue applies SwiGLU (the gate/up activations never reach HBM);
+//   * a linear whose only consumer is a residual add writes x + W.x directly.
+#include <algorithm>
+#include <cstring>
+#include <map>
+
+#include "plugin.hpp"
+
+namespace sbp {
+
+namespace {
+
+bool is_f32(const DType& d) { return d.elem == STRATA_ELEM_F32 && d.qkind == 0; }
+bool is_bf16(const DType& d) { return d.elem == STRATA_ELEM_BF16 && d.qkind == 0; }
+bool is_float(const DType& d) { return is_f32(d) || is_bf16(d); }
+// Integers travel as I32 tagged with a block spec (bare integers are illegal
+// on the wire, wire/graph.rs:466-475).
+bool is_i32(const DType& d) { return d.elem == STRATA_ELEM_I32 && d.qkind == STRATA_QUANT_BLOCK; }
+bool is_w4(const DType& d) {
+  return d.elem == STRATA_ELEM_U8 && d.qkind == STRATA_QUANT_BLOCK && d.block == 32 && d.sym;
+}
+bool is_w8(const DType& d) { return d.elem == STRATA_ELEM_I8 && d.qkind == STRATA_QUANT_BLOCK && d.sym; }
+
+int64_t last_dim(const Value& v) { return v.dims.empty() ? 1 : v.dims.back(); }
+int64_t rows_of(const Value& v) {
+  const int64_t l = last_dim(v);
+  return l == 0 ? 0 : v.elements() / l;
+}
+
+struct Lowerer {
+  const Graph& g;
+  Exe& exe;
+  std::string* reason;
+  std::vector<std::vector<int>> cons;
+  std::vector<bool> absorbed;
+  std::vector<bool> is_output;
+
+  Lowerer(const Graph& gr, Exe& e, std::string* r) : g(gr), exe(e), reason(r) {}
+
+  bool decline(const std::string& why) {
+    *reason = why;
+    return false;
+  }
+
+  uint32_t in(const Node& n, size_t i) const {
+    if (i >= n.inputs.size())
+      fail(STRATA_INVALID_ARGUMENT, "node `" + n.name + "` wants operand " + std::to_string(i) +
+                                        " but declares " + std::to_string(n.inputs.size()));
+    return n.inputs[i];
+  }
+  const Value& V(uint32_t id) const { return g.values[id]; }
+
+  void push(Step s) { exe.steps.push_back(std::move(s)); }
+
+  bool same_dims(uint32_t a, uint32_t b) const { return V(a).dims == V(b).dims; }
+
+  // NumPy broadcast of `a` (and optionally `b`) to the output dims.
+  bool bcast(const std::vector<int64_t>& out, uint32_t a, uint32_t b, sb::BcastShape& bs) const {
+    const int r = int(out.size());
+    if (r > 8) return false;
+    bs.rank = r;
+    bs.total = 1;
+    for (int ax = 0; ax < r; ++ax) {
+      bs.dims[ax] = out[ax];
+      bs.total *= out[ax];
+    }
+    auto fill = [&](uint32_t id, int64_t* st) {
+      const auto& d = V(id).dims;
+      const int off = r - int(d.size());
+      if (off < 0) return false;
+      int64_t stride = 1;
+      for (int ax = r - 1; ax >= 0; --ax) {
+        const int sa = ax - off;
+        if (sa < 0) {
+          st[ax] = 0;
+          continue;
+        }
+        if (d[sa] != 1 && d[sa] != out[ax]) return false;
+        st[ax] = d[sa] == 1 ? 0 : stride;
+        stride *= d[sa];
+      }
+      return true;
+    };
+    if (!fill(a, bs.sa)) return false;
+    if (b != kNone && !fill(b, bs.sb)) return false;
+    return true;
+  }
+
+  bool is_linear(const Node& n) const {
+    return n.op == STRATA_OP_CUSTOM &&
+           (n.pattern == "fused::linear_w4g32" || n.pattern == "fused::linear_w8pc");
+  }
+
+  bool linear_shapes(const Node& n, int64_t& M, int64_t& K, int64_t& N, std::string* why) const {
+    const uint32_t x = n.inputs[0], w = n.inputs[1], s = n.inputs[2], y = n.outputs[0];
+    const bool w4 = n.pattern == "fused::linear_w4g32";
+    if (!is_bf16(V(x).dt) || !is_bf16(V(y).dt)) {
+      *why = "quantised linears take and return bf16";
+      return false;
+    }
+    K = last_dim(V(x));
+    M = rows_of(V(x));
+    N = last_dim(V(y));
+    if (rows_of(V(y)) != M) {
+      *why = "linear output rows do not match input rows";
+      return false;
+    }
+    if (w4) {
+      if (!is_w4(V(w).dt) || V(w).dims != std::vector<int64_t>{N, K / 2} || K % 32) {
+        *why = "int4 weights must be U8 Block{32, symmetric} of shape [N, K/2] with K % 32 == 0";
+        return false;
+      }
+      if (!is_bf16(V(s).dt) || V(s).dims != std::vector<int64_t>{N, K / 32}) {
+        *why = "int4 scales must be bf16 [N, K/32]";
+        return false;
+      }
+    } else {
+      if (!is_w8(V(w).dt) || V(w).dims != std::vector<int64_t>{N, K} || K % 16) {
+        *why = "int8 weights must be I8 Block{K, symmetric} of shape [N, K] with K % 16 == 0";
+        return false;
+      }
+      if (!is_f32(V(s).dt) || V(s).dims != std::vector<int64_t>{N}) {
+        *why = "int8 scales must be f32 [N]";
+        return false;
+      }
+    }
+    if (N % 2) {
+      *why = "output features must be even";
+      return false;
+    }
+    return true;
+  }
+
+  void add_linear_job(Step& st, const Node& n, uint32_t y, uint32_t r) {
+    st.v.push_back(n.inputs[1]);
+    st.v.push_back(n.inputs[2]);
+    st.v.push_back(y);
+    st.v.push_back(r);
+    st.reads.push_back(n.inputs[1]);
+    st.reads.push_back(n.inputs[2]);
+    if (r != kNone) st.reads.push_back(r);
+    st.writes.push_back(y);
+    st.njobs++;
+  }
+
+  Step linear_step(const Node& n, int64_t M, int64_t K) {
+    Step st;
+    st.kind = SK::Linear;
+    st.bf16 = true;
+    st.fmt = n.pattern == "fused::linear_w4g32" ? sb::WFormat::W4G32 : sb::WFormat::W8PC;
+    st.i[0] = M;
+    st.i[1] = K;
+    st.v.push_back(n.inputs[0]);
+    st.reads.push_back(n.inputs[0]);
+    st.label = n.name;
+    return st;
+  }
+
+  int producer(uint32_t v) const { return int(V(v).producer); }
+
+  bool lower_all() {
+    const size_t nv = g.values.size(), nn = g.nodes.size();
+    cons.assign(nv, {});
+    is_output.assign(nv, false);
+    absorbed.assign(nn, false);
+    for (auto o : g.outputs) is_output[o] = true;
+    for (size_t i = 0; i < nn; ++i) {
+      const Node& n = g.nodes[i];
+      const bool bad_field =
+          (n.op == STRATA_OP_LINEAR && (n.weight >= nv || (n.has_bias && n.bias >= nv))) ||
+          (n.op == STRATA_OP_LAYER_NORM && (n.gamma >= nv || n.beta >= nv));
+      if (bad_field)
+        fail(STRATA_INVALID_ARGUMENT, "node `" + n.name + "` names a weight value that does not exist");
+      for (auto v : n.inputs) cons[v].push_back(int(i));
+      if (n.op == STRATA_OP_LINEAR) {
+        cons[n.weight].push_back(int(i));
+        if (n.has_bias) cons[n.bias].push_back(int(i));
+      }
+      if (n.op == STRATA_OP_LAYER_NORM) {
+        cons[n.gamma].push_back(int(i));
+        cons[n.beta].push_back(int(i));
+      }
+      for (auto v : n.outputs)
+        if (g.values[v].producer != int64_t(i))
+          fail(STRATA_INVALID_ARGUMENT, "value `" + g.values[v].name + "` is written by node `" +
+                                            n.name + "` but names another producer");
+    }
+    if (g.outputs.empty()) return decline("a subgraph with no outputs has nothing to run");
+
+    exe.alias.resize(nv);
+    for (size_t v = 0; v < nv; ++v) exe.alias[v] = uint32_t(v);
+
+    for (size_t i = 0; i < nn; ++i) {
+      if (absorbed[i]) continue;
+      if (!lower_node(int(i))) return false;
+    }
+    return true;
+  }
+
+  bool lower_linear(int ni) {
+    const Node& n = g.nodes[ni];
+    in(n, 2);
+    if (n.outputs.size() != 1) return decline("a quantised linear has exactly one output");
+    int64_t M, K, N;
+    std::string why;
+    if (!linear_shapes(n, M, K, N, &why)) return decline(why);
+    const uint32_t x = n.inputs[0], y = n.outputs[0];
+
+    // SwiGLU: silu(gate) * up where gate and up are linears of the same x.
+    if (cons[y].size() == 1 && !is_output[y]) {
+      const int si = cons[y][0];
+      const Node& S = g.nodes[si];
+      if (!absorbed[si] && S.op == STRATA_OP_CUSTOM && S.pattern == "fused::swiglu" &&
+          S.inputs.size() == 2 && S.outputs.size() == 1 && S.inputs[0] != S.inputs[1] &&
+          is_bf16(V(S.outputs[0]).dt)) {
+        const uint32_t other = S.inputs[0] == y ? S.inputs[1] : S.inputs[0];
+        const int pj = producer(other);
+        if (pj >= 0 && pj != ni && !absorbed[pj] && is_linear(g.nodes[pj]) &&
+            g.nodes[pj].pattern == n.pattern && g.nodes[pj].inputs.size() >= 3 &&
+            g.nodes[pj].inputs[0] == x && cons[other].size() == 1 && !is_output[other]) {
+          int64_t M2, K2, N2;
+          if (linear_shapes(g.nodes[pj], M2, K2, N2, &why) && N2 == N && K2 == K &&
+              V(S.outputs[0]).dims == V(y).dims) {
+            const Node& gate = S.inputs[0] == y ? n : g.nodes[pj];
+            const Node& up = S.inputs[0] == y ? g.nodes[pj] : n;
+            Step st = linear_step(n, M, K);
+            st.epi = sb::Epilogue::SwiGLU;
+            add_linear_job(st, gate, S.outputs[0], kNone);
+            add_linear_job(st, up, kNone, kNone);
+            st.writes.pop_back();  // the up job writes nothing
+            st.label = S.name;
+            push(std::move(st));
+            absorbed[ni] = absorbed[pj] = absorbed[si] = true;
+            return true;
+          }
+        }
+      }
+      // Residual: y + r with r already computed.
+      if (!absorbed[si] && S.op == STRATA_OP_ADD && S.inputs.size() == 2 && S.outputs.size() == 1 &&
+          S.inputs[0] != S.inputs[1]) {
+        const uint32_t r = S.inputs[0] == y ? S.inputs[1] : S.inputs[0];
+        const int pr = producer(r);
+        if (is_bf16(V(r).dt) && same_dims(r, y) && V(S.outputs[0]).dims == V(y).dims &&
+            is_bf16(V(S.outputs[0]).dt) && (pr < 0 || pr < ni)) {
+          Step st = linear_step(n, M, K);
+          st.epi = sb::Epilogue::Residual;
+          add_linear_job(st, n, S.outputs[0], r);
+          st.label = n.name + "+" + S.name;
+          push(std::move(st));
+          absorbed[ni] = absorbed[si] = true;
+          return true;
+        }
+      }
+    }
+
+    // Group with later linears of the same x that are not fused otherwise.
+    Step st = linear_step(n, M, K);
+    add_linear_job(st, n, y, kNone);
+    absorbed[ni] = true;
+    for (size_t j = ni + 1; j < g.nodes.size() && st.njobs < sb::kMaxJobs; ++j) {
+      const Node& o = g.nodes[j];
+      if (absorbed[j] || !is_linear(o) || o.pattern != n.pattern || o.inputs.size() < 3 ||
+          o.inputs[0] != x || o.outputs.size() != 1)
+        continue;
+      int64_t M2, K2, N2;
+      if (!linear_shapes(o, M2, K2, N2, &why)) continue;
+      if (would_fuse(int(j))) continue;
+      add_linear_job(st, o, o.outputs[0], kNone);
+      absorbed[j] = true;
+    }
+    push(std::move(st));
+    return true;
+  }
+
+  // Whether linear node j will take the SwiGLU or residual path itself.
+  bool would_fuse(int j) const {
+    const Node& n = g.nodes[j];
+    const uint32_t y = n.outputs[0];
+    if (cons[y].size() != 1 || is_output[y]) return false;
+    const Node& S = g.nodes[cons[y][0]];
+    if (S.op == STRATA_OP_CUSTOM && S.pattern == "fused::swiglu") return true;
+    if (S.op == STRATA_OP_ADD) return true;
+    return false;
+  }
+
+  bool float_unary_ok(uint32_t a, uint32_t b) const {
+    return is_float(V(a).dt) && V(a).dt == V(b).dt;
+  }
+
+  bool lower_node(int ni) {
+    const Node& n = g.nodes[ni];
+    if (n.op == STRATA_OP_INPUT) return true;
+    if (n.outputs.size() != 1 && !(n.op == STRATA_OP_CUSTOM && n.pattern.rfind("fused::quantize_", 0) == 0))
+      return decline("every kernel here is single-output; node `" + n.name + "` has " +
+                     std::to_string(n.outputs.size()));
+    const uint32_t out = n.outputs.empty() ? kNone : n.outputs[0];
+    Step st;
+    st.label = n.name;
+    switch (n.op) {
+      case STRATA_OP_ADD:
+      case STRATA_OP_MUL: {
+        const uint32_t a = in(n, 0), b = in(n, 1);
+        if (!is_float(V(out).dt) || !(V(a).dt == V(out).dt) || !(V(b).dt == V(out).dt))
+          return decline("add/mul needs matching f32 or bf16 operands");
+        st.kind = SK::Binary;
+        st.bf16 = is_bf16(V(out).dt);
+        st.i[0] = n.op == STRATA_OP_ADD ? 0 : 1;
+        if (!bcast(V(out).dims, a, b, st.bs)) return decline("operands do not broadcast to the output");
+        st.v = {a, b, out};
+        st.reads = {a, b};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_MATMUL: {
+        const uint32_t a = in(n, 0), b = in(n, 1);
+        if (!is_f32(V(a).dt) || !is_f32(V(b).dt) || !is_f32(V(out).dt))
+          return decline("matmul runs in f32 only");
+        if (V(a).dims.size() != 2 || V(b).dims.size() != 2)
+          return decline("matmul is rank-2 only");
+        if (V(a).dims[1] != V(b).dims[0])
+          fail(STRATA_INVALID_ARGUMENT, "matmul inner dimensions differ: " +
+                                            std::to_string(V(a).dims[1]) + " vs " +
+                                            std::to_string(V(b).dims[0]));
+        st.kind = SK::GemmF32;
+        st.i[0] = V(a).dims[0];
+        st.i[1] = V(a).dims[1];
+        st.i[2] = V(b).dims[1];
+        st.i[3] = 0;  // b stored [k, n]
+        st.v = {a, b, kNone, out};
+        st.reads = {a, b};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_LOG:
+      case STRATA_OP_EXP:
+      case STRATA_OP_GELU: {
+        const uint32_t a = in(n, 0);
+        if (!float_unary_ok(a, out)) return decline("unary ops need f32 or bf16");
+        st.kind = SK::Unary;
+        st.bf16 = is_bf16(V(out).dt);
+        st.i[0] = n.op == STRATA_OP_GELU ? 0 : (n.op == STRATA_OP_EXP ? 1 : 2);
+        st.i[1] = V(out).elements();
+        st.v = {a, out};
+        st.reads = {a};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_SOFTMAX: {
+        const uint32_t a = in(n, 0);
+        if (!float_unary_ok(a, out)) return decline("softmax needs f32 or bf16");
+        const int64_t r = int64_t(V(a).dims.size());
+        if (!(n.axis == -1 || n.axis == r - 1)) return decline("softmax over a non-trailing axis");
+        st.kind = SK::Softmax;
+        st.bf16 = is_bf16(V(out).dt);
+        st.i[0] = rows_of(V(a));
+        st.i[1] = last_dim(V(a));
+        st.v = {a, out};
+        st.reads = {a};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_LAYER_NORM: {
+        const uint32_t a = in(n, 0);
+        if (!float_unary_ok(a, out) || !(V(n.gamma).dt == V(a).dt) || !(V(n.beta).dt == V(a).dt))
+          return decline("layer norm needs matching f32 or bf16 operands");
+        if (V(n.gamma).elements() != last_dim(V(a)) || V(n.beta).elements() != last_dim(V(a)))
+          fail(STRATA_INVALID_ARGUMENT, "layer norm gamma/beta do not match the trailing axis");
+        st.kind = SK::LayerNorm;
+        st.bf16 = is_bf16(V(out).dt);
+        st.i[0] = rows_of(V(a));
+        st.i[1] = last_dim(V(a));
+        st.d = n.eps;
+        st.v = {a, n.gamma, n.beta, out};
+        st.reads = {a, n.gamma, n.beta};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_LINEAR: {
+        const uint32_t a = in(n, 0);
+        const uint32_t w = n.weight;
+        if (w >= g.values.size() || (n.has_bias && n.bias >= g.values.size()))
+          fail(STRATA_INVALID_ARGUMENT, "linear names a weight or bias that does not exist");
+        const int64_t K = last_dim(V(a)), M = rows_of(V(a));
+        if (V(w).dims.size() != 2) return decline("linear weight must be rank 2");
+        const int64_t N = V(w).dims[0];
+        if (V(w).dims[1] != K)
+          fail(STRATA_INVALID_ARGUMENT, "linear inner dimensions differ: " + std::to_string(K) +
+                                            " vs " + std::to_string(V(w).dims[1]));
+        if (is_f32(V(a).dt) && is_f32(V(w).dt) && is_f32(V(out).dt) &&
+            (!n.has_bias || is_f32(V(n.bias).dt))) {
+          st.kind = SK::GemmF32;
+          st.i[0] = M;
+          st.i[1] = K;
+          st.i[2] = N;
+          st.i[3] = 1;  // b stored [n, k]
+          st.v = {a, w, n.has_bias ? n.bias : kNone, out};
+          st.reads = {a, w};
+          if (n.has_bias) st.reads.push_back(n.bias);
+          st.writes = {out};
+          break;
+        }
+        if (is_bf16(V(a).dt) && is_bf16(V(w).dt) && is_bf16(V(out).dt) && !n.has_bias &&
+            K % 8 == 0 && N % 2 == 0) {
+          st.kind = SK::Linear;
+          st.bf16 = true;
+          st.fmt = sb::WFormat::BF16;
+          st.i[0] = M;
+          st.i[1] = K;
+          st.v = {a, w, kNone, out, kNone};
+          st.njobs = 1;
+          st.reads = {a, w};
+          st.writes = {out};
+          break;
+        }
+        return decline("linear runs as f32, or bf16 without bias");
+      }
+      case STRATA_OP_RESHAPE: {
+        const uint32_t a = in(n, 0);
+        if (V(a).bytes() != V(out).bytes())
+          fail(STRATA_INVALID_ARGUMENT, "reshape changes the byte size");
+        if (is_output[out]) {
+          st.kind = SK::Copy;
+          st.i[0] = int64_t(V(out).bytes());
+          st.v = {a, out};
+          st.reads = {a};
+          st.writes = {out};
+          break;
+        }
+        exe.alias[out] = exe.alias[a];
+        return true;
+      }
+      case STRATA_OP_TRANSPOSE: {
+        const uint32_t a = in(n, 0);
+        if (!float_unary_ok(a, out)) return decline("transpose needs f32 or bf16");
+        if (V(a).dims.size() != 2 || n.perm != std::vector<int64_t>{1, 0})
+          return decline("only the rank-2 [1, 0] transpose is implemented");
+        st.kind = SK::Transpose;
+        st.bf16 = is_bf16(V(out).dt);
+        st.i[0] = V(a).dims[0];
+        st.i[1] = V(a).dims[1];
+        st.v = {a, out};
+        st.reads = {a};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_EXPAND: {
+        const uint32_t a = in(n, 0);
+        if (!float_unary_ok(a, out)) return decline("expand needs f32 or bf16");
+        st.kind = SK::Broadcast;
+        st.bf16 = is_bf16(V(out).dt);
+        if (!bcast(V(out).dims, a, kNone, st.bs)) return decline("operand does not broadcast");
+        st.v = {a, out};
+        st.reads = {a};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_SLICE: {
+        const uint32_t a = in(n, 0);
+        if (!float_unary_ok(a, out)) return decline("slice needs f32 or bf16");
+        if (V(a).dims.size() != 2 || !(n.axis == 1 || n.axis == -1))
+          return decline("slice is implemented along axis 1 of a rank-2 tensor");
+        if (n.s_stride <= 0) fail(STRATA_INVALID_ARGUMENT, "slice stride must be positive");
+        const int64_t cols = V(a).dims[1];
+        int64_t cnt = 0, first = -1;
+        for (int64_t c = n.s_start; c < n.s_end; c += n.s_stride)
+          if (c >= 0 && c < cols) {
+            if (first < 0) first = c;
+            ++cnt;
+          }
+        if (V(out).dims != std::vector<int64_t>{V(a).dims[0], cnt})
+          fail(STRATA_INVALID_ARGUMENT, "slice output shape does not match its bounds");
+        st.kind = SK::Slice;
+        st.bf16 = is_bf16(V(out).dt);
+        st.i[0] = V(a).dims[0];
+        st.i[1] = cols;
+        st.i[2] = first < 0 ? 0 : first;
+        st.i[3] = n.s_stride;
+        st.i[4] = cnt;
+        st.v = {a, out};
+        st.reads = {a};
+        st.writes = {out};
+        break;
+      }
+      case STRATA_OP_CUSTOM:
+        return lower_custom(ni);
+      default:
+        return decline("op tag " + std::to_string(n.op) + " has no kernel");
+    }
+    push(std::move(st));
+    return true;
+  }
+
+  bool lower_custom(int ni) {
+    const Node& n = g.nodes[ni];
+    const std::string& p = n.pattern;
+    if (p == "fused::linear_w4g32" || p == "fused::linear_w8pc") return lower_linear(ni);
+    const uint32_t out = n.outputs.empty() ? kNone : n.outputs[0];
+    Step st;
+    st.label = n.name;
+    if (p == "fused::rms_norm") {
+      const uint32_t x = in(n, 0), gm = in(n, 1);
+      if (!float_unary_ok(x, out) || !(V(gm).dt == V(x).dt)) return decline("rms_norm needs matching f32 or bf16");
+      if (V(gm).elements() != last_dim(V(x)))
+        fail(STRATA_INVALID_ARGUMENT, "rms_norm gamma does not match the trailing axis");
+      st.kind = SK::RmsNorm;
+      st.bf16 = is_bf16(V(x).dt);
+      st.i[0] = rows_of(V(x));
+      st.i[1] = last_dim(V(x));
+      st.d = n.attr_float("eps", 1e-5);
+      st.v = {x, gm, out};
+      st.reads = {x, gm};
+      st.writes = {out};
+    } else if (p == "fused::rope") {
+      const uint32_t x = in(n, 0), pos = in(n, 1);
+      if (!float_unary_ok(x, out) || !is_i32(V(pos).dt)) return decline("rope needs f32/bf16 x and I32 positions");
+      const int64_t hd = n.attr_int("head_dim", 0);
+      if (hd <= 0 || hd % 2 || last_dim(V(x)) % hd)
+        fail(STRATA_INVALID_ARGUMENT, "rope head_dim must be even and divide the row width");
+      if (V(pos).elements() != rows_of(V(x)))
+        fail(STRATA_INVALID_ARGUMENT, "rope needs one position per row");
+      st.kind = SK::Rope;
+      st.bf16 = is_bf16(V(x).dt);
+      st.i[0] = rows_of(V(x));
+      st.i[1] = last_dim(V(x)) / hd;
+      st.i[2] = hd;
+      st.d = n.attr_float("theta", 10000.0);
+      st.v = {x, pos, out};
+      st.reads = {x, pos};
+      st.writes = {out};
+    } else if (p == "fused::swiglu") {
+      const uint32_t a = in(n, 0), b = in(n, 1);
+      if (!float_unary_ok(a, out) || !(V(b).dt == V(a).dt) || !same_dims(a, b) || !same_dims(a, out))
+        return decline("swiglu needs two same-shaped f32 or bf16 operands");
+      st.kind = SK::SwiGLU;
+      st.bf16 = is_bf16(V(a).dt);
+      st.i[0] = V(a).elements();
+      st.v = {a, b, out};
+      st.reads = {a, b};
+      st.writes = {out};
+    } else if (p == "fused::attention") {
+      const uint32_t q = in(n, 0), k = in(n, 1), v = in(n, 2), kc = in(n, 3), vc = in(n, 4),
+                     pos = in(n, 5);
+      const DType& dt = V(q).dt;
+      if (!is_float(dt) || !(V(k).dt == dt) || !(V(v).dt == dt) || !(V(kc).dt == dt) ||
+          !(V(vc).dt == dt) || !(V(out).dt == dt) || !is_i32(V(pos).dt))
+        return decline("attention needs one float dtype throughout and I32 positions");
+      if (V(kc).dims.size() != 4 || V(kc).dims != V(vc).dims)
+        fail(STRATA_INVALID_ARGUMENT, "kv caches must be [batch, kv_heads, max_len, head_dim]");
+      const int64_t B = V(kc).dims[0], KVH = V(kc).dims[1], L = V(kc).dims[2], D = V(kc).dims[3];
+      const int64_t H = n.attr_int("num_heads", 0);
+      if (n.attr_int("num_kv_heads", KVH) != KVH || n.attr_int("head_dim", D) != D)
+        fail(STRATA_INVALID_ARGUMENT, "attention attributes disagree with the cache shape");
+      const int64_t rows = rows_of(V(q));
+      if (H <= 0 || last_dim(V(q)) != H * D || last_dim(V(k)) != KVH * D || rows_of(V(k)) != rows ||
+          !same_dims(k, v) || !same_dims(q, out) || V(pos).elements() != rows || B <= 0 ||
+          rows % B || H % KVH)
+        fail(STRATA_INVALID_ARGUMENT, "attention operand shapes are inconsistent");
+      if (D != 64 && D != 128) return decline("attention head_dim must be 64 or 128");
+      if (H / KVH > 8) return decline("at most 8 query heads per kv head");
+      Step ap;
+      ap.kind = SK::KvAppend;
+      ap.bf16 = is_bf16(dt);
+      ap.label = n.name + ".append";
+      ap.i[0] = rows;
+      ap.i[1] = rows / B;
+      ap.i[2] = KVH;
+      ap.i[3] = D;
+      ap.i[4] = L;
+      ap.v = {k, v, kc, vc, pos};
+      ap.reads = {k, v, kc, vc, pos};
+      ap.writes = {kc, vc};
+      push(std::move(ap));
+      st.kind = SK::Attention;
+      st.bf16 = is_bf16(dt);
+      st.i[0] = rows;
+      st.i[1] = rows / B;
+      st.i[2] = H;
+      st.i[3] = KVH;
+      st.i[4] = D;
+      st.i[5] = L;
+      st.scratch_bytes = sb::attention_scratch_bytes(rows, H, KVH, D, L);
+      st.v = {q, kc, vc, pos, out};
+      st.reads = {q, kc, vc, pos};
+      st.writes = {out};
+    } else if (p == "fused::embed") {
+      const uint32_t ids = in(n, 0), tab = in(n, 1);
+      if (!is_i32(V(ids).dt) || !is_float(V(tab).dt) || !(V(out).dt == V(tab).dt) ||
+          V(tab).dims.size() != 2)
+        return decline("embed needs I32 ids and a rank-2 float table");
+      if (last_dim(V(out)) != V(tab).dims[1] || rows_of(V(out)) != V(ids).elements())
+        fail(STRATA_INVALID_ARGUMENT, "embed output shape does not match ids x table width");
+      st.kind = SK::Embed;
+      st.bf16 = is_bf16(V(tab).dt);
+      st.i[0] = V(ids).elements();
+      st.i[1] = V(tab).dims[0];
+      st.i[2] = V(tab).dims[1];
+      st.v = {ids, tab, out};
+      st.reads = {ids, tab};
+      st.writes = {out};
+    } else if (p == "fused::argmax") {
+      const uint32_t x = in(n, 0);
+      if (!is_float(V(x).dt) || !is_i32(V(out).dt)) return decline("argmax maps f32/bf16 rows to I32");
+      if (V(out).elements() != rows_of(V(x)))
+        fail(STRATA_INVALID_ARGUMENT, "argmax output must have one id per row");
+      st.kind = SK::Argmax;
+      st.bf16 = is_bf16(V(x).dt);
+      st.i[0] = rows_of(V(x));
+      st.i[1] = last_dim(V(x));
+      st.v = {x, out};
+      st.reads = {x};
+      st.writes = {out};
+    } else if (p == "fused::all_reduce") {
+      const uint32_t x = in(n, 0);
+      if (!float_unary_ok(x, out) || !same_dims(x, out)) return decline("all_reduce needs f32 or bf16");
+      st.kind = SK::AllReduce;
+      st.bf16 = is_bf16(V(x).dt);
+      st.i[0] = V(x).elements();
+      st.v = {x, out};
+      st.reads = {x};
+      st.writes = {out};
+    } else if (p == "fused::quantize_w4g32" || p == "fused::quantize_w8pc") {
+      const uint32_t w = in(n, 0);
+      const bool w4 = p == "fused::quantize_w4g32";
+      if (n.outputs.size() != 2 || !is_f32(V(w).dt) || V(w).dims.size() != 2)
+        return decline("quantize takes an f32 [N, K] weight and returns (codes, scales)");
+      const int64_t N = V(w).dims[0], K = V(w).dims[1];
+      const uint32_t c = n.outputs[0], s = n.outputs[1];
+      if (w4 ? (!is_w4(V(c).dt) || V(c).dims != std::vector<int64_t>{N, K / 2} || K % 32 ||
+                !is_bf16(V(s).dt) || V(s).dims != std::vector<int64_t>{N, K / 32})
+             : (!is_w8(V(c).dt) || V(c).dims != std::vector<int64_t>{N, K} || !is_f32(V(s).dt) ||
+                V(s).dims != std::vector<int64_t>{N}))
+        fail(STRATA_INVALID_ARGUMENT, "quantize output dtypes or shapes are wrong");
+      st.kind = w4 ? SK::Quant4 : SK::Quant8;
+      st.i[0] = N;
+      st.i[1] = K;
+      st.v = {w, c, s};
+      st.reads = {w};
+      st.writes = {c, s};
+    } else if (p == "fused::dequantize_w4g32" || p == "fused::dequantize_w8pc") {
+      const uint32_t c = in(n, 0), s = in(n, 1);
+      const bool w4 = p == "fused::dequantize_w4g32";
+      if (!is_f32(V(out).dt) || V(out).dims.size() != 2) return decline("dequantize returns f32 [N, K]");
+      const int64_t N = V(out).dims[0], K = V(out).dims[1];
+      if (w4 ? (!is_w4(V(c).dt) || V(c).dims != std::vector<int64_t>{N, K / 2} || K % 32 ||
+                !is_bf16(V(s).dt) || V(s).dims != std::vector<int64_t>{N, K / 32})
+             : (!is_w8(V(c).dt) || V(c).dims != std::vector<int64_t>{N, K} || !is_f32(V(s).dt) ||
+                V(s).dims != std::vector<int64_t>{N}))
+        fail(STRATA_INVALID_ARGUMENT, "dequantize operand dtypes or shapes are wrong");
+      st.kind = w4 ? SK::Dequant4 : SK::Dequant8;
+      st.i[0] = N;
+      st.i[1] = K;
+      st.v = {c, s, out};
+      st.reads = {c, s};
+      st.writes = {out};
+    } else {
+      return decline("no kernel for pattern `" + p + "`");
+    }
+    push(std::move(st));
+    return true;
+  }
+};
+
+// First-fit workspace planner over step-indexed lifetimes.
+void plan_workspace(Exe& exe) {
+  const Graph& g = exe.g;
+  const size_t nv = g.values.size();
+  std::vector<int> def(nv, -1), last(nv, -1);
+  exe.is_output.assign(nv, false);
+  for (auto o : g.outputs) exe.is_output[o] = true;
+  exe.needed_input.assign(nv, false);
+  for (size_t s = 0; s < exe.steps.size(); ++s) {
+    for (auto v : exe.steps[s].reads) {
+      const uint32_t b = exe.alias[v];
+      last[b] = std::max(last[b], int(s));
+      if (g.values[b].producer < 0) exe.needed_input[b] = true;
+    }
+    for (auto v : exe.steps[s].writes) {
+      const uint32_t b = exe.alias[v];
+      if (g.values[b].producer >= 0 && def[b] < 0) def[b] = int(s);
+      last[b] = std::max(last[b], int(s));
+    }
+  }
+  // Inputs produced by Input nodes are external too.
+  for (size_t v = 0; v < nv; ++v) {
+    const int64_t p = g.values[v].producer;
+    if (p >= 0 && g.nodes[size_t(p)].op == STRATA_OP_INPUT && last[v] >= 0) exe.needed_input[v] = true;
+  }
+  const int end = int(exe.steps.size());
+  for (auto o : g.outputs) {
+    const uint32_t b = exe.alias[o];
+    if (def[b] >= 0) last[b] = end;
+  }
+  exe.ws_off.assign(nv, -1);
+  struct Block {
+    uint64_t off, size;
+  };
+  std::vector<Block> free_list;
+  uint64_t top = 0;
+  auto align = [](uint64_t x) { return (x + 255) & ~uint64_t(255); };
+  auto alloc = [&](uint64_t size) {
+    size = align(std::max<uint64_t>(size, 1));
+    for (size_t i = 0; i < free_list.size(); ++i) {
+      if (free_list[i].size >= size) {
+        const uint64_t off = free_list[i].off;
+        free_list[i].off += size;
+        free_list[i].size -= size;
+        if (free_list[i].size == 0) free_list.erase(free_list.begin() + long(i));
+        return off;
+      }
+    }
+    const uint64_t off = top;
+    top += size;
+    return off;
+  };
+  auto release = [&](uint64_t off, uint64_t size) {
+    size = align(std::max<uint64_t>(size, 1));
+    free_list.push_back({off, size});
+    std::sort(free_list.begin(), free_list.end(), [](const Block& a, const Block& b) { return a.off < b.off; });
+    std::vector<Block> merged;
+    for (auto& b : free_list) {
+      if (!merged.empty() && merged.back().off + merged.back().size == b.off) merged.back().size += b.size;
+      else merged.push_back(b);
+    }
+    free_list.swap(merged);
+  };
+  std::vector<std::vector<uint32_t>> dying(exe.steps.size() + 1);
+  for (size_t v = 0; v < nv; ++v)
+    if (def[v] >= 0) dying[size_t(last[v])].push_back(uint32_t(v));
+  for (size_t s = 0; s < exe.steps.size(); ++s) {
+    for (auto v : exe.steps[s].writes) {
+      const uint32_t b = exe.alias[v];
+      if (def[b] == int(s) && exe.ws_off[b] < 0) exe.ws_off[b] = int64_t(alloc(g.values[b].bytes()));
+    }
+    if (exe.steps[s].scratch_bytes) exe.steps[s].scratch_off = alloc(exe.steps[s].scratch_bytes);
+    if (exe.steps[s].scratch_bytes) release(exe.steps[s].scratch_off, exe.steps[s].scratch_bytes);
+    for (auto v : dying[s]) release(uint64_t(exe.ws_off[v]), g.values[v].bytes());
+  }
+  exe.ws_bytes = top;
+}
+
+}  // namespace
+
+bool lower(const Graph& g, Exe& exe, std::string* reason) {
+  Lowerer L(g, exe, reason);
+  if (!L.lower_all()) return false;
+  plan_workspace(exe);
+  return true;
+}
+
+Exe::~Exe() {
+  for (auto& c : graphs)
+    if (c.exec) cudaGraphExecDestroy(c.exec);
+  if (ws) cudaFree(ws);
+}
+
+namespace {
+
+struct Ptrs {
+  const Exe& exe;
+  const std::vector<void*>& ext;
+  void* at(uint32_t v) const {
+    if (v == kNone) return nullptr;
+    const uint32_t b = exe.alias[v];
+    if (ext[b]) return ext[b];
+    if (exe.ws_off[b] >= 0) return static_cast<char*>(exe.ws) + exe.ws_off[b];
+    return nullptr;
+  }
+};
+
+template <typename T>
+T* P(const Ptrs& p, uint32_t v) {
+  return static_cast<T*>(p.at(v));
+}
+
+void check_rc(int rc, const Step& st) {
+  if (rc == 0) return;
+  fail(rc == SB_INVALID_ARGUMENT ? STRATA_INVALID_ARGUMENT : STRATA_INTERNAL,
+       "kernel launch for `" + st.label + "` failed (status " + std::to_string(rc) + ")");
+}
+
+template <typename T>
+int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
+  cudaStream_t s = ctx.stream;
+  switch (st.kind) {
+    case SK::Binary:
+      return sb::launch_binary<T>(int(st.i[0]), P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]), st.bs, s);
+    case SK::Unary:
+      return sb::launch_unary<T>(int(st.i[0]), P<T>(p, st.v[0]), st.i[1], P<T>(p, st.v[1]), s);
+    case SK::Softmax:
+      return sb::launch_softmax<T>(P<T>(p, st.v[0]), st.i[0], st.i[1], P<T>(p, st.v[1]), s);
+    case SK::LayerNorm:
+      return sb::launch_layer_norm<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]), st.i[0],
+                                      st.i[1], float(st.d), P<T>(p, st.v[3]), s);
+    case SK::RmsNorm:
+      return sb::launch_rms_norm<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), st.i[0], st.i[1], float(st.d),
+                                    P<T>(p, st.v[2]), s);
+    case SK::Rope:
+      return sb::launch_rope<T>(P<T>(p, st.v[0]), P<int32_t>(p, st.v[1]), st.i[0], st.i[1], st.i[2], st.d,
+                                P<T>(p, st.v[2]), s);
+    case SK::SwiGLU:
+      return sb::launch_swiglu<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), st.i[0], P<T>(p, st.v[2]), s);
+    case SK::Transpose:
+      return sb::launch_transpose2<T>(P<T>(p, st.v[0]), st.i[0], st.i[1], P<T>(p, st.v[1]), s);
+    case SK::Slice:
+      return sb::launch_slice_cols<T>(P<T>(p, st.v[0]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
+                                      P<T>(p, st.v[1]), s);
+    case SK::Broadcast:
+      return sb::launch_broadcast<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), st.bs, s);
+    case SK::Embed:
+      return sb::launch_embed<T>(P<int32_t>(p, st.v[0]), st.i[0], P<T>(p, st.v[1]), st.i[1], st.i[2],
+                                 P<T>(p, st.v[2]), ctx.d_err, s);
+    case SK::Argmax:
+      return sb::launch_argmax<T>(P<T>(p, st.v[0]), st.i[0], st.i[1], P<int32_t>(p, st.v[1]), s);
+    case SK::KvAppend:
+      return sb::launch_kv_append<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]), P<T>(p, st.v[3]),
+                                     P<int32_t>(p, st.v[4]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
+                                     ctx.d_err, s);
+    case SK::Attention: {
+      float* scratch = st.scratch_bytes ? reinterpret_cast<float*>(static_cast<char*>(p.exe.ws) + st.scratch_off)
+                                        : nullptr;
+      return sb::launch_attention<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]),
+                                     P<int32_t>(p, st.v[3]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
+                                     st.i[5], scratch, P<T>(p, st.v[4]), ctx.d_err, s);
+    }
+    default:
+      return SB_INTERNAL;
+  }
+}
+
+}  // namespace
+
+void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
+  Ptrs p{exe, ext};
+  cudaStream_t s = ctx.stream;
+  for (const Step& st : exe.steps) {
+    int rc = 0;
+    switch (st.kind) {
+      case SK::Linear: {
+        sb::LinearBatch b{};
+        b.x = P<uint16_t>(p, st.v[0]);
+        b.m = int(st.i[0]);
+        b.k = int(st.i[1]);
+        b.fmt = st.fmt;
+        b.epi = st.epi;
+        b.njobs = st.njobs;
+        for (int j = 0; j < st.njobs; ++j) {
+          const uint32_t w = st.v[1 + 4 * j], sc = st.v[2 + 4 * j], y = st.v[3 + 4 * j], r = st.v[4 + 4 * j];
+          const Value& wv = exe.g.values[w];
+          const int n = int(wv.dims[0]);
+          b.jobs[j] = sb::LinearJob{p.at(w), p.at(sc), n, P<uint16_t>(p, y), n, P<uint16_t>(p, r), n};
+        }
+        rc = sb::launch_linear(b, s);
+        break;
+      }
+      case SK::GemmF32:
+        rc = sb::launch_gemm_f32(P<float>(p, st.v[0]), P<float>(p, st.v[1]), P<float>(p, st.v[2]), st.i[0],
+                                 st.i[1], st.i[2], st.i[3] != 0, P<float>(p, st.v[3]), s);
+        break;
+      case SK::Copy: {
+        void* dst = p.at(st.v[1]);
+        const void* src = p.at(st.v[0]);
+        if (dst != src && cudaMemcpyAsync(dst, src, size_t(st.i[0]), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+          rc = SB_INTERNAL;
+        break;
+      }
+      case SK::AllReduce: {
+        void* src = p.at(st.v[0]);
+        void* dst = p.at(st.v[1]);
+        if (ctx.comm && ctx.world > 1) {
+          const ncclResult_t r = ctx.nccl.all_reduce(src, dst, size_t(st.i[0]),
+                                                     st.bf16 ? ncclBfloat16 : ncclFloat32, ncclSum,
+                                                     ctx.comm, s);
+          if (r != ncclSuccess)
+            fail(STRATA_INTERNAL, std::string("ncclAllReduce failed: ") + ctx.nccl.error_string(r));
+        } else if (dst != src) {
+          const size_t bytes = size_t(st.i[0]) * (st.bf16 ? 2 : 4);
+          if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) rc = SB_INTERNAL;
+        }
+        break;
+      }
+      case SK::Quant4:
+        rc = sb::launch_quant_w4g32(P<float>(p, st.v[0]), st.i[0], st.i[1], P<uint8_t>(p, st.v[1]),
+                                    P<uint16_t>(p, st.v[2]), s);
+        break;
+      case SK::Quant8:
+        rc = sb::launch_quant_w8pc(P<float>(p, st.v[0]), st.i[0], st.i[1], P<int8_t>(p, st.v[1]),
+                                   P<float>(p, st.v[2]), s);
+        break;
+      case SK::Dequant4:
+        rc = sb::launch_dequant_w4g32(P<uint8_t>(p, st.v[0]), P<uint16_t>(p, st.v[1]), st.i[0], st.i[1],
+                                      P<float>(p, st.v[2]), s);
+        break;
+      case SK::Dequant8:
+        rc = sb::launch_dequant_w8pc(P<int8_t>(p, st.v[0]), P<float>(p, st.v[1]), st.i[0], st.i[1],
+                                     P<float>(p, st.v[2]), s);
+        break;
+      default:
+        rc = st.bf16 ? run_float<uint16_t>(ctx, st, p) : run_float<float>(ctx, st, p);
+        break;
+    }
+    check_rc(rc, st);
+  }
+}
+
+}  // namespace sbp

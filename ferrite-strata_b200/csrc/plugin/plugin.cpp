@@ -1,0 +1,743 @@
+// libstrata_b200.so: the Ferrite Strata plugin ABI (StrataPluginV1,
+// crates/ferrite-strata-plugin-api/src/raw.rs:591-789) for NVIDIA B200.
+//
+// Entry point contract, restated from the reference host
+// (crates/ferrite-strata-plugin-api/src/host/plugin.rs and host/loader.rs):
+//   * the host dlopens the library, reads `strata_plugin_v1`, checks the nine
+//     mandatory entries, walks the extension chain and calls plugin_init;
+//   * capabilities() returns a framed blob (count + section table + a
+//     Capabilities section) that the host copies and then frees with
+//     free_blob(ctx, &its_own_copy) -- so the payload is freed through
+//     blob->data, never through the header address (plugin.rs:707-733);
+//   * compile() is tri-state: OK with an executable, DECLINED with nothing
+//     allocated, or a failure with an error object (plugin.rs:289-352);
+//   * run() receives StrataBufferRef entries indexed by the decoded subgraph's
+//     value indices (plugin.rs:426-534).
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <new>
+
+#include "plugin.hpp"
+
+using namespace sbp;
+
+struct StrataError {
+  uint32_t code;
+  std::string msg;
+  StrataMessageExt ext;
+};
+
+struct StrataBuffer {
+  Buffer b;
+};
+
+struct StrataExecutable {
+  Exe exe;
+};
+
+struct StrataEvent {
+  cudaEvent_t ev;
+};
+
+namespace {
+
+StrataError* make_error(int32_t code, const std::string& msg) {
+  auto* e = new (std::nothrow) StrataError;
+  if (!e) return nullptr;
+  e->code = uint32_t(code);
+  e->msg = msg;
+  e->ext.base.struct_size = sizeof(StrataMessageExt);
+  e->ext.base.ty = STRATA_EXT_MESSAGE;
+  e->ext.base.next = nullptr;
+  e->ext.message = e->msg.c_str();
+  return e;
+}
+
+int32_t report(StrataError** out, int32_t code, const std::string& msg) {
+  if (out) *out = make_error(code, msg);
+  return code;
+}
+
+// Run `f`, mapping thrown failures onto status codes and error objects.
+template <typename F>
+int32_t guarded(StrataError** out_error, F&& f) {
+  try {
+    return f();
+  } catch (const Failure& fl) {
+    return report(out_error, fl.code, fl.msg);
+  } catch (const WireError& we) {
+    return report(out_error, STRATA_INVALID_ARGUMENT, std::string("malformed subgraph blob: ") + we.what());
+  } catch (const std::bad_alloc&) {
+    return report(out_error, STRATA_RESOURCE_EXHAUSTED, "host memory exhausted");
+  } catch (const std::exception& ex) {
+    return report(out_error, STRATA_INTERNAL, ex.what());
+  }
+}
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return;
+  const int32_t code = e == cudaErrorMemoryAllocation ? STRATA_RESOURCE_EXHAUSTED : STRATA_INTERNAL;
+  fail(code, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+Ctx* C(void* ctx) {
+  if (!ctx) fail(STRATA_INVALID_ARGUMENT, "null plugin context");
+  return static_cast<Ctx*>(ctx);
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : dflt;
+}
+
+bool graphs_enabled() { return env_int("STRATA_B200_CUDA_GRAPHS", 1) != 0; }
+
+// Cache of device allocations by rounded size, so per-run buffers (the
+// reference host allocates one per value per run) do not hit cudaMalloc.
+struct Pool {
+  std::multimap<uint64_t, void*> free_;
+  void* get(uint64_t bytes) {
+    auto it = free_.find(bytes);
+    if (it == free_.end()) return nullptr;
+    void* p = it->second;
+    free_.erase(it);
+    return p;
+  }
+  void put(uint64_t bytes, void* p) { free_.emplace(bytes, p); }
+  void drain() {
+    for (auto& kv : free_) cudaFree(kv.second);
+    free_.clear();
+  }
+};
+Pool g_pool;
+
+uint64_t round_bytes(uint64_t b) { return (std::max<uint64_t>(b, 1) + 255) & ~uint64_t(255); }
+
+void* device_alloc(Ctx& c, uint64_t bytes) {
+  const uint64_t rb = round_bytes(bytes);
+  if (void* p = g_pool.get(rb)) return p;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, rb);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    g_pool.drain();
+    e = cudaMalloc(&p, rb);
+  }
+  cuda_check(e, "cudaMalloc");
+  (void)c;
+  return p;
+}
+
+void device_free(uint64_t bytes, void* p) {
+  if (p) g_pool.put(round_bytes(bytes), p);
+}
+
+}  // namespace
+
+namespace sbp {
+
+void Ctx::ensure_device() {
+  if (!has_device) fail(STRATA_INTERNAL, "no CUDA device is visible to this process");
+  cuda_check(cudaSetDevice(device), "cudaSetDevice");
+  if (device_ready) return;
+  cuda_check(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  cuda_check(cudaMalloc(&d_err, sizeof(int)), "cudaMalloc(error word)");
+  cuda_check(cudaMemset(d_err, 0, sizeof(int)), "cudaMemset(error word)");
+  device_ready = true;
+}
+
+// After a synchronize: surface launch/execution errors and the kernels'
+// input-validation word.
+void Ctx::check_device_error(const char* where) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) fail(STRATA_INTERNAL, std::string(where) + ": " + cudaGetErrorString(e));
+  int word = 0;
+  cuda_check(cudaMemcpy(&word, d_err, sizeof(int), cudaMemcpyDeviceToHost), "reading the error word");
+  if (word) {
+    cuda_check(cudaMemset(d_err, 0, sizeof(int)), "clearing the error word");
+    const char* what = word == 2 ? "a position is outside the KV cache"
+                     : word == 3 ? "a token id is outside the embedding table"
+                                 : "a kernel rejected its input";
+    fail(STRATA_INVALID_ARGUMENT, std::string(where) + ": " + what);
+  }
+}
+
+bool Nccl::load(std::string* why) {
+  if (lib) return true;
+  for (const char* name : {"libnccl.so.2", "libnccl.so"}) {
+    lib = dlopen(name, RTLD_NOW | RTLD_GLOBAL);
+    if (lib) break;
+  }
+  if (!lib) {
+    *why = "libnccl.so.2 could not be loaded";
+    return false;
+  }
+  get_unique_id = reinterpret_cast<decltype(get_unique_id)>(dlsym(lib, "ncclGetUniqueId"));
+  comm_init_rank = reinterpret_cast<decltype(comm_init_rank)>(dlsym(lib, "ncclCommInitRank"));
+  all_reduce = reinterpret_cast<decltype(all_reduce)>(dlsym(lib, "ncclAllReduce"));
+  comm_destroy = reinterpret_cast<decltype(comm_destroy)>(dlsym(lib, "ncclCommDestroy"));
+  error_string = reinterpret_cast<decltype(error_string)>(dlsym(lib, "ncclGetErrorString"));
+  if (!get_unique_id || !comm_init_rank || !all_reduce || !comm_destroy || !error_string) {
+    *why = "libnccl.so.2 lacks an expected symbol";
+    return false;
+  }
+  return true;
+}
+
+}  // namespace sbp
+
+// ---------------------------------------------------------------------------
+// Error entries (raw.rs:603-616)
+// ---------------------------------------------------------------------------
+
+static void sb_error_free(StrataError* e) { delete e; }
+
+static uint32_t sb_error_code(const StrataError* e) { return e ? e->code : uint32_t(STRATA_INTERNAL); }
+
+static void sb_error_payload(const StrataError* e, StrataPayloadVisitor visitor, void* vctx) {
+  if (!e || !visitor) return;
+  visitor(vctx, const_cast<StrataExtBase*>(&e->ext.base));
+}
+
+// ---------------------------------------------------------------------------
+// Capability (raw.rs:618-640)
+// ---------------------------------------------------------------------------
+
+static int32_t sb_capabilities(void* ctx, StrataWireBlob* out) {
+  if (!ctx || !out) return STRATA_INVALID_ARGUMENT;
+  try {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (c->caps.empty()) c->caps = build_caps(*c);
+    const std::vector<uint8_t> framed = frame_payload(kSectionCaps, c->caps);
+    uint8_t* data = new uint8_t[framed.size() + 1];
+    std::memcpy(data, framed.data(), framed.size());
+    data[framed.size()] = 0;
+    out->magic = kMagic;
+    out->format_major = kFormatMajor;
+    out->format_minor = kFormatMinor;
+    out->payload_len = framed.size();
+    out->data = data;
+    out->nul = 0;
+    return STRATA_OK;
+  } catch (...) {
+    return STRATA_INTERNAL;
+  }
+}
+
+static uint32_t sb_supports(void* ctx, const StrataPatternQuery* q) {
+  (void)ctx;
+  if (!q || q->struct_size < sizeof(StrataPatternQuery) || (!q->pattern_id && q->pattern_id_len))
+    return STRATA_SUPPORT_REFUSE;
+  const std::string pattern(reinterpret_cast<const char*>(q->pattern_id), q->pattern_id_len);
+  DType dt;
+  dt.elem = q->dtype.element;
+  dt.qkind = q->dtype.quant.kind;
+  dt.block = q->dtype.quant.block_size;
+  dt.sym = q->dtype.quant.symmetric;
+  return supports_query(pattern, dt, q->shape_class.kind, q->shape_class.rank);
+}
+
+// ---------------------------------------------------------------------------
+// Compile (raw.rs:642-657)
+// ---------------------------------------------------------------------------
+
+static int32_t sb_compile(void* ctx, const StrataCompileArgs* a, StrataExecutable** out_exe,
+                          StrataError** out_error) {
+  if (out_exe) *out_exe = nullptr;
+  if (out_error) *out_error = nullptr;
+  return guarded(out_error, [&]() -> int32_t {
+    C(ctx);
+    if (!a || !out_exe) fail(STRATA_INVALID_ARGUMENT, "compile needs arguments and an out-parameter");
+    if (a->struct_size < sizeof(StrataCompileArgs))
+      fail(STRATA_INVALID_ARGUMENT, "StrataCompileArgs is shorter than this plugin's ABI");
+    const StrataWireBlob& b = a->subgraph;
+    if (b.magic != kMagic) fail(STRATA_INVALID_ARGUMENT, "the subgraph blob has the wrong magic");
+    if (b.format_major != kFormatMajor)
+      fail(STRATA_INVALID_ARGUMENT, "unsupported wire format major " + std::to_string(b.format_major));
+    if (!b.data && b.payload_len) fail(STRATA_INVALID_ARGUMENT, "null subgraph payload");
+    const uint8_t* sec = nullptr;
+    size_t sec_len = 0;
+    if (!find_section(b.data, size_t(b.payload_len), kSectionGraph, &sec, &sec_len))
+      fail(STRATA_INVALID_ARGUMENT, "the subgraph blob carries no graph section");
+    auto holder = std::make_unique<StrataExecutable>();
+    holder->exe.g = decode_graph(sec, sec_len);
+    holder->exe.label = "b200::" + holder->exe.g.name;
+    std::string reason;
+    if (!lower(holder->exe.g, holder->exe, &reason)) return STRATA_DECLINED;  // nothing allocated
+    *out_exe = holder.release();
+    return STRATA_OK;
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Buffers and events (raw.rs:659-725)
+// ---------------------------------------------------------------------------
+
+static int32_t sb_alloc(void* ctx, const StrataAllocDesc* d, StrataBuffer** out, StrataError** out_error) {
+  if (out) *out = nullptr;
+  if (out_error) *out_error = nullptr;
+  return guarded(out_error, [&]() -> int32_t {
+    Ctx* c = C(ctx);
+    if (!d || !out) fail(STRATA_INVALID_ARGUMENT, "alloc needs a descriptor and an out-parameter");
+    if (d->struct_size < sizeof(StrataAllocDesc)) fail(STRATA_INVALID_ARGUMENT, "StrataAllocDesc is too short");
+    if (d->rank > 8 || (d->rank && !d->dims)) fail(STRATA_INVALID_ARGUMENT, "bad rank or dims");
+    DType dt;
+    dt.elem = d->dtype.element;
+    uint64_t n = 1;
+    for (uint32_t i = 0; i < d->rank; ++i) {
+      if (d->dims[i] && n > (uint64_t(1) << 46) / d->dims[i])
+        fail(STRATA_RESOURCE_EXHAUSTED, "allocation size overflows");
+      n *= d->dims[i];
+    }
+    const uint64_t bytes = n * dt.elem_bytes();
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+    auto buf = std::make_unique<StrataBuffer>();
+    buf->b.ptr = device_alloc(*c, bytes);
+    buf->b.bytes = bytes;
+    buf->b.owned = true;
+    *out = buf.release();
+    return STRATA_OK;
+  });
+}
+
+static int32_t sb_buffer_release(void* ctx, StrataBuffer* b) {
+  if (!ctx || !b) return STRATA_INVALID_ARGUMENT;
+  Ctx* c = static_cast<Ctx*>(ctx);
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (b->b.owned && b->b.ptr) {
+    // The stream may still be reading it; release only after queued work.
+    if (c->device_ready) cudaStreamSynchronize(c->stream);
+    device_free(b->b.bytes, b->b.ptr);
+  }
+  delete b;
+  return STRATA_OK;
+}
+
+static int32_t sb_buffer_write(void* ctx, StrataBuffer* b, uint64_t offset, const uint8_t* data, uint64_t len) {
+  if (!ctx || !b || (!data && len)) return STRATA_INVALID_ARGUMENT;
+  if (offset > b->b.bytes || len > b->b.bytes - offset) return STRATA_INVALID_ARGUMENT;
+  if (len == 0) return STRATA_OK;
+  try {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+    cuda_check(cudaMemcpyAsync(static_cast<char*>(b->b.ptr) + offset, data, size_t(len), cudaMemcpyHostToDevice,
+                               c->stream),
+               "buffer_write");
+    cuda_check(cudaStreamSynchronize(c->stream), "buffer_write");
+    return STRATA_OK;
+  } catch (const Failure& f) {
+    return f.code;
+  }
+}
+
+static int32_t sb_buffer_read(void* ctx, const StrataBuffer* b, uint64_t offset, uint8_t* data, uint64_t len) {
+  if (!ctx || !b || (!data && len)) return STRATA_INVALID_ARGUMENT;
+  if (offset > b->b.bytes || len > b->b.bytes - offset) return STRATA_INVALID_ARGUMENT;
+  if (len == 0) return STRATA_OK;
+  try {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+    cuda_check(cudaMemcpyAsync(data, static_cast<const char*>(b->b.ptr) + offset, size_t(len),
+                               cudaMemcpyDeviceToHost, c->stream),
+               "buffer_read");
+    cuda_check(cudaStreamSynchronize(c->stream), "buffer_read");
+    return STRATA_OK;
+  } catch (const Failure& f) {
+    return f.code;
+  }
+}
+
+static int32_t sb_buffer_event(void* ctx, const StrataBuffer* b, StrataEvent** out) {
+  if (!ctx || !b || !out) return STRATA_INVALID_ARGUMENT;
+  try {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+    auto ev = std::make_unique<StrataEvent>();
+    cuda_check(cudaEventCreateWithFlags(&ev->ev, cudaEventDisableTiming), "cudaEventCreate");
+    cuda_check(cudaEventRecord(ev->ev, c->stream), "cudaEventRecord");
+    *out = ev.release();
+    return STRATA_OK;
+  } catch (const Failure& f) {
+    return f.code;
+  }
+}
+
+static int32_t sb_event_ready(void* ctx, const StrataEvent* e) {
+  if (!ctx || !e) return STRATA_INVALID_ARGUMENT;
+  const cudaError_t r = cudaEventQuery(e->ev);
+  if (r == cudaSuccess) return 1;
+  if (r == cudaErrorNotReady) {
+    cudaGetLastError();
+    return 0;
+  }
+  return STRATA_INTERNAL;
+}
+
+static int32_t sb_event_await(void* ctx, const StrataEvent* e) {
+  if (!ctx || !e) return STRATA_INVALID_ARGUMENT;
+  return cudaEventSynchronize(e->ev) == cudaSuccess ? STRATA_OK : STRATA_INTERNAL;
+}
+
+static int32_t sb_event_free(void* ctx, StrataEvent* e) {
+  if (!ctx || !e) return STRATA_INVALID_ARGUMENT;
+  cudaEventDestroy(e->ev);
+  delete e;
+  return STRATA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Run (raw.rs:727-735)
+// ---------------------------------------------------------------------------
+
+namespace {
+
+// Enqueue one run on the context's stream.  Caller holds c.mu.
+void enqueue_run(Ctx& c, const StrataRunArgs* a) {
+  if (!a) fail(STRATA_INVALID_ARGUMENT, "run needs arguments");
+  if (a->struct_size < sizeof(StrataRunArgs)) fail(STRATA_INVALID_ARGUMENT, "StrataRunArgs is too short");
+  if (!a->executable) fail(STRATA_INVALID_ARGUMENT, "run was given a null executable");
+  if (a->arg_count && !a->args) fail(STRATA_INVALID_ARGUMENT, "run was given a null argument array");
+  Exe& e = const_cast<StrataExecutable*>(a->executable)->exe;
+  const size_t nv = e.g.values.size();
+  std::vector<void*> ext(nv, nullptr);
+  for (uint32_t i = 0; i < a->arg_count; ++i) {
+    const StrataBufferRef& r = a->args[i];
+    if (r.value_index >= nv)
+      fail(STRATA_INVALID_ARGUMENT, "argument names value " + std::to_string(r.value_index) +
+                                        ", which this executable does not have");
+    if (!r.buffer) continue;
+    const uint32_t v = r.value_index;
+    const bool is_in = e.g.values[v].producer < 0 || e.needed_input[v];
+    const bool is_out = e.is_output[v];
+    if (!is_in && !is_out) continue;  // intermediates live in the plugin's workspace
+    if (r.buffer->b.bytes < e.g.values[v].bytes())
+      fail(STRATA_INVALID_ARGUMENT, "the buffer for `" + e.g.values[v].name + "` holds " +
+                                        std::to_string(r.buffer->b.bytes) + " bytes, it needs " +
+                                        std::to_string(e.g.values[v].bytes()));
+    ext[v] = r.buffer->b.ptr;
+  }
+  for (size_t v = 0; v < nv; ++v)
+    if (e.needed_input[v] && !ext[v] && e.g.values[v].bytes() > 0)
+      fail(STRATA_INVALID_ARGUMENT, "no buffer for input `" + e.g.values[v].name + "` of `" + e.label + "`");
+  c.ensure_device();
+  if (!e.ws && e.ws_bytes) cuda_check(cudaMalloc(&e.ws, e.ws_bytes), "workspace cudaMalloc");
+
+  if (!graphs_enabled()) {
+    enqueue(c, e, ext);
+    return;
+  }
+  for (auto& cg : e.graphs) {
+    if (cg.key == ext) {
+      cuda_check(cudaGraphLaunch(cg.exec, c.stream), "cudaGraphLaunch");
+      sb::count_launch(cg.kernels);
+      return;
+    }
+  }
+  if (ext != e.last_key) {
+    // First time with these pointers: run eagerly, capture if they repeat.
+    e.last_key = ext;
+    enqueue(c, e, ext);
+    return;
+  }
+  cuda_check(cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+  const uint64_t before = sb::g_launches.load();
+  try {
+    enqueue(c, e, ext);
+  } catch (...) {
+    cudaGraph_t dead = nullptr;
+    cudaStreamEndCapture(c.stream, &dead);
+    if (dead) cudaGraphDestroy(dead);
+    cudaGetLastError();
+    throw;
+  }
+  const uint64_t kernels = sb::g_launches.load() - before;
+  sb::g_launches.fetch_sub(kernels);
+  cudaGraph_t graph = nullptr;
+  cuda_check(cudaStreamEndCapture(c.stream, &graph), "cudaStreamEndCapture");
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  cuda_check(ie, "cudaGraphInstantiate");
+  if (e.graphs.size() >= 4) {
+    cudaGraphExecDestroy(e.graphs.front().exec);
+    e.graphs.erase(e.graphs.begin());
+  }
+  e.graphs.push_back(Exe::Cached{ext, exec, kernels});
+  cuda_check(cudaGraphLaunch(exec, c.stream), "cudaGraphLaunch");
+  sb::count_launch(kernels);
+}
+
+void copy_to_host_arena(Ctx& c, const StrataRunArgs* a) {
+  if (!a->host_arena || !a->host_arena->entries) return;
+  const Exe& e = a->executable->exe;
+  // Entries are indexed by value index; an output whose entry is present and
+  // sized for it is copied out.
+  std::vector<void*> ext(e.g.values.size(), nullptr);
+  for (uint32_t i = 0; i < a->arg_count; ++i)
+    if (a->args[i].buffer && a->args[i].value_index < ext.size())
+      ext[a->args[i].value_index] = a->args[i].buffer->b.ptr;
+  for (auto o : e.g.outputs) {
+    if (o >= a->host_arena->entry_count) continue;
+    StrataArenaEntryView& ent = a->host_arena->entries[o];
+    if (!ent.data || ent.element_count != uint64_t(e.g.values[o].elements())) continue;
+    const uint32_t b = e.alias[o];
+    const void* src = ext[o] ? ext[o] : (e.ws_off[b] >= 0 ? static_cast<const char*>(e.ws) + e.ws_off[b] : nullptr);
+    if (!src) continue;
+    cuda_check(cudaMemcpyAsync(ent.data, src, e.g.values[o].bytes(), cudaMemcpyDeviceToHost, c.stream),
+               "host arena copy");
+  }
+  cuda_check(cudaStreamSynchronize(c.stream), "host arena copy");
+}
+
+}  // namespace
+
+static int32_t sb_run(void* ctx, const StrataRunArgs* a, StrataError** out_error) {
+  if (out_error) *out_error = nullptr;
+  return guarded(out_error, [&]() -> int32_t {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    enqueue_run(*c, a);
+    cuda_check(cudaStreamSynchronize(c->stream), "run");
+    c->check_device_error(a->executable->exe.label.c_str());
+    copy_to_host_arena(*c, a);
+    return STRATA_OK;
+  });
+}
+
+static int32_t sb_run_async(void* ctx, const StrataRunArgs* a, StrataError** out_error) {
+  if (out_error) *out_error = nullptr;
+  return guarded(out_error, [&]() -> int32_t {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    enqueue_run(*c, a);
+    return STRATA_OK;
+  });
+}
+
+static int32_t sb_synchronize(void* ctx, StrataError** out_error) {
+  if (out_error) *out_error = nullptr;
+  return guarded(out_error, [&]() -> int32_t {
+    Ctx* c = C(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+    cuda_check(cudaStreamSynchronize(c->stream), "synchronize");
+    c->check_device_error("synchronize");
+    return STRATA_OK;
+  });
+}
+
+// ---------------------------------------------------------------------------
+// Teardown (raw.rs:737-757)
+// ---------------------------------------------------------------------------
+
+static void sb_free_executable(void* ctx, StrataExecutable* e) {
+  if (!e) return;
+  if (ctx) {
+    Ctx* c = static_cast<Ctx*>(ctx);
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (c->device_ready) cudaStreamSynchronize(c->stream);
+  }
+  delete e;
+}
+
+static void sb_free_blob(void* ctx, StrataWireBlob* blob) {
+  (void)ctx;
+  if (!blob) return;
+  delete[] const_cast<uint8_t*>(blob->data);
+  blob->data = nullptr;
+}
+
+static void* sb_plugin_init(void) {
+  auto* c = new (std::nothrow) Ctx;
+  if (!c) return nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess) {
+    cudaGetLastError();
+    count = 0;
+  }
+  c->has_device = count > 0;
+  c->device = env_int("STRATA_B200_DEVICE", env_int("LOCAL_RANK", 0));
+  if (c->has_device) {
+    if (c->device >= count) c->device = c->device % count;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, c->device) == cudaSuccess) {
+      c->device_name = prop.name;
+      c->memory_bytes = prop.totalGlobalMem;
+    }
+  }
+  return c;
+}
+
+static void sb_plugin_free(void* ctx) {
+  if (!ctx) return;
+  Ctx* c = static_cast<Ctx*>(ctx);
+  if (c->device_ready) {
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->comm) c->nccl.comm_destroy(c->comm);
+    g_pool.drain();
+    cudaFree(c->d_err);
+    cudaStreamDestroy(c->stream);
+  }
+  delete c;
+}
+
+// ---------------------------------------------------------------------------
+// Extension chain: plugin version, then the B200 device extension
+// ---------------------------------------------------------------------------
+
+static int32_t ext_buffer_wrap(void* ctx, void* ptr, uint64_t bytes, StrataBuffer** out) {
+  if (!ctx || !out || (!ptr && bytes)) return STRATA_INVALID_ARGUMENT;
+  auto* b = new (std::nothrow) StrataBuffer;
+  if (!b) return STRATA_RESOURCE_EXHAUSTED;
+  b->b.ptr = ptr;
+  b->b.bytes = bytes;
+  b->b.owned = false;
+  *out = b;
+  return STRATA_OK;
+}
+
+static int32_t ext_buffer_device_ptr(void* ctx, const StrataBuffer* b, void** out_ptr, uint64_t* out_bytes) {
+  if (!ctx || !b) return STRATA_INVALID_ARGUMENT;
+  if (out_ptr) *out_ptr = b->b.ptr;
+  if (out_bytes) *out_bytes = b->b.bytes;
+  return STRATA_OK;
+}
+
+static void* ext_stream(void* ctx) {
+  if (!ctx) return nullptr;
+  Ctx* c = static_cast<Ctx*>(ctx);
+  try {
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+  } catch (...) {
+    return nullptr;
+  }
+  return c->stream;
+}
+
+static uint64_t ext_launch_count(void* ctx) {
+  (void)ctx;
+  return sb::g_launches.load();
+}
+
+static int32_t ext_tp_unique_id(void* ctx, uint8_t out[128]) {
+  if (!ctx || !out) return STRATA_INVALID_ARGUMENT;
+  Ctx* c = static_cast<Ctx*>(ctx);
+  std::string why;
+  if (!c->nccl.load(&why)) return STRATA_UNIMPLEMENTED;
+  ncclUniqueId id;
+  if (c->nccl.get_unique_id(&id) != ncclSuccess) return STRATA_INTERNAL;
+  static_assert(sizeof(id) == 128, "ncclUniqueId is 128 bytes");
+  std::memcpy(out, &id, 128);
+  return STRATA_OK;
+}
+
+static int32_t ext_tp_init(void* ctx, int32_t rank, int32_t world, const uint8_t id[128], StrataError** out_error) {
+  if (out_error) *out_error = nullptr;
+  return guarded(out_error, [&]() -> int32_t {
+    Ctx* c = C(ctx);
+    if (!id || world < 1 || rank < 0 || rank >= world) fail(STRATA_INVALID_ARGUMENT, "bad tensor-parallel rank");
+    std::lock_guard<std::mutex> lk(c->mu);
+    c->ensure_device();
+    if (world == 1) {
+      c->rank = 0;
+      c->world = 1;
+      return STRATA_OK;
+    }
+    std::string why;
+    if (!c->nccl.load(&why)) fail(STRATA_UNIMPLEMENTED, why);
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, 128);
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = c->nccl.comm_init_rank(&comm, world, uid, rank);
+    if (r != ncclSuccess) fail(STRATA_INTERNAL, std::string("ncclCommInitRank: ") + c->nccl.error_string(r));
+    c->comm = comm;
+    c->rank = rank;
+    c->world = world;
+    return STRATA_OK;
+  });
+}
+
+static int32_t ext_set_device(void* ctx, int32_t device) {
+  if (!ctx) return STRATA_INVALID_ARGUMENT;
+  Ctx* c = static_cast<Ctx*>(ctx);
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (c->device_ready && c->device != device) return STRATA_INVALID_ARGUMENT;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count) {
+    cudaGetLastError();
+    return STRATA_INVALID_ARGUMENT;
+  }
+  c->device = device;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) {
+    c->device_name = prop.name;
+    c->memory_bytes = prop.totalGlobalMem;
+  }
+  c->caps.clear();
+  return STRATA_OK;
+}
+
+static StrataB200DeviceExt g_device_ext = {
+    {sizeof(StrataB200DeviceExt), STRATA_B200_EXT_DEVICE, nullptr},
+    STRATA_B200_EXT_DEVICE_VERSION,
+    0,
+    ext_buffer_wrap,
+    ext_buffer_device_ptr,
+    sb_run_async,
+    sb_synchronize,
+    ext_stream,
+    ext_launch_count,
+    ext_tp_unique_id,
+    ext_tp_init,
+    ext_set_device,
+};
+
+static StrataPluginVersionExt g_version_ext = {
+    {sizeof(StrataPluginVersionExt), STRATA_EXT_PLUGIN_VERSION,
+     reinterpret_cast<StrataExtBase*>(&g_device_ext)},
+    0,
+    1,
+    0,
+    {STRATA_ABI_MAJOR, STRATA_ABI_MINOR},
+};
+
+extern "C" {
+__attribute__((visibility("default"))) StrataPluginV1 strata_plugin_v1 = {
+    sizeof(StrataPluginV1),
+    reinterpret_cast<StrataExtBase*>(&g_version_ext),
+    {STRATA_ABI_MAJOR, STRATA_ABI_MINOR},
+    sb_error_free,
+    sb_error_code,
+    sb_error_payload,
+    sb_capabilities,
+    sb_supports,
+    sb_compile,
+    sb_alloc,
+    sb_buffer_release,
+    sb_buffer_write,
+    sb_buffer_read,
+    sb_buffer_event,
+    sb_event_ready,
+    sb_event_await,
+    sb_event_free,
+    sb_run,
+    sb_free_executable,
+    sb_free_blob,
+    sb_plugin_init,
+    sb_plugin_free,
+    nullptr,  // serialize
+    nullptr,  // deserialize_load
+    nullptr,  // abi_compatible
+};
+}  // extern "C"

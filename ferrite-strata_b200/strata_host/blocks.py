@@ -1,0 +1,195 @@
+"""Decoder-block subgraphs in the Strata IR, ready for the B200 plugin.
+
+The reference IR has no decoder ops (crates/ferrite-strata/src/graph.rs:56-128),
+so each one is an ``Op::Custom`` with a vendor pattern id and its parameters in
+node attributes (attrs.rs:39-51), and every weight is a node input so that a
+subgraph cut keeps it (graph.rs:422-436 remaps only node inputs):
+
+==========================  =========================================  ====================
+pattern                     inputs                                     attributes
+==========================  =========================================  ====================
+fused::linear_w4g32         x bf16 [M,K], codes U8{32} [N,K/2],        bits=4, group_size=32
+                            scales bf16 [N,K/32]
+fused::linear_w8pc          x bf16 [M,K], codes I8{K} [N,K], f32 [N]   bits=8
+fused::rms_norm             x [R,C], gamma [C]                         eps
+fused::rope                 x [R,H*d], pos I32 [R]                     head_dim, theta
+fused::swiglu               gate, up (same shape)
+fused::attention            q [R,H*d], k [R,G*d], v [R,G*d],           num_heads,
+                            k_cache, v_cache [B,G,L,d], pos I32 [R]    num_kv_heads, head_dim
+fused::embed                ids I32 [R], table [V,D]
+fused::argmax               x [R,C] -> I32 [R] (lowest index on ties)
+fused::all_reduce           x -> sum of x over the tensor-parallel group
+==========================  =========================================  ====================
+
+``fused::attention`` appends row r's k/v at ``pos[r]`` of sequence
+``r // (R / B)`` in the caches (an in-place update of two inputs) and then
+attends over positions ``0..pos[r]``; causality comes from the positions.
+Tensor-parallel builds shard q/k/v/gate/up by output column and o/down by
+input row, with an all-reduce after o_proj and after down_proj only.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+from .ir import BF16, F32, I32, W4G32, DType, GraphBuilder, Op, w8pc
+
+
+@dataclass(frozen=True)
+class DecoderShape:
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    layers: int
+    eps: float = 1e-5
+    theta: float = 10000.0
+
+
+# The shapes the benchmark configurations name.
+BLOCK_512 = DecoderShape(512, 8, 8, 64, 1408, 0, 1)
+LLAMA_7B = DecoderShape(4096, 32, 32, 128, 11008, 32000, 32)
+LLAMA_70B = DecoderShape(8192, 64, 8, 128, 28672, 0, 80)
+
+
+@dataclass
+class LayerHandles:
+    ids: dict = field(default_factory=dict)   # weight / cache name -> value id
+
+
+@dataclass
+class DecoderHandles:
+    tokens: int = -1            # ids I32 [R] (embed=True) or activations [R, D]
+    pos: int = -1               # I32 [R]
+    layers: list = field(default_factory=list)
+    final_norm: int = -1
+    lm_w: int = -1
+    lm_s: int = -1
+    embed_table: int = -1
+    out: int = -1               # argmax ids, logits, or the last hidden state
+    hidden_out: int = -1
+
+
+def weight_shapes(shape: DecoderShape, fmt: str, tp_world: int = 1) -> dict:
+    """Per-layer weight tensors (name -> (dtype, dims)) for one rank."""
+    D, H, G, d, F = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn
+    t = tp_world
+    if H % t or G % t or F % t:
+        raise ValueError("heads, kv heads and ffn must divide by the tensor-parallel size")
+    act = F32 if fmt == "f32" else BF16
+    mats = {"q": (H // t * d, D), "k": (G // t * d, D), "v": (G // t * d, D), "o": (D, H // t * d),
+            "g": (F // t, D), "u": (F // t, D), "d": (D, F // t)}
+    out = {"attn_norm": (act, (D,)), "ffn_norm": (act, (D,))}
+    for key, (n, k) in mats.items():
+        if fmt == "w4g32":
+            out["w" + key] = (W4G32, (n, k // 2))
+            out["s" + key] = (BF16, (n, k // 32))
+        elif fmt == "w8pc":
+            out["w" + key] = (w8pc(k), (n, k))
+            out["s" + key] = (F32, (n,))
+        elif fmt in ("f32", "bf16"):
+            out["w" + key] = (act, (n, k))
+        else:
+            raise ValueError(f"unknown weight format {fmt}")
+    return out
+
+
+def _linear(b: GraphBuilder, x: int, W: dict, key: str, m: int, n: int, fmt: str, act: DType,
+            name: str) -> int:
+    if fmt == "w4g32":
+        return b.node(Op.custom("fused::linear_w4g32"), [x, W["w" + key], W["s" + key]],
+                      [(BF16, (m, n))], {"bits": 4, "group_size": 32}, name)[0]
+    if fmt == "w8pc":
+        return b.node(Op.custom("fused::linear_w8pc"), [x, W["w" + key], W["s" + key]],
+                      [(BF16, (m, n))], {"bits": 8}, name)[0]
+    return b.node(Op("linear", weight=W["w" + key]), [x], [(act, (m, n))], {}, name)[0]
+
+
+def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fmt: str = "w4g32",
+                  layers: int | None = None, embed: bool = True, head: str = "argmax",
+                  lm_fmt: str | None = None, tp_rank: int = 0, tp_world: int = 1,
+                  name: str = "decoder"):
+    """One forward step of ``layers`` decoder blocks over ``batch * seq`` rows.
+
+    ``seq == 1`` is a decode step; ``seq > 1`` a prefill from position 0 (the
+    caller fills ``pos``).  ``head``: "argmax" (next-token ids), "logits", or
+    "none" (the last hidden state is the output).
+    """
+    layers = shape.layers if layers is None else layers
+    act = F32 if fmt == "f32" else BF16
+    D, H, G, d = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim
+    t = tp_world
+    R = batch * seq
+    b = GraphBuilder(name)
+    hd = DecoderHandles()
+    if embed:
+        hd.tokens = b.input(I32, (R,), "ids")
+        hd.embed_table = b.input(act, (shape.vocab, D), "embed_table")
+    else:
+        hd.tokens = b.input(act, (R, D), "x")
+    hd.pos = b.input(I32, (R,), "pos")
+    wshapes = weight_shapes(shape, fmt, t)
+    for li in range(layers):
+        W = {k: b.input(dt, dims, f"l{li}.{k}") for k, (dt, dims) in wshapes.items()}
+        W["k_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.k_cache")
+        W["v_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.v_cache")
+        hd.layers.append(LayerHandles(W))
+    if head != "none":
+        hd.final_norm = b.input(act, (D,), "final_norm")
+        lmf = lm_fmt or fmt
+        if lmf == "w4g32":
+            hd.lm_w = b.input(W4G32, (shape.vocab, D // 2), "lm_head.w")
+            hd.lm_s = b.input(BF16, (shape.vocab, D // 32), "lm_head.s")
+        elif lmf == "w8pc":
+            hd.lm_w = b.input(w8pc(D), (shape.vocab, D), "lm_head.w")
+            hd.lm_s = b.input(F32, (shape.vocab,), "lm_head.s")
+        else:
+            hd.lm_w = b.input(act, (shape.vocab, D), "lm_head.w")
+
+    if embed:
+        h = b.node(Op.custom("fused::embed"), [hd.tokens, hd.embed_table], [(act, (R, D))], {}, "embed")[0]
+    else:
+        h = hd.tokens
+    Hl, Gl, Fl = H // t, G // t, shape.ffn // t
+    for li, L in enumerate(hd.layers):
+        W = L.ids
+        p = f"l{li}."
+        n1 = b.node(Op.custom("fused::rms_norm"), [h, W["attn_norm"]], [(act, (R, D))],
+                    {"eps": float(shape.eps)}, p + "attn_rms")[0]
+        q = _linear(b, n1, W, "q", R, Hl * d, fmt, act, p + "q_proj")
+        k = _linear(b, n1, W, "k", R, Gl * d, fmt, act, p + "k_proj")
+        v = _linear(b, n1, W, "v", R, Gl * d, fmt, act, p + "v_proj")
+        rope_attrs = {"head_dim": d, "theta": float(shape.theta)}
+        qr = b.node(Op.custom("fused::rope"), [q, hd.pos], [(act, (R, Hl * d))], rope_attrs, p + "q_rope")[0]
+        kr = b.node(Op.custom("fused::rope"), [k, hd.pos], [(act, (R, Gl * d))], rope_attrs, p + "k_rope")[0]
+        o = b.node(Op.custom("fused::attention"), [qr, kr, v, W["k_cache"], W["v_cache"], hd.pos],
+                   [(act, (R, Hl * d))], {"num_heads": Hl, "num_kv_heads": Gl, "head_dim": d},
+                   p + "attention")[0]
+        a = _linear(b, o, W, "o", R, D, fmt, act, p + "o_proj")
+        if t > 1:
+            a = b.node(Op.custom("fused::all_reduce"), [a], [(act, (R, D))], {}, p + "o_allreduce")[0]
+        h2 = b.node(Op("add"), [h, a], [(act, (R, D))], {}, p + "attn_residual")[0]
+        n2 = b.node(Op.custom("fused::rms_norm"), [h2, W["ffn_norm"]], [(act, (R, D))],
+                    {"eps": float(shape.eps)}, p + "ffn_rms")[0]
+        gt = _linear(b, n2, W, "g", R, Fl, fmt, act, p + "gate_proj")
+        up = _linear(b, n2, W, "u", R, Fl, fmt, act, p + "up_proj")
+        s = b.node(Op.custom("fused::swiglu"), [gt, up], [(act, (R, Fl))], {}, p + "swiglu")[0]
+        dn = _linear(b, s, W, "d", R, D, fmt, act, p + "down_proj")
+        if t > 1:
+            dn = b.node(Op.custom("fused::all_reduce"), [dn], [(act, (R, D))], {}, p + "down_allreduce")[0]
+        h = b.node(Op("add"), [h2, dn], [(act, (R, D))], {}, p + "ffn_residual")[0]
+    hd.hidden_out = h
+    if head == "none":
+        hd.out = h
+    else:
+        hf = b.node(Op.custom("fused::rms_norm"), [h, hd.final_norm], [(act, (R, D))],
+                    {"eps": float(shape.eps)}, "final_norm_op")[0]
+        W = {"wlm": hd.lm_w, "slm": hd.lm_s}
+        logits = _linear(b, hf, W, "lm", R, shape.vocab, lm_fmt or fmt, act, "lm_head")
+        if head == "logits":
+            hd.out = logits
+        else:
+            hd.out = b.node(Op.custom("fused::argmax"), [logits], [(I32, (R,))], {}, "argmax")[0]
+    b.output(hd.out)
+    return b.build(), hd

@@ -1,0 +1,235 @@
+"""Graph-level parity on the B200 through the plugin ABI (strata_plugin_v1):
+compile a subgraph, run it with device buffers, compare with the oracle."""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import graph_eval, oracle as ora
+from strata_host import BF16, F32, I32, W4G32, Device, GraphBuilder, Op, StrataError, w8pc
+from strata_host.blocks import BLOCK_512, LLAMA_7B, LLAMA_70B, decoder_graph
+from tests.helpers import TOL_BF16, TOL_F32, assert_close, seeded_graph_inputs, to_device_bytes
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_kat.json")
+
+
+def run_graph(plugin, graph, host_vals, every_value=False):
+    """Upload every input as a device-resident buffer, run, return outputs."""
+    arena = {}
+    bufs = []
+    for i, v in enumerate(graph.values):
+        if v.producer is None and i in host_vals:
+            b = plugin.upload(v.dtype, v.dims, to_device_bytes(v, host_vals[i]))
+            bufs.append(b)
+            arena[i] = Device(b)
+    exe = plugin.compile(graph)
+    assert exe is not None, "the plugin declined a hot-path graph"
+    try:
+        exe.run(arena, every_value=every_value)
+        out = {o: arena[o] for o in graph.outputs}
+        caches = {i: bytes(arena[i].buffer.read()) for i, v in enumerate(graph.values)
+                  if v.name.endswith("cache") and i in arena}
+    finally:
+        for b in bufs:
+            b.release()
+        exe.free()
+    return out, caches
+
+
+def as_f32(v, arr):
+    if v.dtype == BF16:
+        return ora.from_bf16(np.asarray(arr).view(np.uint16))
+    return np.asarray(arr)
+
+
+@pytest.mark.parametrize("case", json.load(open(GOLDEN)), ids=lambda c: c["id"])
+def test_reference_known_answers_through_the_plugin(cuda, plugin, case):
+    """kernels.rs / end_to_end.rs golden values, run as one-node f32 graphs."""
+    b = GraphBuilder(case["id"])
+    op = case["op"]
+    host = {}
+    arr = lambda k: np.array(case[k], np.float32)
+    if op in ("add", "matmul"):
+        a, c = arr("a"), arr("b")
+        ia, ic = b.input(F32, a.shape, "a"), b.input(F32, c.shape, "b")
+        host = {ia: a, ic: c}
+        shape = tuple(case.get("out_shape") or (a.shape[0], c.shape[1]))
+        out = b.node(Op(op), [ia, ic], [(F32, shape)], {}, "op0")[0]
+    elif op in ("softmax", "gelu", "transpose", "expand"):
+        x = arr("x")
+        ix = b.input(F32, x.shape, "x")
+        host = {ix: x}
+        if op == "softmax":
+            out = b.node(Op("softmax", axis=-1), [ix], [(F32, x.shape)], {}, "op0")[0]
+        elif op == "gelu":
+            out = b.node(Op("gelu"), [ix], [(F32, x.shape)], {}, "op0")[0]
+        elif op == "transpose":
+            out = b.node(Op("transpose", permutation=(1, 0)), [ix], [(F32, x.shape[::-1])], {}, "op0")[0]
+        else:
+            shape = tuple(case["out_shape"])
+            out = b.node(Op("expand", shape=shape), [ix], [(F32, shape)], {}, "op0")[0]
+    elif op == "layer_norm":
+        x, g, be = arr("x"), arr("gamma"), arr("beta")
+        ix, ig, ib = b.input(F32, x.shape, "x"), b.input(F32, g.shape, "gamma"), b.input(F32, be.shape, "beta")
+        host = {ix: x, ig: g, ib: be}
+        out = b.node(Op("layer_norm", gamma=ig, beta=ib, eps=case["eps"]), [ix], [(F32, x.shape)], {}, "ln0")[0]
+    elif op == "linear":
+        x, w = arr("x"), arr("w")
+        ix, iw = b.input(F32, x.shape, "x"), b.input(F32, w.shape, "w")
+        host = {ix: x, iw: w}
+        ibias = None
+        if case["bias"] is not None:
+            ibias = b.input(F32, (w.shape[0],), "b")
+            host[ibias] = arr("bias")
+        out = b.node(Op("linear", weight=iw, bias=ibias), [ix], [(F32, (x.shape[0], w.shape[0]))], {}, "fc0")[0]
+    elif op == "gelu_mul":
+        x = arr("x")
+        ix = b.input(F32, x.shape, "x")
+        host = {ix: x}
+        g = b.node(Op("gelu"), [ix], [(F32, x.shape)], {}, "gelu0")[0]
+        out = b.node(Op("mul"), [g, ix], [(F32, x.shape)], {}, "mul0")[0]
+    else:
+        raise AssertionError(op)
+    b.output(out)
+    g = b.build()
+    res, _ = run_graph(plugin, g, host, every_value=True)
+    got = np.asarray(res[out]).ravel()
+    if op == "gelu_mul":
+        for v, w, t in zip(got[:2], case["want_first"], case["tol"]):
+            assert abs(v - w) < t
+    else:
+        assert np.all(np.abs(got - np.array(case["want"], np.float32)) <= max(case["tol"], 1e-6)), got
+
+
+def test_f32_llama_block_matches_oracle(cuda, plugin):
+    """The single f32 decoder block: hidden 512, 8 x 64 MHA, FFN 1408, seq 128."""
+    S = 128
+    g, hd = decoder_graph(BLOCK_512, batch=1, seq=S, max_len=S, fmt="f32", embed=False, head="none")
+    host = seeded_graph_inputs(g)
+    host[hd.pos] = np.arange(S, dtype=np.int32)
+    res, _ = run_graph(plugin, g, host)
+    want = graph_eval.evaluate(g, dict(host))[hd.out]
+    assert_close(res[hd.out], want, TOL_F32, "f32 block")
+
+
+@pytest.mark.parametrize("fmt", ["w4g32", "w8pc"])
+@pytest.mark.parametrize("m", [1, 16, 128])
+def test_quantized_linear_node(cuda, plugin, fmt, m):
+    k = n = 4096
+    b = GraphBuilder("qlin")
+    ix = b.input(BF16, (m, k), "x")
+    if fmt == "w4g32":
+        iw, is_ = b.input(W4G32, (n, k // 2), "w"), b.input(BF16, (n, k // 32), "s")
+    else:
+        iw, is_ = b.input(w8pc(k), (n, k), "w"), b.input(F32, (n,), "s")
+    out = b.node(Op.custom(f"fused::linear_{fmt}"), [ix, iw, is_], [(BF16, (m, n))], {}, "lin")[0]
+    b.output(out)
+    g = b.build()
+    host = seeded_graph_inputs(g)
+    host[ix] = ora.round_bf16(ora.normal(0, (m, k)))
+    res, _ = run_graph(plugin, g, host)
+    want = graph_eval.evaluate(g, dict(host))[out]
+    assert_close(as_f32(g.values[out], res[out]), want, TOL_BF16, f"{fmt} m={m}")
+
+
+def _decode_case(plugin, shape, batch, layers, max_len, fill, tp_world=1, head="logits"):
+    g, hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt="w4g32", layers=layers,
+                          embed=shape.vocab > 0, head=head if shape.vocab else "none",
+                          tp_world=tp_world)
+    host = seeded_graph_inputs(g, cache_fill=fill)
+    if shape.vocab:
+        host[hd.tokens] = ora.uniform_i32(2, batch, 0, shape.vocab)
+    else:
+        host[hd.tokens] = ora.round_bf16(ora.normal(0, (batch, shape.hidden)))
+    host[hd.pos] = np.array([fill - i for i in range(batch)], np.int32)
+    res, caches = run_graph(plugin, g, host)
+    ref = graph_eval.evaluate(g, {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in host.items()})
+    return g, hd, res, caches, ref
+
+
+@pytest.mark.parametrize("batch", [1, 8])
+def test_llama7b_shape_decode_two_layers(cuda, plugin, batch):
+    """7B-shape decode (int4 g32, KV 2048 prefilled) at reduced depth: 2 layers."""
+    g, hd, res, caches, ref = _decode_case(plugin, LLAMA_7B, batch, 2, 2112, 2048)
+    assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, "7B logits")
+    for i, raw in caches.items():  # the appended k/v rows match the oracle's
+        got = ora.from_bf16(np.frombuffer(raw, np.uint16).reshape(g.values[i].dims))
+        assert_close(got, ref[i], TOL_BF16, g.values[i].name)
+
+
+def test_llama7b_shape_argmax_is_exact_on_device_logits(cuda, plugin):
+    g, hd = decoder_graph(LLAMA_7B, batch=4, seq=1, max_len=2112, fmt="w4g32", layers=1, head="argmax")
+    logits_id = g.nodes[-1].inputs[0]
+    g.outputs.append(logits_id)
+    host = seeded_graph_inputs(g, cache_fill=2048)
+    host[hd.tokens] = ora.uniform_i32(2, 4, 0, LLAMA_7B.vocab)
+    host[hd.pos] = np.full(4, 2048, np.int32)
+    res, _ = run_graph(plugin, g, host)
+    logits = as_f32(g.values[logits_id], res[logits_id])
+    assert np.array_equal(np.asarray(res[hd.out]), ora.argmax(logits))
+    ref = graph_eval.evaluate(g, host)
+    assert_close(logits, ref[logits_id], TOL_BF16, "lm_head logits")
+
+
+def test_llama70b_gqa_shard_decode(cuda, plugin):
+    """70B-shape GQA (64 q / 8 kv heads), one tensor-parallel shard of 8, KV 4096."""
+    g, hd, res, caches, ref = _decode_case(plugin, LLAMA_70B, 2, 1, 4160, 4096, tp_world=8, head="none")
+    assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, "70B shard hidden")
+
+
+def test_cuda_graph_replay_is_deterministic_and_counted(cuda, plugin):
+    g, hd = decoder_graph(LLAMA_7B, batch=2, seq=1, max_len=256, fmt="w4g32", layers=1, head="argmax")
+    host = seeded_graph_inputs(g, cache_fill=100)
+    host[hd.tokens] = ora.uniform_i32(2, 2, 0, LLAMA_7B.vocab)
+    host[hd.pos] = np.full(2, 100, np.int32)
+    arena, bufs = {}, []
+    for i, v in enumerate(g.values):
+        if v.producer is None:
+            b = plugin.upload(v.dtype, v.dims, to_device_bytes(v, host[i]))
+            bufs.append(b)
+            arena[i] = Device(b)
+    exe = plugin.compile(g)
+    bound = exe.bind(arena)
+    outs = []
+    for _ in range(4):  # eager, capture, replay, replay
+        before = plugin.launch_count()
+        bound.run()
+        assert plugin.launch_count() > before
+        outs.append(bound.outputs[hd.out].read())
+    assert all(o == outs[0] for o in outs)
+    bound.release()
+    for b in bufs:
+        b.release()
+    exe.free()
+
+
+def test_bad_token_id_is_an_invalid_argument_not_a_fault(cuda, plugin):
+    b = GraphBuilder("emb")
+    ids = b.input(I32, (3,), "ids")
+    tab = b.input(BF16, (10, 16), "table")
+    out = b.node(Op.custom("fused::embed"), [ids, tab], [(BF16, (3, 16))], {}, "embed")[0]
+    b.output(out)
+    g = b.build()
+    with pytest.raises(StrataError) as e:
+        run_graph(plugin, g, {ids: np.array([1, 10, 2], np.int32), tab: np.zeros((10, 16), np.float32)})
+    assert e.value.code == -3 and "embedding table" in str(e.value)
+    # the context stays usable
+    res, _ = run_graph(plugin, g, {ids: np.array([1, 9, 2], np.int32), tab: np.ones((10, 16), np.float32)})
+    assert np.all(as_f32(g.values[out], res[out]) == 1.0)
+
+
+def test_device_quantize_node_is_bit_exact(cuda, plugin):
+    b = GraphBuilder("quant")
+    w = b.input(F32, (64, 256), "w")
+    c, s = b.node(Op.custom("fused::quantize_w4g32"), [w], [(W4G32, (64, 128)), (BF16, (64, 8))], {}, "q")
+    b.output(c)
+    b.output(s)
+    g = b.build()
+    wv = ora.normal(1, (64, 256), std=0.02)
+    res, _ = run_graph(plugin, g, {w: wv})
+    want_c, want_s = ora.quant_w4g32(wv)
+    assert np.frombuffer(res[c], np.uint8).tobytes() == want_c.tobytes()
+    assert np.array_equal(np.asarray(res[s]).view(np.uint16).ravel(), want_s.ravel())
