@@ -1,0 +1,451 @@
+"""Decode throughput of a Llama-7B-shape int4 (group-32) stack on B200.
+
+One step = one decode token for every sequence of the batch through all 32
+layers plus the int4 lm_head and argmax, with a 2048-entry KV cache
+prefilled, run through the plugin ABI (libstrata_b200.so, strata_plugin_v1).
+
+  value  device-timed tokens/s: CUDA events on the plugin's stream around K
+         CUDA-graph replays, inputs resident in HBM (max over ranks).
+  e2e    the same steps through the ABI with host buffers: each step writes
+         the token ids and positions from pinned host memory, runs, and reads
+         the next ids back (blocking ABI copies inside the timed region).
+
+N > 1 runs the same model tensor-parallel over N GPUs (q/k/v/gate/up column
+shards, o/down row shards, an NCCL all-reduce after o_proj and down_proj):
+total work is fixed, so scaling is "strong".
+
+``--impl reference`` times the CPU oracle (a restatement of the reference's
+CPU backend plus the decoder ops it lacks) on this host's cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "ferrite-strata_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+from strata_host.blocks import LLAMA_7B, decoder_graph  # noqa: E402
+
+METRIC = "decode tokens/s, 7B-shape int4 g32 stack"
+KV_FILL = 2048            # prefilled cache entries; the new token sits at position 2048
+MAX_LEN = 2112            # cache capacity per sequence
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+
+
+def step_bytes(shape, batch, tp=1):
+    """Algorithmic HBM bytes of one decode step (whole job): every int4
+    weight and bf16 scale once, the KV cache read over KV_FILL + 1 positions,
+    the new k/v rows written."""
+    D, H, G, d, F, V, L = (shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
+                           shape.vocab, shape.layers)
+    mats = [(H * d, D), (G * d, D), (G * d, D), (D, H * d), (F, D), (F, D), (D, F)]
+    w = sum(n * k // 2 + n * (k // 32) * 2 for n, k in mats) * L + V * D // 2 + V * (D // 32) * 2
+    kv = 2 * batch * G * (KV_FILL + 1) * d * 2 * L
+    return w + kv
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# the B200 arm
+# ---------------------------------------------------------------------------
+class Model:
+    """A 7B-shape int4 stack resident on one GPU (one tensor-parallel shard)."""
+
+    def __init__(self, plugin, torch, batch, rank, world, layers):
+        from strata_host import Device
+        self.plugin, self.torch, self.batch = plugin, torch, batch
+        g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=1, max_len=MAX_LEN, fmt="w4g32", layers=layers,
+                              head="argmax", tp_rank=rank, tp_world=world)
+        self.graph, self.hd = g, hd
+        lib = C.CDLL(plugin.path)
+        q4 = lib.strata_b200_quant_w4g32
+        q4.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
+        q4.restype = C.c_int32
+        dev = torch.device("cuda", torch.cuda.current_device())
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(1234 + rank)
+        self.tensors, self.arena, self.bufs = {}, {}, []
+        stream = torch.cuda.current_stream().cuda_stream
+        for i, v in enumerate(g.values):
+            if v.producer is not None:
+                continue
+            if v.dtype.element == 10:  # int4 codes: quantise N(0, 0.02) f32 on the device
+                n, kh = v.dims
+                w = torch.randn((n, kh * 2), generator=gen, device=dev, dtype=torch.float32) * 0.02
+                codes = torch.empty((n, kh), dtype=torch.uint8, device=dev)
+                scales = torch.empty((n, kh * 2 // 32), dtype=torch.int16, device=dev)
+                rc = q4(w.data_ptr(), n, kh * 2, codes.data_ptr(), scales.data_ptr(), stream)
+                assert rc == 0, rc
+                del w
+                self.tensors[i], self.tensors[i + 1] = codes, scales
+            elif i in self.tensors:
+                continue
+            elif v.dtype.element == 8:  # ids / positions
+                self.tensors[i] = torch.zeros(v.dims, dtype=torch.int32, device=dev)
+            elif v.name.endswith("cache"):
+                c = torch.zeros(v.dims, dtype=torch.bfloat16, device=dev)
+                c[:, :, :KV_FILL].normal_(generator=gen)
+                self.tensors[i] = c
+            elif "norm" in v.name:
+                self.tensors[i] = (1 + 0.02 * torch.randn(v.dims, generator=gen, device=dev)).to(torch.bfloat16)
+            else:
+                self.tensors[i] = torch.randn(v.dims, generator=gen, device=dev).to(torch.bfloat16)
+        torch.cuda.synchronize()
+        self.tensors[hd.pos].fill_(KV_FILL)
+        ids = torch.randint(0, LLAMA_7B.vocab, (batch,), generator=gen, device=dev, dtype=torch.int32)
+        self.tensors[hd.tokens].copy_(ids)
+        for i, t in self.tensors.items():
+            b = plugin.wrap(t.data_ptr(), t.numel() * t.element_size())
+            self.bufs.append(b)
+            self.arena[i] = Device(b)
+        self.exe = plugin.compile(g)
+        if self.exe is None:
+            raise RuntimeError("the plugin declined the decode step")
+        self.bound = self.exe.bind(self.arena)
+        self.ids_buf = self.arena[hd.tokens].buffer
+        self.pos_buf = self.arena[hd.pos].buffer
+        self.out_buf = self.bound.outputs[hd.out]
+
+    def close(self):
+        self.bound.release()
+        self.exe.free()
+        for b in self.bufs:
+            b.release()
+        self.tensors.clear()
+
+
+def dominant_kernel(plugin, torch, reps=32):
+    """Time the gate/up + SwiGLU int4 GEMV launch (the largest weight stream of
+    the step) over 32 distinct weight sets, on the plugin's stream."""
+    from strata_host import BF16, W4G32, Device, GraphBuilder, Op
+    D, F = LLAMA_7B.hidden, LLAMA_7B.ffn
+    b = GraphBuilder("gateup")
+    x = b.input(BF16, (1, D), "x")
+    outs = []
+    for i in range(reps):
+        wg, sg = b.input(W4G32, (F, D // 2), f"wg{i}"), b.input(BF16, (F, D // 32), f"sg{i}")
+        wu, su = b.input(W4G32, (F, D // 2), f"wu{i}"), b.input(BF16, (F, D // 32), f"su{i}")
+        g_ = b.node(Op.custom("fused::linear_w4g32"), [x, wg, sg], [(BF16, (1, F))], {}, f"g{i}")[0]
+        u_ = b.node(Op.custom("fused::linear_w4g32"), [x, wu, su], [(BF16, (1, F))], {}, f"u{i}")[0]
+        s_ = b.node(Op.custom("fused::swiglu"), [g_, u_], [(BF16, (1, F))], {}, f"s{i}")[0]
+        outs.append(s_)
+    for o in outs:
+        b.output(o)
+    g = b.build()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tensors, arena, bufs = [], {}, []
+    for i, v in enumerate(g.values):
+        if v.producer is None:
+            t = torch.randint(0, 255, v.dims, dtype=torch.uint8, device=dev) if v.dtype == W4G32 else \
+                (torch.rand(v.dims, device=dev) * 0.01).to(torch.bfloat16)
+            tensors.append(t)
+            bb = plugin.wrap(t.data_ptr(), t.numel() * t.element_size())
+            bufs.append(bb)
+            arena[i] = Device(bb)
+    exe = plugin.compile(g)
+    bound = exe.bind(arena)
+    stream = torch.cuda.ExternalStream(plugin.stream())
+    for _ in range(3):
+        bound.run_async()
+    plugin.synchronize()
+    iters = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(iters):
+        bound.run_async()
+    e1.record(stream)
+    plugin.synchronize()
+    per_launch_s = e0.elapsed_time(e1) / 1e3 / (iters * reps)
+    bytes_per_launch = 2 * (F * D // 2 + F * (D // 32) * 2) + D * 2 + F * 2
+    bound.release()
+    exe.free()
+    for bb in bufs:
+        bb.release()
+    return per_launch_s, bytes_per_launch
+
+
+def cpu_baseline_sample(batch, threads, budget_s=20.0):
+    """One 7B decode layer on the CPU oracle (all host threads), scaled to the
+    32-layer step plus the lm_head; returns tokens/s and what was timed."""
+    import numpy as np
+
+    from oracle import graph_eval, oracle as ora
+    from tests.helpers import seeded_graph_inputs
+    g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=1, max_len=KV_FILL + 1, fmt="w4g32", layers=1,
+                          embed=False, head="none")
+    host = seeded_graph_inputs(g, cache_fill=KV_FILL)
+    host[hd.tokens] = ora.round_bf16(ora.normal(0, (batch, LLAMA_7B.hidden)))
+    host[hd.pos] = np.full(batch, KV_FILL, np.int32)
+    # graph_eval is single-threaded; the linears and attention dominate, so
+    # time them with the threaded oracle kernels directly.
+    W = {name: host[vid] for name, vid in hd.layers[0].ids.items()}
+    x = host[hd.tokens]
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for key in ("q", "k", "v", "o", "g", "u", "d"):
+            k = W["w" + key].shape[1] * 2
+            xin = x if x.shape[1] == k else np.zeros((batch, k), np.float32)
+            ora.linear_w4g32(xin, W["w" + key], W["s" + key], threads=threads)
+        q = np.zeros((batch, LLAMA_7B.heads * LLAMA_7B.head_dim), np.float32)
+        ora.attention(q, W["k_cache"], W["v_cache"], np.arange(batch), host[hd.pos], LLAMA_7B.heads,
+                      LLAMA_7B.kv_heads, LLAMA_7B.head_dim, threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 > budget_s / 4 or reps >= 3:
+            break
+    layer_s = (time.perf_counter() - t0) / reps
+    lm = np.zeros((batch, LLAMA_7B.hidden), np.float32)
+    lw, ls = ora.quant_w4g32(ora.normal(99, (LLAMA_7B.vocab, LLAMA_7B.hidden), std=0.02))
+    t1 = time.perf_counter()
+    ora.linear_w4g32(lm, lw, ls, threads=threads)
+    head_s = time.perf_counter() - t1
+    step_s = layer_s * LLAMA_7B.layers + head_s
+    del graph_eval
+    return batch / step_s, (f"one decode layer (7 int4 linears + attention over {KV_FILL + 1} positions) "
+                            f"x{reps} at batch {batch}, scaled x{LLAMA_7B.layers} + the lm_head; "
+                            f"threaded oracle (C, OpenMP)")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np  # noqa: F401
+    from oracle import oracle as ora
+    threads = ora.max_threads()
+    values = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        tps, sample = cpu_baseline_sample(args.batch, threads, budget_s=8.0)
+        if i >= args.warmup:
+            values.append(tps)
+    v = statistics.median(values)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.batch / v * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights, f32 compute",
+            "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV)",
+            "config": {"workload": f"7B-shape int4 g32 decode, batch {args.batch}, KV 2048",
+                       "batch": args.batch, "kv_len": KV_FILL, "parallelism": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--layers", type=int, default=LLAMA_7B.layers)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+    from strata_host import Plugin
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    os.environ["STRATA_B200_DEVICE"] = str(local)
+    plugin = Plugin(os.path.join(PKG, "libstrata_b200.so"))
+    if world > 1:
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(plugin.tp_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        plugin.tp_init(rank, world, bytes(uid.cpu().numpy().tobytes()))
+
+    model = Model(plugin, torch, args.batch, rank, world, args.layers)
+    stream = torch.cuda.ExternalStream(plugin.stream())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        plugin.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed steps (inputs resident, CUDA-graph replay) -------------
+    for _ in range(args.warmup):
+        model.bound.run_async()
+    barrier()
+    launches0 = plugin.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.bound.run_async()
+        e1.record(stream)
+        barrier()
+    launches = plugin.launch_count() - launches0
+    dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    ms_step = dev_s / args.steps * 1e3
+    tokens = args.batch * args.steps
+    value = tokens / dev_s
+
+    # ---- end to end through the ABI with host buffers ------------------------
+    ids_h = torch.zeros(args.batch, dtype=torch.int32).pin_memory()
+    pos_h = torch.full((args.batch,), KV_FILL, dtype=torch.int32).pin_memory()
+    out_h = torch.zeros(args.batch, dtype=torch.int32).pin_memory()
+    nb = args.batch * 4
+
+    def e2e_step():
+        model.ids_buf.write_ptr(ids_h.data_ptr(), nb)
+        model.pos_buf.write_ptr(pos_h.data_ptr(), nb)
+        model.bound.run()
+        model.out_buf.read_into(out_h.data_ptr(), nb)
+        ids_h.copy_(out_h)  # feed the predicted ids back as the next tokens
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    t_wall = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    f1.record(stream)
+    barrier()
+    wall = time.perf_counter() - t_wall
+    e2e_s = max_over_ranks(max(f0.elapsed_time(f1) / 1e3, wall))
+    e2e = tokens / e2e_s
+
+    # ---- roofline of the dominant kernel and of the whole step ----------------
+    peak, peak_kind = load_peaks()
+    k_s, k_bytes = dominant_kernel(plugin, torch)
+    k_gbs = k_bytes / k_s / 1e9
+    sb = step_bytes(LLAMA_7B, args.batch) * args.layers // LLAMA_7B.layers
+    step_gbs = sb / (ms_step / 1e3) / 1e9 / world
+    clock = clocks.summary()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as ora
+        tps, sample = cpu_baseline_sample(args.batch, ora.max_threads())
+        cpu = {"value": tps, "unit": "tokens/s", "cores": ora.max_threads(), "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights (g32, bf16 scales), bf16 activations, f32 accumulate",
+            "data": "synthetic: device-generated N(0,0.02) weights quantised by the plugin, N(0,1) bf16 KV",
+            "config": {"workload": f"7B-shape int4 g32 decode stack ({args.layers} layers + int4 lm_head + argmax), "
+                                   f"batch {args.batch}, KV cache 2048 prefilled",
+                       "batch": args.batch, "kv_len": KV_FILL, "layers": args.layers,
+                       "parallelism": f"tp{world}",
+                       "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB streamed per step"},
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nb, "d2h_bytes_per_step": nb},
+            "roofline": {"bound": "hbm", "kernel": "w4g32 gate/up GEMV + SwiGLU epilogue, M=1, N=2x11008, K=4096",
+                         "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
+                         "peak_kind": peak_kind, "traffic": None,
+                         "bytes_per_launch": k_bytes, "us_per_launch": k_s * 1e6},
+            "step_roofline": {"bytes_per_step": sb, "achieved_gbs_per_gpu": step_gbs, "frac": step_gbs / peak,
+                              "frac_of_8tbs": step_gbs / 8000.0},
+            "gpu_launches": launches,
+            "clocks": clock,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    model.close()
+    plugin.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
