@@ -1,9 +1,20 @@
 // Kernel-level C entry points declared in include/strata_b200.h.
 #include "../../include/strata_b200.h"
 #include "k_elem.cuh"
+#include "k_gemv_mma.cuh"
+
+#include <cstdlib>
 
 namespace sb {
 std::atomic<uint64_t> g_launches{0};
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STRATA_B200_PDL");
+    return !(v && *v == '0');
+  }();
+  return on;
+}
 }
 
 using namespace sb;
@@ -45,6 +56,11 @@ static int32_t linear_common(WFormat fmt, const uint16_t* x, int64_t m, int64_t 
   b.epi = residual ? Epilogue::Residual : Epilogue::None;
   b.njobs = 1;
   b.jobs[0] = LinearJob{w, s, int(n), y, int(n), residual, int(n)};
+  GemvMmaArgs ga{};
+  ga.lb = b;
+  ga.mode = GemvMode::Plain;
+  ga.pdl = pdl_enabled();
+  if (gemv_mma_supported(ga)) return launch_gemv_mma(ga, S(stream));
   return launch_linear(b, S(stream));
 }
 
@@ -79,8 +95,8 @@ uint64_t strata_b200_attention_decode_scratch_bytes(int64_t batch, int64_t heads
                                                     int64_t head_dim, int64_t max_len) {
   // The split count depends on the kv-head count only through the grid size;
   // size for the worst case (one kv head per query head).
-  return attention_scratch_bytes(batch, heads, heads, head_dim, max_len) +
-         attention_scratch_bytes(batch, heads, 1, head_dim, max_len);
+  const uint64_t splits64 = uint64_t((max_len + 63) / 64);  // the most splits any kv-head count uses
+  return uint64_t(batch) * heads * splits64 * (head_dim + 2) * sizeof(float);
 }
 
 int32_t strata_b200_attention_decode_bf16(const uint16_t* q, const uint16_t* k_new,
@@ -92,9 +108,8 @@ int32_t strata_b200_attention_decode_bf16(const uint16_t* q, const uint16_t* k_n
   int rc = launch_kv_append<uint16_t>(k_new, v_new, k_cache, v_cache, pos, batch, 1, kv_heads,
                                       head_dim, max_len, nullptr, S(stream));
   if (rc) return rc;
-  return launch_attention<uint16_t>(q, k_cache, v_cache, pos, batch, 1, heads, kv_heads,
-                                    head_dim, max_len, static_cast<float*>(scratch), out, nullptr,
-                                    S(stream));
+  return launch_attention_v2(q, k_cache, v_cache, pos, batch, 1, heads, kv_heads, head_dim, max_len,
+                             true, static_cast<float*>(scratch), out, nullptr, S(stream));
 }
 
 int32_t strata_b200_embed_bf16(const int32_t* ids, int64_t rows, const uint16_t* table,

@@ -19,6 +19,10 @@ constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
 
 inline int ceil_div(int64_t a, int64_t b) { return int((a + b - 1) / b); }
 
+#if !defined(__CUDACC__)
+bool pdl_enabled();
+#endif
+
 #if defined(__CUDACC__)
 
 __device__ __forceinline__ float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
@@ -59,6 +63,40 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
 
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// independent prologue now, then wait until every kernel this one depends on
+// has completed and its writes are visible.  Both are no-ops for a launch
+// without the programmatic attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+bool pdl_enabled();
+
+// Launch with the programmatic-stream-serialization attribute (when enabled).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 #endif  // __CUDACC__

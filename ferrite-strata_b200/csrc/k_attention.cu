@@ -70,6 +70,8 @@ __global__ void kv_append_kernel(const T* __restrict__ k_new, const T* __restric
                                  T* __restrict__ k_cache, T* __restrict__ v_cache,
                                  const int32_t* __restrict__ pos, int rows, int tokens_per_seq,
                                  int kv_heads, int head_dim, int max_len, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int p = pos[row];
   if (p < 0 || p >= max_len) {
@@ -95,11 +97,15 @@ __global__ void __launch_bounds__(kThreads)
                 const int32_t* __restrict__ pos, int tokens_per_seq, int heads, int kv_heads,
                 int max_len, int splits, float scale, float* __restrict__ partial,
                 T* __restrict__ out, int* err) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int kPairs = D / 2;              // d pairs per row
   constexpr int kPhases = kThreads / kPairs;  // position phases in the PV loop
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int G = heads / kv_heads;
   const int tid = threadIdx.x;
+  pdl_trigger();
+  pdl_wait();
 
   __shared__ float qs[kMaxGroup][D];
   __shared__ float ps[kMaxGroup][kThreads];
@@ -237,6 +243,8 @@ __global__ void __launch_bounds__(kThreads)
 template <typename T, int D>
 __global__ void attn_merge_kernel(const float* __restrict__ partial, int heads, int splits,
                                   T* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int rh = blockIdx.x;  // row * heads + h
   const float* pp = partial + int64_t(rh) * splits * (D + 2);
   float mx = -INFINITY;
@@ -256,6 +264,256 @@ __global__ void attn_merge_kernel(const float* __restrict__ partial, int heads, 
   }
 }
 
+// ---------------------------------------------------------------------------
+// bf16 decode attention, version 2: one block per (chunk of CH positions, kv
+// head, query row).  Cache rows below the row's position never change during
+// this step, so they are copied to shared memory with cp.async *before*
+// griddepcontrol.wait -- under programmatic dependent launch the KV stream
+// overlaps the previous kernel (the q/k/v projection).  The row at the
+// position itself (just appended by that kernel) and q are read after the
+// wait.  The block computes the G query heads' scores for its chunk from the
+// staged k rows, a local softmax, and the unnormalised PV sum, and writes
+// (max, sum, acc) partials for attn_merge_kernel.
+// ---------------------------------------------------------------------------
+template <int D, int CH>
+struct AttnV2Smem {
+  static constexpr int kRowK = D * 2 + 16;  // padded k row (bytes): conflict-free 16-byte reads
+  static constexpr int kRowV = D * 2;
+  static constexpr size_t bytes(int G) {
+    return size_t(CH) * kRowK + size_t(CH) * kRowV + size_t(G) * D * 4 + size_t(G) * CH * 4 +
+           size_t(kThreads / (D / 2)) * G * D * 4 + 2 * size_t(G) * 4;
+  }
+};
+
+template <int D, int CH>
+__global__ void __launch_bounds__(kThreads)
+    attn_v2_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
+                   const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos,
+                   int tokens_per_seq, int heads, int kv_heads, int max_len, int splits,
+                   float scale, int pos_external, float* __restrict__ partial,
+                   uint16_t* __restrict__ out, int* err) {
+  pdl_trigger();
+  pdl_wait();
+  using L = AttnV2Smem<D, CH>;
+  constexpr int kPairs = D / 2;
+  constexpr int kPhases = kThreads / kPairs;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+  const int G = heads / kv_heads;
+  const int tid = threadIdx.x;
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + CH * L::kRowK;
+  float* sQ = reinterpret_cast<float*>(sV + CH * L::kRowV);  // [G][D]
+  float* sS = sQ + G * D;                                    // [G][CH]
+  float* sA = sS + G * CH;                                   // [kPhases][G][D]
+  float* sM = sA + kPhases * G * D;                          // [G] max, [G] sum
+
+  pdl_trigger();
+  const int seq = row / tokens_per_seq;
+  const uint8_t* kb = reinterpret_cast<const uint8_t*>(kc + (int64_t(seq) * kv_heads + kvh) * int64_t(max_len) * D);
+  const uint8_t* vb = reinterpret_cast<const uint8_t*>(vc + (int64_t(seq) * kv_heads + kvh) * int64_t(max_len) * D);
+  const int t_begin = split * CH;
+
+  auto stage = [&](int r0, int r1) {  // rows [r0, r1) of this chunk, chunk-relative
+    const int n = (r1 - r0) * (D / 8);
+    for (int c = tid; c < 2 * n; c += kThreads) {
+      const bool isv = c >= n;
+      const int cc = isv ? c - n : c;
+      const int r = r0 + cc / (D / 8), off = (cc % (D / 8)) * 16;
+      const int64_t src = int64_t(t_begin + r) * D * 2 + off;
+      if (isv) cp_async16(sV + r * L::kRowV + off, vb + src);
+      else cp_async16(sK + r * L::kRowK + off, kb + src);
+    }
+  };
+
+  int pre = 0;  // rows staged before the wait
+  int p_early = -1;
+  if (pos_external) {
+    p_early = pos[row];
+    if (p_early >= 0 && p_early < max_len) {
+      pre = min(CH, max(0, p_early - t_begin));
+      stage(0, pre);
+    }
+  }
+  pdl_wait();
+  const int p = pos_external ? p_early : pos[row];
+  const bool bad = p < 0 || p >= max_len;
+  if (bad && tid == 0 && err) atomicExch(err, 2);
+  const int len = bad ? 0 : p + 1;
+  const int n_t = max(0, min(CH, len - t_begin));
+  if (n_t > pre) stage(pre, n_t);
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    sQ[i] = bf2f(q[int64_t(row) * heads * D + int64_t(kvh * G + g) * D + d]);
+  }
+  cp_async_commit_wait_all();
+  __syncthreads();
+
+  // Scores: position t = tid % CH, heads strided by kThreads / CH.
+  for (int item = tid; item < CH * G; item += kThreads) {
+    const int t = item % CH, g = item / CH;
+    float acc = 0.0f;
+    if (t < n_t) {
+      const uint8_t* kr = sK + t * L::kRowK;
+      const float* qg = sQ + g * D;
+#pragma unroll 4
+      for (int d = 0; d < D; d += 8) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(kr + d * 2);
+        acc = fmaf(qg[d + 0], bf_lo(kv.x), acc);
+        acc = fmaf(qg[d + 1], bf_hi(kv.x), acc);
+        acc = fmaf(qg[d + 2], bf_lo(kv.y), acc);
+        acc = fmaf(qg[d + 3], bf_hi(kv.y), acc);
+        acc = fmaf(qg[d + 4], bf_lo(kv.z), acc);
+        acc = fmaf(qg[d + 5], bf_hi(kv.z), acc);
+        acc = fmaf(qg[d + 6], bf_lo(kv.w), acc);
+        acc = fmaf(qg[d + 7], bf_hi(kv.w), acc);
+      }
+      acc *= scale;
+    }
+    sS[g * CH + t] = t < n_t ? acc : -INFINITY;
+  }
+  __syncthreads();
+  // Softmax statistics: warp w handles heads w, w + 4, ...
+  {
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int g = warp; g < G; g += kThreads / 32) {
+      float mx = -INFINITY;
+      for (int t = lane; t < CH; t += 32) mx = fmaxf(mx, sS[g * CH + t]);
+      mx = warp_max(mx);
+      float sum = 0.0f;
+      for (int t = lane; t < CH; t += 32) {
+        const float e = t < n_t ? expf(sS[g * CH + t] - mx) : 0.0f;
+        sS[g * CH + t] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        sM[g] = mx;
+        sM[G + g] = sum;
+      }
+    }
+  }
+  __syncthreads();
+  // PV: thread owns a d pair and one position phase; each v row read once.
+  {
+    const int pair = tid % kPairs, phase = tid / kPairs;
+    float a[kMaxGroup][2];
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) a[g][0] = a[g][1] = 0.0f;
+    for (int t = phase; t < n_t; t += kPhases) {
+      const uint32_t vv = *reinterpret_cast<const uint32_t*>(sV + t * L::kRowV + pair * 4);
+      const float v0 = bf_lo(vv), v1 = bf_hi(vv);
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g) {
+        if (g < G) {
+          const float pg = sS[g * CH + t];
+          a[g][0] = fmaf(pg, v0, a[g][0]);
+          a[g][1] = fmaf(pg, v1, a[g][1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+      if (g < G) {
+        sA[(phase * G + g) * D + 2 * pair] = a[g][0];
+        sA[(phase * G + g) * D + 2 * pair + 1] = a[g][1];
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    float acc = 0.0f;
+#pragma unroll
+    for (int ph = 0; ph < kPhases; ++ph) acc += sA[(ph * G + g) * D + d];
+    const int h = kvh * G + g;
+    const float mx = n_t > 0 ? sM[g] : -INFINITY, l = n_t > 0 ? sM[G + g] : 0.0f;
+    if (splits == 1) {
+      out[int64_t(row) * heads * D + int64_t(h) * D + d] = f2bf(l > 0.0f ? acc / l : 0.0f);
+    } else {
+      float* pp = partial + ((int64_t(row) * heads + h) * splits + split) * (D + 2);
+      pp[2 + d] = acc;
+      if (d == 0) {
+        pp[0] = mx;
+        pp[1] = l;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int attention_chunk(int64_t rows, int64_t kv_heads) {
+  // Small grids (one or a few sequences) use shorter chunks for more blocks.
+  return rows * kv_heads <= 64 ? 64 : 128;
+}
+
+int attention_v2_splits(int64_t rows, int64_t kv_heads, int64_t max_len) {
+  const int ch = attention_chunk(rows, kv_heads);
+  return int((max_len + ch - 1) / ch);
+}
+
+uint64_t attention_v2_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                    int64_t max_len) {
+  const int s = attention_v2_splits(rows, kv_heads, max_len);
+  if (s == 1) return 0;
+  return uint64_t(rows) * heads * s * (head_dim + 2) * sizeof(float);
+}
+
+template <int D, int CH>
+static int launch_v2(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos,
+                     int64_t rows, int64_t tps, int64_t heads, int64_t kv_heads, int64_t max_len,
+                     int splits, bool pos_external, float* scratch, uint16_t* out, int* err,
+                     cudaStream_t st) {
+  const int G = int(heads / kv_heads);
+  const size_t smem = AttnV2Smem<D, CH>::bytes(G);
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(attn_v2_kernel<D, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             int(AttnV2Smem<D, CH>::bytes(kMaxGroup))) != cudaSuccess)
+      return SB_INTERNAL;
+    configured = true;
+  }
+  const float scale = 1.0f / sqrtf(float(D));
+  const dim3 grid(splits, unsigned(kv_heads), unsigned(rows));
+  if (launch_pdl(attn_v2_kernel<D, CH>, grid, dim3(kThreads), smem, st, q, kc, vc, pos, int(tps), int(heads),
+                 int(kv_heads), int(max_len), splits, scale, pos_external ? 1 : 0, scratch, out, err) !=
+      cudaSuccess)
+    return SB_INTERNAL;
+  count_launch();
+  if (splits > 1) {
+    const unsigned nb = unsigned(rows * heads);
+    if (launch_pdl(attn_merge_kernel<uint16_t, D>, dim3(nb), dim3(D), 0, st, (const float*)scratch, int(heads),
+                   splits, out) != cudaSuccess)
+      return SB_INTERNAL;
+    count_launch();
+  }
+  return SB_OK;
+}
+
+int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                        const int32_t* pos, int64_t rows, int64_t tokens_per_seq, int64_t heads,
+                        int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
+                        float* scratch, uint16_t* out, int* err, cudaStream_t st) {
+  if (rows == 0) return SB_OK;
+  if (kv_heads <= 0 || heads % kv_heads || heads / kv_heads > kMaxGroup) return SB_INVALID_ARGUMENT;
+  const int splits = attention_v2_splits(rows, kv_heads, max_len);
+  if (splits > 1 && scratch == nullptr) return SB_INVALID_ARGUMENT;
+  const int ch = attention_chunk(rows, kv_heads);
+  if (head_dim == 128)
+    return ch == 64 ? launch_v2<128, 64>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, max_len,
+                                         splits, pos_external, scratch, out, err, st)
+                    : launch_v2<128, 128>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads,
+                                          max_len, splits, pos_external, scratch, out, err, st);
+  if (head_dim == 64)
+    return ch == 64 ? launch_v2<64, 64>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, max_len,
+                                        splits, pos_external, scratch, out, err, st)
+                    : launch_v2<64, 128>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads,
+                                         max_len, splits, pos_external, scratch, out, err, st);
+  return SB_INVALID_ARGUMENT;
+}
+
+namespace {
 }  // namespace
 
 // Splits so that the grid covers about two waves of the 148 SMs, with at
@@ -281,7 +539,7 @@ int launch_kv_append(const T* k_new, const T* v_new, T* k_cache, T* v_cache, con
                      int64_t rows, int64_t tokens_per_seq, int64_t kv_heads, int64_t head_dim,
                      int64_t max_len, int* err, cudaStream_t st) {
   if (rows == 0) return SB_OK;
-  kv_append_kernel<T><<<unsigned(rows), 256, 0, st>>>(k_new, v_new, k_cache, v_cache, pos,
+  launch_pdl(kv_append_kernel<T>, dim3(unsigned(rows)), dim3(256), 0, st, k_new, v_new, k_cache, v_cache, pos,
                                                       int(rows), int(tokens_per_seq),
                                                       int(kv_heads), int(head_dim),
                                                       int(max_len), err);
@@ -303,11 +561,11 @@ int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32
   const float scale = 1.0f / sqrtf(float(head_dim));
   const dim3 grid(splits, unsigned(kv_heads), unsigned(rows));
   if (head_dim == 128) {
-    attn_kernel<T, 128><<<grid, kThreads, 0, st>>>(q, k_cache, v_cache, pos, int(tokens_per_seq),
+    launch_pdl(attn_kernel<T, 128>, dim3(grid), dim3(kThreads), 0, st, q, k_cache, v_cache, pos, int(tokens_per_seq),
                                                    int(heads), int(kv_heads), int(max_len),
                                                    splits, scale, scratch, out, err);
   } else {
-    attn_kernel<T, 64><<<grid, kThreads, 0, st>>>(q, k_cache, v_cache, pos, int(tokens_per_seq),
+    launch_pdl(attn_kernel<T, 64>, dim3(grid), dim3(kThreads), 0, st, q, k_cache, v_cache, pos, int(tokens_per_seq),
                                                   int(heads), int(kv_heads), int(max_len), splits,
                                                   scale, scratch, out, err);
   }
@@ -315,9 +573,9 @@ int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32
   if (splits > 1) {
     const unsigned nb = unsigned(rows * heads);
     if (head_dim == 128)
-      attn_merge_kernel<T, 128><<<nb, 128, 0, st>>>(scratch, int(heads), splits, out);
+      launch_pdl(attn_merge_kernel<T, 128>, dim3(nb), dim3(128), 0, st, scratch, int(heads), splits, out);
     else
-      attn_merge_kernel<T, 64><<<nb, 64, 0, st>>>(scratch, int(heads), splits, out);
+      launch_pdl(attn_merge_kernel<T, 64>, dim3(nb), dim3(64), 0, st, scratch, int(heads), splits, out);
     SB_LAUNCH_CHECK();
   }
   return SB_OK;

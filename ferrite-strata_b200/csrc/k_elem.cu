@@ -49,6 +49,8 @@ __device__ float block_max(float v, float* red) {
 template <typename T>
 __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g, int64_t cols,
                                 float eps, T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * cols;
@@ -67,6 +69,8 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g
 template <typename T>
 __global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__ pos, int64_t rows,
                             int heads, int head_dim, double theta, T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   const int half = head_dim / 2;
   const int64_t total = rows * heads * half;
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -87,6 +91,8 @@ __global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__
 template <typename T>
 __global__ void swiglu_kernel(const T* __restrict__ gate, const T* __restrict__ up, int64_t n,
                               T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += int64_t(gridDim.x) * blockDim.x) {
     const float gv = ld(gate, i);
@@ -98,6 +104,8 @@ __global__ void swiglu_kernel(const T* __restrict__ gate, const T* __restrict__ 
 template <typename T>
 __global__ void binary_kernel(int op, const T* __restrict__ a, const T* __restrict__ b,
                               T* __restrict__ out, BcastShape sh) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < sh.total;
        i += int64_t(gridDim.x) * blockDim.x) {
     int64_t rem = i, ia = 0, ib = 0;
@@ -124,6 +132,8 @@ __device__ __forceinline__ float erf_as(float x) {
 
 template <typename T>
 __global__ void unary_kernel(int op, const T* __restrict__ x, int64_t n, T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += int64_t(gridDim.x) * blockDim.x) {
     const float v = ld(x, i);
@@ -137,6 +147,8 @@ __global__ void unary_kernel(int op, const T* __restrict__ x, int64_t n, T* __re
 
 template <typename T>
 __global__ void softmax_kernel(const T* __restrict__ x, int64_t cols, T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * cols;
@@ -154,6 +166,8 @@ template <typename T>
 __global__ void layer_norm_kernel(const T* __restrict__ x, const T* __restrict__ gamma,
                                   const T* __restrict__ beta, int64_t cols, float eps,
                                   T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * cols;
@@ -174,6 +188,8 @@ __global__ void layer_norm_kernel(const T* __restrict__ x, const T* __restrict__
 template <typename T>
 __global__ void transpose2_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
                                   T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * cols;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
@@ -185,6 +201,8 @@ template <typename T>
 __global__ void slice_cols_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
                                   int64_t start, int64_t stride, int64_t out_cols,
                                   T* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < rows * out_cols;
        i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = i / out_cols, j = i % out_cols;
@@ -194,6 +212,8 @@ __global__ void slice_cols_kernel(const T* __restrict__ x, int64_t rows, int64_t
 
 template <typename T>
 __global__ void broadcast_kernel(const T* __restrict__ a, T* __restrict__ out, BcastShape sh) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < sh.total;
        i += int64_t(gridDim.x) * blockDim.x) {
     int64_t rem = i, ia = 0;
@@ -209,6 +229,8 @@ __global__ void broadcast_kernel(const T* __restrict__ a, T* __restrict__ out, B
 template <typename T>
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restrict__ table,
                              int64_t vocab, int64_t dim, T* __restrict__ out, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const int32_t id = ids[row];
   if (id < 0 || id >= vocab) {
@@ -223,6 +245,8 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const T* __restric
 // Lowest index among the maxima; NaN never wins; an all-NaN row gives 0.
 template <typename T>
 __global__ void argmax_kernel(const T* __restrict__ x, int64_t cols, int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float sv[32];
   __shared__ int32_t si[32];
   const int64_t row = blockIdx.x;
@@ -264,6 +288,8 @@ constexpr int kT = 32;
 __global__ void gemm_f32_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                 const float* __restrict__ bias, int64_t m, int64_t k, int64_t n,
                                 int64_t b_sk, int64_t b_sn, float* __restrict__ c) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float as[kT][kT + 1];
   __shared__ float bs[kT][kT + 1];
   const int tx = threadIdx.x % kT, ty = threadIdx.x / kT;  // 32 x 8 threads
@@ -292,6 +318,8 @@ __global__ void gemm_f32_kernel(const float* __restrict__ a, const float* __rest
 }
 
 __global__ void convert_kernel(int dir, const void* __restrict__ x, int64_t n, void* __restrict__ y) {
+  pdl_trigger();
+  pdl_wait();
   for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += int64_t(gridDim.x) * blockDim.x) {
     if (dir == 0)
@@ -320,7 +348,7 @@ template <typename T>
 int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float eps, T* y,
                     cudaStream_t st) {
   if (rows == 0 || cols == 0) return SB_OK;
-  rms_norm_kernel<T><<<unsigned(rows), row_threads(cols), 0, st>>>(x, g, cols, eps, y);
+  launch_pdl(rms_norm_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols)), 0, st, x, g, cols, eps, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -331,7 +359,7 @@ int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int
   if (head_dim % 2) return SB_INVALID_ARGUMENT;
   const int64_t n = rows * heads * (head_dim / 2);
   if (n == 0) return SB_OK;
-  rope_kernel<T><<<grid_for(n), 256, 0, st>>>(x, pos, rows, int(heads), int(head_dim), theta, y);
+  launch_pdl(rope_kernel<T>, dim3(grid_for(n)), dim3(256), 0, st, x, pos, rows, int(heads), int(head_dim), theta, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -339,7 +367,7 @@ int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int
 template <typename T>
 int launch_swiglu(const T* gate, const T* up, int64_t n, T* y, cudaStream_t st) {
   if (n == 0) return SB_OK;
-  swiglu_kernel<T><<<grid_for(n), 256, 0, st>>>(gate, up, n, y);
+  launch_pdl(swiglu_kernel<T>, dim3(grid_for(n)), dim3(256), 0, st, gate, up, n, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -347,7 +375,7 @@ int launch_swiglu(const T* gate, const T* up, int64_t n, T* y, cudaStream_t st) 
 template <typename T>
 int launch_binary(int op, const T* a, const T* b, T* out, const BcastShape& sh, cudaStream_t st) {
   if (sh.total == 0) return SB_OK;
-  binary_kernel<T><<<grid_for(sh.total), 256, 0, st>>>(op, a, b, out, sh);
+  launch_pdl(binary_kernel<T>, dim3(grid_for(sh.total)), dim3(256), 0, st, op, a, b, out, sh);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -355,7 +383,7 @@ int launch_binary(int op, const T* a, const T* b, T* out, const BcastShape& sh, 
 template <typename T>
 int launch_unary(int op, const T* x, int64_t n, T* y, cudaStream_t st) {
   if (n == 0) return SB_OK;
-  unary_kernel<T><<<grid_for(n), 256, 0, st>>>(op, x, n, y);
+  launch_pdl(unary_kernel<T>, dim3(grid_for(n)), dim3(256), 0, st, op, x, n, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -363,7 +391,7 @@ int launch_unary(int op, const T* x, int64_t n, T* y, cudaStream_t st) {
 template <typename T>
 int launch_softmax(const T* x, int64_t rows, int64_t cols, T* y, cudaStream_t st) {
   if (rows == 0 || cols == 0) return SB_OK;
-  softmax_kernel<T><<<unsigned(rows), row_threads(cols), 0, st>>>(x, cols, y);
+  launch_pdl(softmax_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols)), 0, st, x, cols, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -372,7 +400,7 @@ template <typename T>
 int launch_layer_norm(const T* x, const T* gamma, const T* beta, int64_t rows, int64_t cols,
                       float eps, T* y, cudaStream_t st) {
   if (rows == 0 || cols == 0) return SB_OK;
-  layer_norm_kernel<T><<<unsigned(rows), row_threads(cols), 0, st>>>(x, gamma, beta, cols, eps, y);
+  launch_pdl(layer_norm_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols)), 0, st, x, gamma, beta, cols, eps, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -380,7 +408,7 @@ int launch_layer_norm(const T* x, const T* gamma, const T* beta, int64_t rows, i
 template <typename T>
 int launch_transpose2(const T* x, int64_t rows, int64_t cols, T* y, cudaStream_t st) {
   if (rows * cols == 0) return SB_OK;
-  transpose2_kernel<T><<<grid_for(rows * cols), 256, 0, st>>>(x, rows, cols, y);
+  launch_pdl(transpose2_kernel<T>, dim3(grid_for(rows * cols)), dim3(256), 0, st, x, rows, cols, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -389,7 +417,7 @@ template <typename T>
 int launch_slice_cols(const T* x, int64_t rows, int64_t cols, int64_t start, int64_t stride,
                       int64_t out_cols, T* y, cudaStream_t st) {
   if (rows * out_cols == 0) return SB_OK;
-  slice_cols_kernel<T><<<grid_for(rows * out_cols), 256, 0, st>>>(x, rows, cols, start, stride,
+  launch_pdl(slice_cols_kernel<T>, dim3(grid_for(rows * out_cols)), dim3(256), 0, st, x, rows, cols, start, stride,
                                                                   out_cols, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
@@ -398,7 +426,7 @@ int launch_slice_cols(const T* x, int64_t rows, int64_t cols, int64_t start, int
 template <typename T>
 int launch_broadcast(const T* a, T* out, const BcastShape& sh, cudaStream_t st) {
   if (sh.total == 0) return SB_OK;
-  broadcast_kernel<T><<<grid_for(sh.total), 256, 0, st>>>(a, out, sh);
+  launch_pdl(broadcast_kernel<T>, dim3(grid_for(sh.total)), dim3(256), 0, st, a, out, sh);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -407,7 +435,7 @@ template <typename T>
 int launch_embed(const int32_t* ids, int64_t rows, const T* table, int64_t vocab, int64_t dim,
                  T* out, int* err, cudaStream_t st) {
   if (rows == 0 || dim == 0) return SB_OK;
-  embed_kernel<T><<<unsigned(rows), 256, 0, st>>>(ids, table, vocab, dim, out, err);
+  launch_pdl(embed_kernel<T>, dim3(unsigned(rows)), dim3(256), 0, st, ids, table, vocab, dim, out, err);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -415,7 +443,7 @@ int launch_embed(const int32_t* ids, int64_t rows, const T* table, int64_t vocab
 template <typename T>
 int launch_argmax(const T* x, int64_t rows, int64_t cols, int32_t* out, cudaStream_t st) {
   if (rows == 0) return SB_OK;
-  argmax_kernel<T><<<unsigned(rows), 512, 0, st>>>(x, cols, out);
+  launch_pdl(argmax_kernel<T>, dim3(unsigned(rows)), dim3(512), 0, st, x, cols, out);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -426,14 +454,14 @@ int launch_gemm_f32(const float* a, const float* b, const float* bias, int64_t m
   const dim3 grid(unsigned((n + kT - 1) / kT), unsigned((m + kT - 1) / kT));
   // b_is_nk: B stored [n, k] (Linear weight); else [k, n] (MatMul).
   const int64_t sk = b_is_nk ? 1 : n, sn = b_is_nk ? k : 1;
-  gemm_f32_kernel<<<grid, 256, 0, st>>>(a, b, bias, m, k, n, sk, sn, c);
+  launch_pdl(gemm_f32_kernel, dim3(grid), dim3(256), 0, st, a, b, bias, m, k, n, sk, sn, c);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
 
 int launch_convert(int dir, const void* x, int64_t n, void* y, cudaStream_t st) {
   if (n == 0) return SB_OK;
-  convert_kernel<<<grid_for(n), 256, 0, st>>>(dir, x, n, y);
+  launch_pdl(convert_kernel, dim3(grid_for(n)), dim3(256), 0, st, dir, x, n, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }

@@ -67,6 +67,16 @@ int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32
                      int64_t head_dim, int64_t max_len, float* scratch, T* out, int* err,
                      cudaStream_t st);
 
+// bf16 decode/prefill attention with cache prefetch under programmatic launch.
+int attention_chunk(int64_t rows, int64_t kv_heads);
+int attention_v2_splits(int64_t rows, int64_t kv_heads, int64_t max_len);
+uint64_t attention_v2_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                    int64_t max_len);
+int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                        const int32_t* pos, int64_t rows, int64_t tokens_per_seq, int64_t heads,
+                        int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
+                        float* scratch, uint16_t* out, int* err, cudaStream_t st);
+
 // Quantisation (k_quant.cu).
 int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, uint16_t* scale,
                        cudaStream_t st);

@@ -124,6 +124,8 @@ constexpr int kUnroll = 4;
 template <WFormat F, int MT>
 __global__ void __launch_bounds__(kWarps * 32)
     gemv_kernel(const LinearBatch b, int units, int m0) {
+  pdl_trigger();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int unit = blockIdx.x * kWarps + warp;
   if (unit >= units) return;
@@ -232,17 +234,17 @@ int launch_fmt(const LinearBatch& b, cudaStream_t st) {
   for (int m0 = 0; m0 < b.m; m0 += 8) {
     const int left = b.m - m0;
     if (left >= 8) {
-      gemv_kernel<F, 8><<<blocks, kWarps * 32, 0, st>>>(b, units, m0);
+      launch_pdl(gemv_kernel<F, 8>, dim3(blocks), dim3(kWarps * 32), 0, st, b, units, m0);
     } else if (left > 2) {
-      gemv_kernel<F, 4><<<blocks, kWarps * 32, 0, st>>>(b, units, m0);
+      launch_pdl(gemv_kernel<F, 4>, dim3(blocks), dim3(kWarps * 32), 0, st, b, units, m0);
       if (left > 4) {
-        gemv_kernel<F, 4><<<blocks, kWarps * 32, 0, st>>>(b, units, m0 + 4);
+        launch_pdl(gemv_kernel<F, 4>, dim3(blocks), dim3(kWarps * 32), 0, st, b, units, m0 + 4);
         SB_LAUNCH_CHECK();
       }
     } else if (left == 2) {
-      gemv_kernel<F, 2><<<blocks, kWarps * 32, 0, st>>>(b, units, m0);
+      launch_pdl(gemv_kernel<F, 2>, dim3(blocks), dim3(kWarps * 32), 0, st, b, units, m0);
     } else {
-      gemv_kernel<F, 1><<<blocks, kWarps * 32, 0, st>>>(b, units, m0);
+      launch_pdl(gemv_kernel<F, 1>, dim3(blocks), dim3(kWarps * 32), 0, st, b, units, m0);
     }
     SB_LAUNCH_CHECK();
   }

@@ -12,6 +12,8 @@ namespace sb {
 
 __global__ void quant_w4g32_kernel(const float* __restrict__ w, int64_t n, int64_t k,
                                    uint8_t* __restrict__ packed, uint16_t* __restrict__ scale) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t groups = k / 32;
   const int64_t gid = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (gid >= n * groups) return;
@@ -45,6 +47,8 @@ __global__ void quant_w4g32_kernel(const float* __restrict__ w, int64_t n, int64
 // One block per row: block-wide amax, then codes.
 __global__ void quant_w8pc_kernel(const float* __restrict__ w, int64_t n, int64_t k,
                                   int8_t* __restrict__ q, float* __restrict__ scale) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const float* src = w + row * k;
   float amax = 0.0f;
@@ -70,6 +74,8 @@ __global__ void quant_w8pc_kernel(const float* __restrict__ w, int64_t n, int64_
 __global__ void dequant_w4g32_kernel(const uint8_t* __restrict__ packed,
                                      const uint16_t* __restrict__ scale, int64_t n, int64_t k,
                                      float* __restrict__ w) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= n * k) return;
   const int64_t row = idx / k, col = idx % k;
@@ -81,6 +87,8 @@ __global__ void dequant_w4g32_kernel(const uint8_t* __restrict__ packed,
 
 __global__ void dequant_w8pc_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale,
                                     int64_t n, int64_t k, float* __restrict__ w) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t idx = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= n * k) return;
   w[idx] = float(q[idx]) * scale[idx / k];
@@ -91,7 +99,7 @@ int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, ui
   if (n < 0 || k <= 0 || k % 32) return SB_INVALID_ARGUMENT;
   const int64_t total = n * (k / 32);
   if (total == 0) return SB_OK;
-  quant_w4g32_kernel<<<ceil_div(total, 128), 128, 0, st>>>(w, n, k, packed, scale);
+  launch_pdl(quant_w4g32_kernel, dim3(ceil_div(total, 128)), dim3(128), 0, st, w, n, k, packed, scale);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -100,7 +108,7 @@ int launch_quant_w8pc(const float* w, int64_t n, int64_t k, int8_t* q, float* sc
                       cudaStream_t st) {
   if (n < 0 || k <= 0) return SB_INVALID_ARGUMENT;
   if (n == 0) return SB_OK;
-  quant_w8pc_kernel<<<unsigned(n), 256, 0, st>>>(w, n, k, q, scale);
+  launch_pdl(quant_w8pc_kernel, dim3(unsigned(n)), dim3(256), 0, st, w, n, k, q, scale);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -109,7 +117,7 @@ int launch_dequant_w4g32(const uint8_t* packed, const uint16_t* scale, int64_t n
                          float* w, cudaStream_t st) {
   if (n < 0 || k <= 0 || k % 32) return SB_INVALID_ARGUMENT;
   if (n == 0) return SB_OK;
-  dequant_w4g32_kernel<<<ceil_div(n * k, 256), 256, 0, st>>>(packed, scale, n, k, w);
+  launch_pdl(dequant_w4g32_kernel, dim3(ceil_div(n * k, 256)), dim3(256), 0, st, packed, scale, n, k, w);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -118,7 +126,7 @@ int launch_dequant_w8pc(const int8_t* q, const float* scale, int64_t n, int64_t 
                         cudaStream_t st) {
   if (n < 0 || k <= 0) return SB_INVALID_ARGUMENT;
   if (n == 0) return SB_OK;
-  dequant_w8pc_kernel<<<ceil_div(n * k, 256), 256, 0, st>>>(q, scale, n, k, w);
+  launch_pdl(dequant_w8pc_kernel, dim3(ceil_div(n * k, 256)), dim3(256), 0, st, q, scale, n, k, w);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }

@@ -10,8 +10,10 @@
 //     epilogue applies SwiGLU (the gate/up activations never reach HBM);
 //   * a linear whose only consumer is a residual add writes x + W.x directly.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <map>
+#include <type_traits>
 
 #include "plugin.hpp"
 
@@ -59,7 +61,11 @@ struct Lowerer {
   }
   const Value& V(uint32_t id) const { return g.values[id]; }
 
-  void push(Step s) { exe.steps.push_back(std::move(s)); }
+  int cur_node = -1;
+  void push(Step s) {
+    if (s.node < 0) s.node = cur_node;
+    exe.steps.push_back(std::move(s));
+  }
 
   bool same_dims(uint32_t a, uint32_t b) const { return V(a).dims == V(b).dims; }
 
@@ -201,9 +207,75 @@ struct Lowerer {
 
     for (size_t i = 0; i < nn; ++i) {
       if (absorbed[i]) continue;
+      cur_node = int(i);
       if (!lower_node(int(i))) return false;
     }
+    fuse_qkv_rope();
     return true;
+  }
+
+  // q/k/v linears of one x whose outputs feed only rope(q), rope(k) and one
+  // attention node become one launch: the GEMV epilogue rotates q and k and
+  // appends k and v to the caches, and the attention step skips its append.
+  void fuse_qkv_rope() {
+    auto only = [&](uint32_t v, int node) {
+      return cons[v].size() == 1 && cons[v][0] == node && !is_output[v];
+    };
+    auto find_step = [&](SK kind, int node) {
+      for (size_t i = 0; i < exe.steps.size(); ++i)
+        if (exe.steps[i].kind == kind && exe.steps[i].node == node) return int(i);
+      return -1;
+    };
+    for (size_t si = 0; si < exe.steps.size(); ++si) {
+      Step& L = exe.steps[si];
+      if (L.kind != SK::Linear || L.njobs != 3 || L.epi != sb::Epilogue::None ||
+          (L.fmt != sb::WFormat::W4G32 && L.fmt != sb::WFormat::W8PC))
+        continue;
+      const uint32_t yq = L.v[3], yk = L.v[7], yv = L.v[11];
+      if (cons[yq].size() != 1 || cons[yk].size() != 1 || cons[yv].size() != 1) continue;
+      const int rq = cons[yq][0], rk = cons[yk][0], an = cons[yv][0];
+      const Node& RQ = g.nodes[rq];
+      const Node& RK = g.nodes[rk];
+      const Node& A = g.nodes[an];
+      auto is_rope = [](const Node& n) { return n.op == STRATA_OP_CUSTOM && n.pattern == "fused::rope"; };
+      if (!is_rope(RQ) || !is_rope(RK) || !(A.op == STRATA_OP_CUSTOM && A.pattern == "fused::attention"))
+        continue;
+      if (RQ.outputs.size() != 1 || RK.outputs.size() != 1 || A.inputs.size() < 6) continue;
+      const uint32_t qr = RQ.outputs[0], kr = RK.outputs[0];
+      if (!only(yq, rq) || !only(yk, rk) || !only(kr, an) || !only(yv, an) || !only(qr, an)) continue;
+      if (A.inputs[0] != qr || A.inputs[1] != kr || A.inputs[2] != yv) continue;
+      if (RQ.inputs[1] != A.inputs[5] || RK.inputs[1] != A.inputs[5]) continue;
+      const int64_t hd = RQ.attr_int("head_dim", 0);
+      if (hd != RK.attr_int("head_dim", 0) || RQ.attr_float("theta", 10000.0) != RK.attr_float("theta", 10000.0))
+        continue;
+      const int ap = find_step(SK::Attention, an), kp = find_step(SK::KvAppend, an);
+      const int sq = find_step(SK::Rope, rq), sk = find_step(SK::Rope, rk);
+      if (ap < 0 || kp < 0 || sq < 0 || sk < 0) continue;
+      const Step& AT = exe.steps[ap];
+      if (!AT.bf16 || AT.i[4] != hd) continue;
+      Step f;
+      f.kind = SK::QkvRope;
+      f.bf16 = true;
+      f.fmt = L.fmt;
+      f.node = L.node;
+      f.label = L.label + "+rope+kv_append";
+      f.i[0] = L.i[0];       // M
+      f.i[1] = L.i[1];       // K
+      f.i[2] = AT.i[2];      // heads
+      f.i[3] = AT.i[3];      // kv heads
+      f.i[4] = hd;
+      f.i[5] = AT.i[5];      // max_len
+      f.i[6] = AT.i[1];      // tokens per sequence
+      f.d = RQ.attr_float("theta", 10000.0);
+      const uint32_t kc = A.inputs[3], vc = A.inputs[4], pos = A.inputs[5];
+      f.v = {L.v[0], L.v[1], L.v[2], L.v[5], L.v[6], L.v[9], L.v[10], qr, kc, vc, pos};
+      f.reads = {L.v[0], L.v[1], L.v[2], L.v[5], L.v[6], L.v[9], L.v[10], pos, kc, vc};
+      f.writes = {qr, kc, vc};
+      exe.steps[si] = f;
+      std::vector<int> drop = {sq, sk, kp};
+      std::sort(drop.rbegin(), drop.rend());
+      for (int d : drop) exe.steps.erase(exe.steps.begin() + d);
+    }
   }
 
   bool lower_linear(int ni) {
@@ -587,7 +659,9 @@ struct Lowerer {
       st.i[3] = KVH;
       st.i[4] = D;
       st.i[5] = L;
-      st.scratch_bytes = sb::attention_scratch_bytes(rows, H, KVH, D, L);
+      st.i[6] = V(pos).producer < 0 ? 1 : 0;  // positions come from the host, not a kernel
+      st.scratch_bytes = is_bf16(dt) ? sb::attention_v2_scratch_bytes(rows, H, KVH, D, L)
+                                     : sb::attention_scratch_bytes(rows, H, KVH, D, L);
       st.v = {q, kc, vc, pos, out};
       st.reads = {q, kc, vc, pos};
       st.writes = {out};
@@ -827,6 +901,10 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
     case SK::Attention: {
       float* scratch = st.scratch_bytes ? reinterpret_cast<float*>(static_cast<char*>(p.exe.ws) + st.scratch_off)
                                         : nullptr;
+      if constexpr (std::is_same<T, uint16_t>::value)
+        return sb::launch_attention_v2(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]),
+                                       P<int32_t>(p, st.v[3]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
+                                       st.i[5], st.i[6] != 0, scratch, P<T>(p, st.v[4]), ctx.d_err, s);
       return sb::launch_attention<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]),
                                      P<int32_t>(p, st.v[3]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
                                      st.i[5], scratch, P<T>(p, st.v[4]), ctx.d_err, s);
@@ -858,7 +936,43 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
           const int n = int(wv.dims[0]);
           b.jobs[j] = sb::LinearJob{p.at(w), p.at(sc), n, P<uint16_t>(p, y), n, P<uint16_t>(p, r), n};
         }
-        rc = sb::launch_linear(b, s);
+        sb::GemvMmaArgs ga{};
+        ga.lb = b;
+        ga.mode = st.epi == sb::Epilogue::SwiGLU ? sb::GemvMode::SwiGLU : sb::GemvMode::Plain;
+        ga.pdl = sb::pdl_enabled();
+        rc = sb::gemv_mma_supported(ga) ? sb::launch_gemv_mma(ga, s) : sb::launch_linear(b, s);
+        break;
+      }
+      case SK::QkvRope: {
+        sb::GemvMmaArgs ga{};
+        sb::LinearBatch& b = ga.lb;
+        b.x = P<uint16_t>(p, st.v[0]);
+        b.m = int(st.i[0]);
+        b.k = int(st.i[1]);
+        b.fmt = st.fmt;
+        b.epi = sb::Epilogue::None;
+        b.njobs = 3;
+        const int hd = int(st.i[4]);
+        const int ns[3] = {int(st.i[2]) * hd, int(st.i[3]) * hd, int(st.i[3]) * hd};
+        for (int j = 0; j < 3; ++j)
+          b.jobs[j] = sb::LinearJob{p.at(st.v[1 + 2 * j]), p.at(st.v[2 + 2 * j]), ns[j], nullptr, ns[j], nullptr, ns[j]};
+        ga.mode = sb::GemvMode::QkvRope;
+        ga.pdl = sb::pdl_enabled();
+        sb::QkvExtra& e = ga.qkv;
+        e.pos = P<int32_t>(p, st.v[10]);
+        e.q_out = P<uint16_t>(p, st.v[7]);
+        e.k_cache = P<uint16_t>(p, st.v[8]);
+        e.v_cache = P<uint16_t>(p, st.v[9]);
+        e.hq = int(st.i[2]);
+        e.hkv = int(st.i[3]);
+        e.head_dim = hd;
+        e.max_len = int(st.i[5]);
+        e.tokens_per_seq = int(st.i[6]);
+        e.theta = st.d;
+        e.err = ctx.d_err;
+        if (!sb::gemv_mma_supported(ga))
+          fail(STRATA_INTERNAL, "fused q/k/v projection `" + st.label + "` has an unsupported layout");
+        rc = sb::launch_gemv_mma(ga, s);
         break;
       }
       case SK::GemmF32:

@@ -11,6 +11,7 @@
 
 #include "../../../include/strata_b200.h"
 #include "../k_elem.cuh"
+#include "../k_gemv_mma.cuh"
 #include "wire.hpp"
 
 namespace sbp {
@@ -64,7 +65,7 @@ struct Ctx {
 enum class SK {
   Linear, RmsNorm, Rope, SwiGLU, Binary, Unary, Softmax, LayerNorm, Transpose, Slice,
   Broadcast, Copy, Embed, Argmax, GemmF32, KvAppend, Attention, AllReduce,
-  Quant4, Quant8, Dequant4, Dequant8,
+  Quant4, Quant8, Dequant4, Dequant8, QkvRope,
 };
 
 struct Step {
@@ -80,6 +81,7 @@ struct Step {
   int njobs = 0;
   uint64_t scratch_off = 0, scratch_bytes = 0;
   std::vector<uint32_t> reads, writes;  // for liveness; writes may include in-place inputs
+  int node = -1;                       // originating graph node
   std::string label;
 };
 
