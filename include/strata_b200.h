@@ -122,6 +122,25 @@ int32_t strata_b200_attention_decode_bf16(
     int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_len,
     void *scratch, uint16_t *out, void *stream);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that cannot call cudaMalloc -- for example code running
+ * while a stream is captured in a mode that refuses allocation, or a runtime
+ * whose device memory is all owned by its own pool.  The split-KV partials go
+ * to a scratch area inside the library (a __device__ array of
+ * strata_b200_noalloc_scratch_capacity() bytes, 32 MiB, reserved on every GPU
+ * that loads the library until the process exits) instead of a caller buffer.
+ * Same arguments and results as strata_b200_attention_decode_bf16 otherwise.
+ * Returns STRATA_RESOURCE_EXHAUSTED if the shape needs more scratch than the
+ * capacity.  The first call on a device looks up the scratch address there;
+ * make that first call before any stream capture.  Calls that overlap on the
+ * GPU share the scratch and race: serialise them (one stream, or events). */
+uint64_t strata_b200_noalloc_scratch_capacity(void);
+int32_t strata_b200_attention_decode_bf16_noalloc(
+    const uint16_t *q, const uint16_t *k_new, const uint16_t *v_new,
+    uint16_t *k_cache, uint16_t *v_cache, const int32_t *pos, int64_t batch,
+    int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_len,
+    uint16_t *out, void *stream);
+
 int32_t strata_b200_embed_bf16(const int32_t *ids, int64_t rows,
                                const uint16_t *table, int64_t vocab,
                                int64_t dim, uint16_t *out, void *stream);
