@@ -245,22 +245,40 @@ __global__ void attn_merge_kernel(const float* __restrict__ partial, int heads, 
                                   T* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
+  extern __shared__ float wts[];  // [splits] weight of each split
+  __shared__ float inv_l;
   const int rh = blockIdx.x;  // row * heads + h
   const float* pp = partial + int64_t(rh) * splits * (D + 2);
-  float mx = -INFINITY;
-  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, pp[s * (D + 2)]);
-  float l = 0.0f;
-  for (int s = 0; s < splits; ++s) {
-    const float ms = pp[s * (D + 2)];
-    if (ms != -INFINITY) l += pp[s * (D + 2) + 1] * expf(ms - mx);
-  }
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float a = 0.0f;
-    for (int s = 0; s < splits; ++s) {
-      const float ms = pp[s * (D + 2)];
-      if (ms != -INFINITY) a += pp[s * (D + 2) + 2 + d] * expf(ms - mx);
+  const int tid = threadIdx.x;
+  // Per-split maxima, loaded in parallel.
+  for (int s = tid; s < splits; s += blockDim.x) wts[s] = pp[s * (D + 2)];
+  __syncthreads();
+  if (tid < 32) {
+    float mx = -INFINITY;
+    for (int s = tid; s < splits; s += 32) mx = fmaxf(mx, wts[s]);
+    mx = warp_max(mx);
+    float l = 0.0f;
+    for (int s = tid; s < splits; s += 32) {
+      const float ms = wts[s];
+      const float w = ms == -INFINITY ? 0.0f : expf(ms - mx);
+      l += pp[s * (D + 2) + 1] * w;
+      wts[s] = w;
     }
-    st1(out + int64_t(rh) * D + d, l > 0.0f ? a / l : 0.0f);
+    l = warp_sum(l);
+    if (tid == 0) inv_l = l > 0.0f ? 1.0f / l : 0.0f;
+  }
+  __syncthreads();
+  for (int d = tid; d < D; d += blockDim.x) {
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int s = 0;
+    for (; s + 4 <= splits; s += 4) {  // four independent loads in flight
+      a0 = fmaf(pp[(s + 0) * (D + 2) + 2 + d], wts[s + 0], a0);
+      a1 = fmaf(pp[(s + 1) * (D + 2) + 2 + d], wts[s + 1], a1);
+      a2 = fmaf(pp[(s + 2) * (D + 2) + 2 + d], wts[s + 2], a2);
+      a3 = fmaf(pp[(s + 3) * (D + 2) + 2 + d], wts[s + 3], a3);
+    }
+    for (; s < splits; ++s) a0 = fmaf(pp[s * (D + 2) + 2 + d], wts[s], a0);
+    st1(out + int64_t(rh) * D + d, ((a0 + a1) + (a2 + a3)) * inv_l);
   }
 }
 
@@ -483,7 +501,7 @@ static int launch_v2(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, 
   count_launch();
   if (splits > 1) {
     const unsigned nb = unsigned(rows * heads);
-    if (launch_pdl(attn_merge_kernel<uint16_t, D>, dim3(nb), dim3(D), 0, st, (const float*)scratch, int(heads),
+    if (launch_pdl(attn_merge_kernel<uint16_t, D>, dim3(nb), dim3(D), splits * sizeof(float), st, (const float*)scratch, int(heads),
                    splits, out) != cudaSuccess)
       return SB_INTERNAL;
     count_launch();
@@ -573,9 +591,9 @@ int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32
   if (splits > 1) {
     const unsigned nb = unsigned(rows * heads);
     if (head_dim == 128)
-      launch_pdl(attn_merge_kernel<T, 128>, dim3(nb), dim3(128), 0, st, scratch, int(heads), splits, out);
+      launch_pdl(attn_merge_kernel<T, 128>, dim3(nb), dim3(128), splits * sizeof(float), st, scratch, int(heads), splits, out);
     else
-      launch_pdl(attn_merge_kernel<T, 64>, dim3(nb), dim3(64), 0, st, scratch, int(heads), splits, out);
+      launch_pdl(attn_merge_kernel<T, 64>, dim3(nb), dim3(64), splits * sizeof(float), st, scratch, int(heads), splits, out);
     SB_LAUNCH_CHECK();
   }
   return SB_OK;
