@@ -1,28 +1,36 @@
 // Tensor-core GEMV for decode (M <= 16 rows of x per launch), int4 group-32
 // and int8 per-channel weights, with fused epilogues.
 //
-// Work decomposition.  A block computes one 16-row mma.m16n8k16 tile of the
-// output.  Its 8 warps split K into 8 slices of whole 32-code groups; each
-// warp streams its slice of the 16 weight rows straight from HBM into mma
-// fragment registers (no shared-memory staging), and the 8 partial fragments
-// are summed through shared memory at the end.  A 4096 x 4096 matrix is 256
-// blocks x 8 warps = 2048 streaming warps.
+// Work decomposition.  The output is cut into 16-row mma.m16n8k16 tiles.  The
+// grid is persistent (at most one wave of resident blocks); block b computes
+// tiles b, b + grid, b + 2 grid, ...  Within a tile the 8 warps split K into 8
+// slices of whole 32-code groups and the 8 partial fragments are summed
+// through shared memory by finish_tile.
 //
-// Memory pipeline.  Each warp issues the loads for its first 16 groups (and
-// their scales) before griddepcontrol.wait, so under programmatic dependent
-// launch the weight stream of this kernel overlaps the tail of the previous
-// kernel; only the activations, which the previous kernel produces, are read
-// after the wait.
+// Memory pipeline.  Each warp copies its slice of the 16 weight rows to its
+// own shared-memory ring with 16-byte cp.async (a row's slice is contiguous,
+// so every copy instruction moves whole 32-byte sectors), two chunks of 8
+// groups deep, together with the int4 scales of those groups.  The ring runs
+// over the block's whole tile sequence, so the next tile's weights stream in
+// while the current tile is reduced.  The first two chunks are issued before
+// griddepcontrol.wait: under programmatic dependent launch the weight stream
+// overlaps the tail of the previous kernel, and only the activations, which
+// that kernel produces, are read after the wait.  ldmatrix m8n8 (b16) then
+// hands thread (g, q) exactly the 32-bit word q of rows g and g + 8 of a group,
+// which is the fragment the dequantisation below needs.
 //
-// Dequantisation.  Thread (g, q) of the fragment holds, per row and group,
-// the 32-bit word q: eight int4 codes at k offsets 8q..8q+7.  XOR 0x88888888
-// turns each code c into c + 8; OR-ing nibble pairs (j, j+4) into the mantissa
-// of bf16 128.0 and subtracting 136.0 gives the exact codes as bf16x2 pairs.
-// The MMA's k order inside a group is permuted to match (virtual k 2q,2q+1 <->
-// real 8q+2s, 8q+2s+4 for k16 step s) and the activations are permuted the
-// same way with byte permutes, so the dot product is unchanged.  Each group's
-// two MMAs accumulate into a fresh fragment that is scaled by the group's
-// bf16 scale in f32: dequantisation is exactly code * scale, as in the oracle.
+// Dequantisation.  Thread (g, q) holds, per row and group, the word q: eight
+// int4 codes at k offsets 8q..8q+7.  XOR 0x88888888 turns each code c into
+// c + 8; OR-ing nibble pairs (j, j+4) into the mantissa of bf16 128.0 and
+// subtracting 136.0 gives the exact codes as bf16x2 pairs.  The MMA's k order
+// inside a group is permuted to match (virtual k 2q,2q+1 <-> real 8q+2s,
+// 8q+2s+4 for k16 step s) and the activations are permuted the same way with
+// byte permutes, so the dot product is unchanged.  Each group's two MMAs
+// accumulate into a fresh fragment that is scaled by the group's bf16 scale in
+// f32: dequantisation is exactly code * scale, as in the oracle.
+#include <cstdlib>
+#include <string>
+
 #include "k_gemv_mma.cuh"
 
 namespace sb {
@@ -31,7 +39,8 @@ namespace {
 
 constexpr int kWarps = 8;      // K-slices per block
 constexpr int kTileRows = 16;  // output rows per block
-constexpr int kChunk = 16;     // groups loaded per batch of loads
+constexpr int kChunk = 8;      // groups per pipeline stage
+constexpr int kStages = 2;
 
 struct Params {
   const uint16_t* x;
@@ -45,6 +54,7 @@ struct Params {
   uint16_t* y[3];
   const uint16_t* res[3];
   int m_base;        // absolute row of this launch's first x row (sequence index)
+  int tiles;         // 16-row output tiles
   QkvExtra qkv;
 };
 
@@ -83,12 +93,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-__device__ __forceinline__ uint32_t ldg32_stream(const void* p) {
-  uint32_t r;
-  asm volatile("ld.global.nc.L1::evict_first.u32 %0, [%1];" : "=r"(r) : "l"(p));
-  return r;
-}
-
 // Job and matrix row of tile row t (0..15) in block y.  Tile rows t and t + 8
 // form one epilogue pair.
 template <int MODE>
@@ -119,103 +123,18 @@ __device__ __forceinline__ void row_of(const Params& p, int y, int t, int& job, 
   }
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+// Sum the 8 K-slice partials of tile y through shared memory and run the
+// epilogue.  Every thread of the block calls this once per tile.
 template <int FMT, int NT, int MODE>
-__global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_constant__ Params p) {
-  __shared__ float red[kWarps][kTileRows][16];
-  const int y = blockIdx.x;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, q = lane & 3;
-  constexpr int BPG = FMT == 0 ? 16 : 32;  // bytes per row per 32-code group
-
-  int jlo, rlo, jhi, rhi;
-  row_of<MODE>(p, y, g, jlo, rlo);
-  row_of<MODE>(p, y, g + 8, jhi, rhi);
-  const int64_t row_bytes = int64_t(p.k) * BPG / 32;
-  const uint8_t* wlo = p.w[jlo] + int64_t(rlo) * row_bytes;
-  const uint8_t* whi = p.w[jhi] + int64_t(rhi) * row_bytes;
-  const int gb = warp * p.gpw;
-  const int ge = min(p.groups, gb + p.gpw);
-
-  pdl_trigger();
-
-  float acc[NT][4];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-
-  // x row used by this thread's B fragment for n-tile t: rows past M repeat
-  // the last row (their output columns are never written).
-  const uint16_t* xrow[NT];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) xrow[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k;
-
-  bool waited = false;
-  for (int c0 = gb; c0 < ge; c0 += kChunk) {
-    const int nc = min(kChunk, ge - c0);
-    // ---- weights and scales: independent of the previous kernel
-    uint32_t wl[kChunk][BPG / 16], wh[kChunk][BPG / 16];
-    float sl[kChunk], sh[kChunk];
-#pragma unroll
-    for (int i = 0; i < kChunk; ++i) {
-      if (i < nc) {
-#pragma unroll
-        for (int s = 0; s < BPG / 16; ++s) {
-          wl[i][s] = ldg32_stream(wlo + int64_t(c0 + i) * BPG + 16 * s + 4 * q);
-          wh[i][s] = ldg32_stream(whi + int64_t(c0 + i) * BPG + 16 * s + 4 * q);
-        }
-        if constexpr (FMT == 0) {
-          const unsigned short* s_lo = reinterpret_cast<const unsigned short*>(p.s[jlo]);
-          const unsigned short* s_hi = reinterpret_cast<const unsigned short*>(p.s[jhi]);
-          sl[i] = bf2f(__ldg(s_lo + int64_t(rlo) * p.groups + c0 + i));
-          sh[i] = bf2f(__ldg(s_hi + int64_t(rhi) * p.groups + c0 + i));
-        }
-      }
-    }
-    if (!waited) {
-      pdl_wait();  // the activations come from the previous kernel
-      waited = true;
-    }
-#pragma unroll
-    for (int i = 0; i < kChunk; ++i) {
-      if (i < nc) {
-        const int gi = c0 + i;
-        if constexpr (FMT == 0) {
-          const uint32_t ul = wl[i][0] ^ 0x88888888u, uh = wh[i][0] ^ 0x88888888u;
-          const uint32_t p0 = int4_pair(ul, 0), p1 = int4_pair(ul, 1), p2 = int4_pair(ul, 2),
-                         p3 = int4_pair(ul, 3);
-          const uint32_t h0 = int4_pair(uh, 0), h1 = int4_pair(uh, 1), h2 = int4_pair(uh, 2),
-                         h3 = int4_pair(uh, 3);
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const uint4 xv = ldg16(xrow[t] + int64_t(gi) * 32 + 8 * q);
-            float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            mma_bf16(d, p0, h0, p1, h1, prmt(xv.x, xv.z, 0x5410), prmt(xv.x, xv.z, 0x7632));
-            mma_bf16(d, p2, h2, p3, h3, prmt(xv.y, xv.w, 0x5410), prmt(xv.y, xv.w, 0x7632));
-            acc[t][0] = fmaf(d[0], sl[i], acc[t][0]);
-            acc[t][1] = fmaf(d[1], sl[i], acc[t][1]);
-            acc[t][2] = fmaf(d[2], sh[i], acc[t][2]);
-            acc[t][3] = fmaf(d[3], sh[i], acc[t][3]);
-          }
-        } else {
-#pragma unroll
-          for (int s = 0; s < 2; ++s) {
-            const uint32_t ul = wl[i][s] ^ 0x80808080u, uh = wh[i][s] ^ 0x80808080u;
-            const uint32_t a0 = pack_bf16x2(int8_code(ul, 0), int8_code(ul, 2));
-            const uint32_t a2 = pack_bf16x2(int8_code(ul, 1), int8_code(ul, 3));
-            const uint32_t a1 = pack_bf16x2(int8_code(uh, 0), int8_code(uh, 2));
-            const uint32_t a3 = pack_bf16x2(int8_code(uh, 1), int8_code(uh, 3));
-#pragma unroll
-            for (int t = 0; t < NT; ++t) {
-              const uint2 xv = __ldg(reinterpret_cast<const uint2*>(xrow[t] + int64_t(gi) * 32 + 16 * s + 4 * q));
-              mma_bf16(acc[t], a0, a1, a2, a3, prmt(xv.x, xv.y, 0x5410), prmt(xv.x, xv.y, 0x7632));
-            }
-          }
-        }
-      }
-    }
-  }
-  if (!waited) pdl_wait();
-
-  // ---- sum the 8 K-slice partials
+__device__ __forceinline__ void finish_tile(const Params& p, int y, float (&red)[kWarps][kTileRows][16],
+                                            const float (&acc)[NT][4], int warp, int g, int q, int tid) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     red[warp][g][t * 8 + 2 * q] = acc[t][0];
@@ -287,21 +206,189 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_cons
       }
     }
   }
+  __syncthreads();  // red is reused by the next tile
+}
+
+template <int FMT>
+struct Stage {
+  static constexpr int kBPG = FMT == 0 ? 16 : 32;            // bytes per row per group
+  static constexpr int kW = kChunk * kTileRows * kBPG;        // weight bytes of one stage
+  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;  // bf16 scales of one stage
+  static constexpr int kBytes = kW + kS;
+};
+
+// Per warp: the ring of kStages stages (weights, then bf16 scales [16][kChunk]).
+__host__ __device__ constexpr size_t warp_smem_bytes(int fmt) {
+  return size_t(kStages) * (fmt == 0 ? Stage<0>::kBytes : Stage<1>::kBytes);
+}
+
+template <int FMT, int NT, int MODE>
+__global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_constant__ Params p) {
+  __shared__ float red[kWarps][kTileRows][16];
+  extern __shared__ __align__(128) uint8_t dsm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  constexpr int BPG = Stage<FMT>::kBPG;
+  uint8_t* ring = dsm + size_t(warp) * warp_smem_bytes(FMT);
+
+  const int64_t row_bytes = int64_t(p.k) * BPG / 32;
+  const int gb = warp * p.gpw;
+  const int ng = max(0, min(p.groups, gb + p.gpw) - gb);
+  const int nchunks = max(1, (ng + kChunk - 1) / kChunk);  // a warp with no groups still steps
+  // This block's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int my_tiles = (p.tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
+  const int items = my_tiles * nchunks;
+
+  // Copy item it (tile it / nchunks, chunk it % nchunks) into stage it % kStages:
+  // 16 rows x nj groups of weights (16 B copies, consecutive lanes along a
+  // row) and, for int4, the matching bf16 scales (4 B copies).
+  auto issue = [&](int it) {
+    if (it < items) {
+      const int y = int(blockIdx.x) + (it / nchunks) * int(gridDim.x);
+      const int c = it % nchunks;
+      const int nj = max(0, min(kChunk, ng - c * kChunk));
+      uint8_t* dst = ring + (it % kStages) * Stage<FMT>::kBytes;
+      const int per_row = nj * (BPG / 16);
+      for (int e = lane; e < kTileRows * per_row; e += 32) {
+        const int r = e / per_row, i = e % per_row;
+        const int j = i / (BPG / 16), h = i % (BPG / 16);
+        int job, row;
+        row_of<MODE>(p, y, r, job, row);
+        cp_async16(dst + ((j * kTileRows + r) * BPG) + h * 16,
+                   p.w[job] + int64_t(row) * row_bytes + int64_t(gb + c * kChunk + j) * BPG + h * 16);
+      }
+      if constexpr (FMT == 0) {
+        // Scales as bf16 pairs: needs an even group count and an even slice start.
+        uint8_t* sdst = dst + Stage<FMT>::kW;
+        const int pairs = (nj + 1) / 2;
+        for (int e = lane; e < kTileRows * pairs; e += 32) {
+          const int r = e / pairs, i = e % pairs;
+          int job, row;
+          row_of<MODE>(p, y, r, job, row);
+          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.s[job]) +
+                               (int64_t(row) * p.groups + gb + c * kChunk + 2 * i) * 2;
+          const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(sdst + (r * kChunk + 2 * i) * 2));
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(src) : "memory");
+        }
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  pdl_trigger();
+  for (int it = 0; it < kStages; ++it) issue(it);
+  pdl_wait();  // activations come from the previous kernel
+
+  float acc[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+  // x row used by this thread's B fragment for n-tile t: rows past M repeat
+  // the last row (their output columns are never written).
+  const uint16_t* xrow[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) xrow[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k + int64_t(gb) * 32;
+  const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix mi, row rr
+
+  for (int it = 0; it < items; ++it) {
+    const int c = it % nchunks;
+    const int y = int(blockIdx.x) + (it / nchunks) * int(gridDim.x);
+    asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 1) : "memory");
+    __syncwarp();
+    const uint8_t* st = ring + (it % kStages) * Stage<FMT>::kBytes;
+    const int nj = max(0, min(kChunk, ng - c * kChunk));
+#pragma unroll
+    for (int j = 0; j < kChunk; j += 2) {
+      if (j < nj) {
+        if constexpr (FMT == 0) {
+          uint32_t f[4];
+          ldsm_x4(f, st + (((j + (mi >> 1)) * kTileRows + (mi & 1) * 8 + rr) * BPG));
+          const uint16_t* ss = reinterpret_cast<const uint16_t*>(st + Stage<FMT>::kW);
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            if (j + jj < nj) {
+              const int gi = c * kChunk + j + jj;  // group within the slice
+              const uint32_t ul = f[2 * jj] ^ 0x88888888u, uh = f[2 * jj + 1] ^ 0x88888888u;
+              const uint32_t p0 = int4_pair(ul, 0), p1 = int4_pair(ul, 1), p2 = int4_pair(ul, 2),
+                             p3 = int4_pair(ul, 3);
+              const uint32_t h0 = int4_pair(uh, 0), h1 = int4_pair(uh, 1), h2 = int4_pair(uh, 2),
+                             h3 = int4_pair(uh, 3);
+              const float sl = bf2f(ss[g * kChunk + j + jj]), sh = bf2f(ss[(g + 8) * kChunk + j + jj]);
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const uint4 xv = ldg16(xrow[t] + int64_t(gi) * 32 + 8 * q);
+                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                mma_bf16(d, p0, h0, p1, h1, prmt(xv.x, xv.z, 0x5410), prmt(xv.x, xv.z, 0x7632));
+                mma_bf16(d, p2, h2, p3, h3, prmt(xv.y, xv.w, 0x5410), prmt(xv.y, xv.w, 0x7632));
+                acc[t][0] = fmaf(d[0], sl, acc[t][0]);
+                acc[t][1] = fmaf(d[1], sl, acc[t][1]);
+                acc[t][2] = fmaf(d[2], sh, acc[t][2]);
+                acc[t][3] = fmaf(d[3], sh, acc[t][3]);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 2; ++jj) {
+            if (j + jj < nj) {
+              const int gi = c * kChunk + j + jj;
+              // int8: a group is 32 B per row = two 16 B halves, one k16 step each.
+              uint32_t f[4];
+              ldsm_x4(f, st + (((j + jj) * kTileRows + (mi & 1) * 8 + rr) * BPG) + (mi >> 1) * 16);
+#pragma unroll
+              for (int s = 0; s < 2; ++s) {
+                const uint32_t ul = f[2 * s] ^ 0x80808080u, uh = f[2 * s + 1] ^ 0x80808080u;
+                const uint32_t a0 = pack_bf16x2(int8_code(ul, 0), int8_code(ul, 2));
+                const uint32_t a2 = pack_bf16x2(int8_code(ul, 1), int8_code(ul, 3));
+                const uint32_t a1 = pack_bf16x2(int8_code(uh, 0), int8_code(uh, 2));
+                const uint32_t a3 = pack_bf16x2(int8_code(uh, 1), int8_code(uh, 3));
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                  const uint2 xv =
+                      __ldg(reinterpret_cast<const uint2*>(xrow[t] + int64_t(gi) * 32 + 16 * s + 4 * q));
+                  mma_bf16(acc[t], a0, a1, a2, a3, prmt(xv.x, xv.y, 0x5410), prmt(xv.x, xv.y, 0x7632));
+                }
+              }
+            }
+          }
+        }
+      }
+    }
+    __syncwarp();
+    issue(it + kStages);  // keeps the ring full across tile boundaries
+    if (c == nchunks - 1) {
+      finish_tile<FMT, NT, MODE>(p, y, red, acc, warp, g, q, tid);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 template <int FMT, int NT, int MODE>
 int launch_one(const Params& p, int blocks, bool pdl, cudaStream_t st) {
+  auto kern = gemv_mma_kernel<FMT, NT, MODE>;
+  const size_t smem = kWarps * warp_smem_bytes(FMT);
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+      return SB_INTERNAL;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+  }
+  // Persistent: at most one full wave of blocks, each walking tiles.
+  const int grid = blocks < per_sm * kNumSMs ? blocks : per_sm * kNumSMs;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(blocks, 1, 1);
+  cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kWarps * 32, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr;
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (cudaLaunchKernelEx(&cfg, gemv_mma_kernel<FMT, NT, MODE>, p) != cudaSuccess) return SB_INTERNAL;
+  if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return SB_INTERNAL;
   count_launch();
   return SB_OK;
 }
@@ -318,10 +405,21 @@ int dispatch_mode(GemvMode mode, const Params& p, int blocks, bool pdl, cudaStre
 
 }  // namespace
 
+// STRATA_B200_GEMV=cudacore routes every batch to the CUDA-core GEMV (for A/B measurements).
+static bool tensor_core_gemv_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STRATA_B200_GEMV");
+    return !(v && std::string(v) == "cudacore");
+  }();
+  return on;
+}
+
 bool gemv_mma_supported(const GemvMmaArgs& a) {
+  if (!tensor_core_gemv_enabled() && a.mode != GemvMode::QkvRope) return false;
   const LinearBatch& b = a.lb;
   if (b.fmt != WFormat::W4G32 && b.fmt != WFormat::W8PC) return false;
   if (b.k % 32 || b.m <= 0) return false;
+  if (b.fmt == WFormat::W4G32 && (b.k / 32) % 2) return false;  // scales copied as bf16 pairs
   auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!aligned(b.x)) return false;
   for (int j = 0; j < b.njobs; ++j)
@@ -349,7 +447,8 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
   const LinearBatch& b = a.lb;
   const int fmt = b.fmt == WFormat::W4G32 ? 0 : 1;
   const int groups = b.k / 32;
-  const int gpw = (groups + kWarps - 1) / kWarps;
+  int gpw = (groups + kWarps - 1) / kWarps;
+  gpw += gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
   int rows = 0;
   switch (a.mode) {
     case GemvMode::Plain:
@@ -378,6 +477,7 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
     }
     p.qkv = a.qkv;
     p.m_base = m0;
+    p.tiles = blocks;
     if (a.mode == GemvMode::QkvRope) {
       const QkvExtra& e = a.qkv;
       p.qkv.pos = e.pos + m0;

@@ -193,3 +193,45 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
             hd.out = b.node(Op.custom("fused::argmax"), [logits], [(I32, (R,))], {}, "argmax")[0]
     b.output(hd.out)
     return b.build(), hd
+
+
+# Matrices split by output feature (column-parallel) and by input feature
+# (row-parallel) in the tensor-parallel layout; everything else is replicated.
+_COLUMN_PARALLEL = ("q", "k", "v", "g", "u")
+_ROW_PARALLEL = ("o", "d")
+
+
+def shard_layer(full: dict, shape: DecoderShape, fmt: str, rank: int, world: int) -> dict:
+    """One rank's slice of one layer's full (unsharded) weights.
+
+    ``full`` maps the names of ``weight_shapes(shape, fmt, 1)`` (and
+    ``k_cache`` / ``v_cache``) to numpy arrays in the graph's layouts: int4
+    codes [N, K/2] with bf16 scales [N, K/32], int8 codes [N, K] with f32
+    scales [N], or plain [N, K] weights.  Column-parallel matrices keep rows
+    [r*N/t, (r+1)*N/t); row-parallel ones keep columns [r*K/t, (r+1)*K/t) of
+    the codes and the matching scale groups (per-channel int8 scales belong
+    to the unsharded output rows and are kept whole).  KV caches keep their
+    rank's kv heads.
+    """
+    t, r = world, rank
+    out = {}
+    for name, arr in full.items():
+        if name in ("attn_norm", "ffn_norm"):
+            out[name] = arr
+        elif name in ("k_cache", "v_cache"):
+            g = arr.shape[1] // t
+            out[name] = arr[:, r * g:(r + 1) * g].copy()
+        else:
+            kind, key = name[0], name[1:]
+            if key in _COLUMN_PARALLEL:
+                n = arr.shape[0] // t
+                out[name] = arr[r * n:(r + 1) * n].copy()
+            elif key in _ROW_PARALLEL:
+                if kind == "s" and fmt == "w8pc":
+                    out[name] = arr  # per output channel: unsharded rows
+                else:
+                    c = arr.shape[1] // t
+                    out[name] = arr[:, r * c:(r + 1) * c].copy()
+            else:
+                raise ValueError(f"unknown weight {name}")
+    return out

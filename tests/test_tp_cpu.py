@@ -1,0 +1,72 @@
+"""Tensor parallelism without a GPU: two gloo ranks each run their shard graph
+on the oracle, all-reducing after o_proj and down_proj, and must reproduce the
+unsharded decoder step (the host-side sharding and graph construction that
+bench.py --gpus N and the plugin's fused::all_reduce rely on)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from tests.conftest import PKG, ROOT
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_path):
+    import sys
+    for p in (ROOT, PKG):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch
+    import torch.distributed as dist
+    from oracle import graph_eval, oracle as ora
+    from strata_host.blocks import DecoderShape, decoder_graph, shard_layer
+    from tests.helpers import seeded_graph_inputs
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    shape = DecoderShape(256, 4, 2, 64, 512, 100, 2)
+    batch, max_len, fill = 2, 40, 30
+    full_g, full_hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt="w4g32", head="logits")
+    full = seeded_graph_inputs(full_g, cache_fill=fill)
+    ids = ora.uniform_i32(2, batch, 0, shape.vocab)
+    pos = np.array([fill, fill - 1], np.int32)
+    full[full_hd.tokens], full[full_hd.pos] = ids, pos
+
+    g, hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt="w4g32", head="logits",
+                          tp_rank=rank, tp_world=world)
+    inputs = {hd.tokens: ids, hd.pos: pos, hd.embed_table: full[full_hd.embed_table],
+              hd.final_norm: full[full_hd.final_norm], hd.lm_w: full[full_hd.lm_w], hd.lm_s: full[full_hd.lm_s]}
+    for li in range(shape.layers):
+        layer_full = {k: full[v] for k, v in full_hd.layers[li].ids.items()}
+        shard = shard_layer(layer_full, shape, "w4g32", rank, world)
+        for k, v in hd.layers[li].ids.items():
+            assert shard[k].shape == tuple(g.values[v].dims), (k, shard[k].shape, g.values[v].dims)
+            inputs[v] = shard[k]
+
+    def all_reduce(_name, x):
+        t = torch.from_numpy(np.ascontiguousarray(x, np.float32))
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return ora.round_bf16(t.numpy())
+
+    got = graph_eval.evaluate(g, inputs, all_reduce=all_reduce)[hd.out]
+    if rank == 0:
+        want = graph_eval.evaluate(full_g, full)[full_hd.out]
+        np.save(result_path, np.stack([got, want]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_tensor_parallel_step_matches_unsharded(tmp_path):
+    path = str(tmp_path / "tp.npy")
+    mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
+    got, want = np.load(path)
+    err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    assert err <= 2e-2, f"tensor-parallel logits differ from unsharded by {err:.3e}"
