@@ -40,7 +40,7 @@ namespace {
 constexpr int kWarps = 8;      // K-slices per block
 constexpr int kTileRows = 16;  // output rows per block
 constexpr int kChunk = 8;      // groups per pipeline stage
-constexpr int kStages = 2;
+constexpr int kMaxRows = 64;  // x rows per launch
 
 struct Params {
   const uint16_t* x;
@@ -93,34 +93,37 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Job and matrix row of tile row t (0..15) in block y.  Tile rows t and t + 8
-// form one epilogue pair.
+// Tile y's matrix rows: tile row t < 8 is row row_lo + t of job job_lo, tile
+// row t >= 8 is row row_hi + t - 8 of job job_hi.  Rows t and t + 8 form one
+// epilogue pair (gate/up for SwiGLU, the two rotate-half partners for QkvRope).
+struct TileRows {
+  int job_lo, row_lo, job_hi, row_hi;
+};
+
 template <int MODE>
-__device__ __forceinline__ void row_of(const Params& p, int y, int t, int& job, int& row) {
+__device__ __forceinline__ TileRows tile_rows(const Params& p, int y) {
+  TileRows tr;
   if constexpr (MODE == 0) {
-    int r = y * kTileRows + t;
-    job = 0;
+    int r = y * kTileRows, job = 0;
     while (job + 1 < p.njobs && r >= p.n[job]) r -= p.n[job++];
-    row = r;
+    tr = {job, r, job, r + 8};
   } else if constexpr (MODE == 1) {
-    job = t < 8 ? 0 : 1;
-    row = y * 8 + (t & 7);
+    tr = {0, y * 8, 1, y * 8};
   } else {
     const int hd = p.qkv.head_dim;
-    const int bph = hd / 16;  // blocks per head: 8 rotate-half pairs per block
-    const int head = y / bph, j = y % bph;
-    const int in_head = 8 * j + (t & 7) + (t < 8 ? 0 : hd / 2);
-    if (head < p.qkv.hq) {
-      job = 0;
-      row = head * hd + in_head;
-    } else if (head < p.qkv.hq + p.qkv.hkv) {
-      job = 1;
-      row = (head - p.qkv.hq) * hd + in_head;
-    } else {
+    const int bph = hd / 16;  // tiles per head: 8 rotate-half pairs per tile
+    const int head = y / bph, j = y - head * bph;
+    int job = 0, hb = head;
+    if (head >= p.qkv.hq + p.qkv.hkv) {
       job = 2;
-      row = (head - p.qkv.hq - p.qkv.hkv) * hd + in_head;
+      hb = head - p.qkv.hq - p.qkv.hkv;
+    } else if (head >= p.qkv.hq) {
+      job = 1;
+      hb = head - p.qkv.hq;
     }
+    tr = {job, hb * hd + 8 * j, job, hb * hd + 8 * j + hd / 2};
   }
+  return tr;
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem) {
@@ -130,31 +133,42 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem) {
                : "r"(a));
 }
 
-// Sum the 8 K-slice partials of tile y through shared memory and run the
+__device__ __forceinline__ uint32_t lds32(const void* smem) {
+  return *reinterpret_cast<const uint32_t*>(smem);
+}
+
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(a), "l"(gmem) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Sum the 8 K-slice partials of one tile through shared memory and run the
 // epilogue.  Every thread of the block calls this once per tile.
 template <int FMT, int NT, int MODE>
-__device__ __forceinline__ void finish_tile(const Params& p, int y, float (&red)[kWarps][kTileRows][16],
+__device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
+                                            float (&red)[kWarps][kTileRows][8 * NT],
                                             const float (&acc)[NT][4], int warp, int g, int q, int tid) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    red[warp][g][t * 8 + 2 * q] = acc[t][0];
-    red[warp][g][t * 8 + 2 * q + 1] = acc[t][1];
-    red[warp][g + 8][t * 8 + 2 * q] = acc[t][2];
-    red[warp][g + 8][t * 8 + 2 * q + 1] = acc[t][3];
+    *reinterpret_cast<float2*>(&red[warp][g][t * 8 + 2 * q]) = make_float2(acc[t][0], acc[t][1]);
+    *reinterpret_cast<float2*>(&red[warp][g + 8][t * 8 + 2 * q]) = make_float2(acc[t][2], acc[t][3]);
   }
   __syncthreads();
   const int items = 8 * p.m;
   for (int it = tid; it < items; it += kWarps * 32) {
-    const int pp = it / p.m, m = it % p.m;
+    const int pp = it / p.m, m = it - pp * p.m;
     float vlo = 0.0f, vhi = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       vlo += red[w][pp][m];
       vhi += red[w][pp + 8][m];
     }
-    int jl, nlo, jh, nhi;
-    row_of<MODE>(p, y, pp, jl, nlo);
-    row_of<MODE>(p, y, pp + 8, jh, nhi);
+    const int jl = tr.job_lo, nlo = tr.row_lo + pp, jh = tr.job_hi, nhi = tr.row_hi + pp;
     if (FMT == 1) {
       vlo *= reinterpret_cast<const float*>(p.s[jl])[nlo];
       vhi *= reinterpret_cast<const float*>(p.s[jh])[nhi];
@@ -209,113 +223,137 @@ __device__ __forceinline__ void finish_tile(const Params& p, int y, float (&red)
   __syncthreads();  // red is reused by the next tile
 }
 
+// One pipeline stage of one warp: kChunk groups of the tile's 16 rows, laid
+// out [group][row][bytes per group] so that an ldmatrix 8x8 matrix (8 rows of
+// one group) is 8 x 16 contiguous bytes; int4 stages also hold the bf16
+// scales [row][kChunk].  int8 rows are 32 B: the two 16-byte halves of rows
+// 4..7 (mod 8) are swapped so that ldmatrix reads are free of bank conflicts.
 template <int FMT>
 struct Stage {
-  static constexpr int kBPG = FMT == 0 ? 16 : 32;            // bytes per row per group
-  static constexpr int kW = kChunk * kTileRows * kBPG;        // weight bytes of one stage
-  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;  // bf16 scales of one stage
+  static constexpr int kBPG = FMT == 0 ? 16 : 32;                    // bytes per row per group
+  static constexpr int kW = kChunk * kTileRows * kBPG;                // weight bytes
+  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;    // scale bytes
   static constexpr int kBytes = kW + kS;
+  static constexpr int kDepth = FMT == 0 ? 4 : 2;                     // stages per warp (power of two)
 };
 
-// Per warp: the ring of kStages stages (weights, then bf16 scales [16][kChunk]).
 __host__ __device__ constexpr size_t warp_smem_bytes(int fmt) {
-  return size_t(kStages) * (fmt == 0 ? Stage<0>::kBytes : Stage<1>::kBytes);
+  return fmt == 0 ? size_t(Stage<0>::kDepth) * Stage<0>::kBytes : size_t(Stage<1>::kDepth) * Stage<1>::kBytes;
 }
 
 template <int FMT, int NT, int MODE>
 __global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_constant__ Params p) {
-  __shared__ float red[kWarps][kTileRows][16];
+  using S = Stage<FMT>;
+  __shared__ __align__(16) float red[kWarps][kTileRows][8 * NT];
   extern __shared__ __align__(128) uint8_t dsm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
-  constexpr int BPG = Stage<FMT>::kBPG;
   uint8_t* ring = dsm + size_t(warp) * warp_smem_bytes(FMT);
 
-  const int64_t row_bytes = int64_t(p.k) * BPG / 32;
-  const int gb = warp * p.gpw;
-  const int ng = max(0, min(p.groups, gb + p.gpw) - gb);
-  const int nchunks = max(1, (ng + kChunk - 1) / kChunk);  // a warp with no groups still steps
-  // This block's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
-  const int my_tiles = (p.tiles - int(blockIdx.x) + int(gridDim.x) - 1) / int(gridDim.x);
-  const int items = my_tiles * nchunks;
+  const int64_t row_bytes = int64_t(p.k) * S::kBPG / 32;
+  const int gb = warp * p.gpw;                               // first group of this warp's K-slice
+  const int ng = max(0, min(p.groups, gb + p.gpw) - gb);     // groups in the slice
+  const int nchunks = max(1, (ng + kChunk - 1) / kChunk);    // a warp with no groups still steps
 
-  // Copy item it (tile it / nchunks, chunk it % nchunks) into stage it % kStages:
-  // 16 rows x nj groups of weights (16 B copies, consecutive lanes along a
-  // row) and, for int4, the matching bf16 scales (4 B copies).
-  auto issue = [&](int it) {
-    if (it < items) {
-      const int y = int(blockIdx.x) + (it / nchunks) * int(gridDim.x);
-      const int c = it % nchunks;
-      const int nj = max(0, min(kChunk, ng - c * kChunk));
-      uint8_t* dst = ring + (it % kStages) * Stage<FMT>::kBytes;
-      const int per_row = nj * (BPG / 16);
-      for (int e = lane; e < kTileRows * per_row; e += 32) {
-        const int r = e / per_row, i = e % per_row;
-        const int j = i / (BPG / 16), h = i % (BPG / 16);
-        int job, row;
-        row_of<MODE>(p, y, r, job, row);
-        cp_async16(dst + ((j * kTileRows + r) * BPG) + h * 16,
-                   p.w[job] + int64_t(row) * row_bytes + int64_t(gb + c * kChunk + j) * BPG + h * 16);
-      }
+  // Copy side.  Lane l always copies tile row cr = l & 15; lanes 0-15 and
+  // 16-31 take alternate 16-byte pieces of the row's chunk, so each copy
+  // instruction writes 512 contiguous bytes of shared memory.  The copy runs
+  // kDepth items ahead of the math and crosses tile boundaries.
+  const int cr = lane & 15, ch = lane >> 4;
+  int i_tile = blockIdx.x, i_c = 0, i_slot = 0;
+  const uint8_t* wrow = nullptr;
+  const uint8_t* srow = nullptr;
+  auto set_rows = [&](int y) {
+    const TileRows tr = tile_rows<MODE>(p, y);
+    const int job = cr < 8 ? tr.job_lo : tr.job_hi;
+    const int row = cr < 8 ? tr.row_lo + cr : tr.row_hi + cr - 8;
+    wrow = p.w[job] + int64_t(row) * row_bytes + int64_t(gb) * S::kBPG;
+    if constexpr (FMT == 0)
+      srow = static_cast<const uint8_t*>(p.s[job]) + (int64_t(row) * p.groups + gb) * 2;
+  };
+  if (i_tile < p.tiles) set_rows(i_tile);
+  auto issue = [&]() {
+    if (i_tile < p.tiles) {
+      const int nj = min(kChunk, ng - i_c * kChunk);  // <= 0 for a warp with no groups
+      uint8_t* dst = ring + i_slot * S::kBytes;
       if constexpr (FMT == 0) {
-        // Scales as bf16 pairs: needs an even group count and an even slice start.
-        uint8_t* sdst = dst + Stage<FMT>::kW;
-        const int pairs = (nj + 1) / 2;
-        for (int e = lane; e < kTileRows * pairs; e += 32) {
-          const int r = e / pairs, i = e % pairs;
-          int job, row;
-          row_of<MODE>(p, y, r, job, row);
-          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.s[job]) +
-                               (int64_t(row) * p.groups + gb + c * kChunk + 2 * i) * 2;
-          const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(sdst + (r * kChunk + 2 * i) * 2));
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(src) : "memory");
+        const uint8_t* src = wrow + i_c * (kChunk * 16);
+#pragma unroll
+        for (int i = 0; i < kChunk / 2; ++i) {
+          const int h = ch + 2 * i;
+          if (h < nj) cp_async16(dst + (h * kTileRows + cr) * 16, src + h * 16);
         }
+        // Scales as bf16 pairs (the slice start and nj are even).
+        const uint8_t* ssrc = srow + i_c * (kChunk * 2);
+#pragma unroll
+        for (int i = 0; i < kChunk / 4; ++i) {
+          const int pr = ch + 2 * i;
+          if (2 * pr < nj) cp_async4(dst + S::kW + cr * (kChunk * 2) + pr * 4, ssrc + pr * 4);
+        }
+      } else {
+        const uint8_t* src = wrow + i_c * (kChunk * 32);
+        const int sw = (cr >> 2) & 1;
+#pragma unroll
+        for (int i = 0; i < kChunk; ++i) {
+          const int pc = ch + 2 * i;
+          if ((pc >> 1) < nj)
+            cp_async16(dst + ((pc >> 1) * kTileRows + cr) * 32 + (((pc & 1) ^ sw) * 16), src + pc * 16);
+        }
+      }
+      if (++i_c == nchunks) {
+        i_c = 0;
+        i_tile += gridDim.x;
+        if (i_tile < p.tiles) set_rows(i_tile);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
+    i_slot = (i_slot + 1) & (S::kDepth - 1);
   };
 
   pdl_trigger();
-  for (int it = 0; it < kStages; ++it) issue(it);
+#pragma unroll
+  for (int i = 0; i < S::kDepth; ++i) issue();
   pdl_wait();  // activations come from the previous kernel
 
-  float acc[NT][4];
-#pragma unroll
-  for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
   // x row used by this thread's B fragment for n-tile t: rows past M repeat
   // the last row (their output columns are never written).
-  const uint16_t* xrow[NT];
+  const uint16_t* xbase[NT];
 #pragma unroll
-  for (int t = 0; t < NT; ++t) xrow[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k + int64_t(gb) * 32;
+  for (int t = 0; t < NT; ++t)
+    xbase[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k + int64_t(gb) * 32 + (FMT == 0 ? 8 * q : 4 * q);
   const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix mi, row rr
+  int slot = 0;
 
-  for (int it = 0; it < items; ++it) {
-    const int c = it % nchunks;
-    const int y = int(blockIdx.x) + (it / nchunks) * int(gridDim.x);
-    asm volatile("cp.async.wait_group %0;" ::"n"(kStages - 1) : "memory");
-    __syncwarp();
-    const uint8_t* st = ring + (it % kStages) * Stage<FMT>::kBytes;
-    const int nj = max(0, min(kChunk, ng - c * kChunk));
+  for (int y = blockIdx.x; y < p.tiles; y += gridDim.x) {
+    float acc[NT][4];
 #pragma unroll
-    for (int j = 0; j < kChunk; j += 2) {
-      if (j < nj) {
-        if constexpr (FMT == 0) {
-          uint32_t f[4];
-          ldsm_x4(f, st + (((j + (mi >> 1)) * kTileRows + (mi & 1) * 8 + rr) * BPG));
-          const uint16_t* ss = reinterpret_cast<const uint16_t*>(st + Stage<FMT>::kW);
+    for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+    for (int c = 0; c < nchunks; ++c) {
+      cp_async_wait<S::kDepth - 1>();
+      __syncwarp();
+      const uint8_t* st = ring + slot * S::kBytes;
+      const int nj = min(kChunk, ng - c * kChunk);
+      if constexpr (FMT == 0) {
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            if (j + jj < nj) {
-              const int gi = c * kChunk + j + jj;  // group within the slice
+        for (int j = 0; j < kChunk; j += 2) {
+          if (j < nj) {  // nj is even
+            uint32_t f[4];
+            ldsm_x4(f, st + ((j + (mi >> 1)) * kTileRows + (mi & 1) * 8 + rr) * 16);
+            const uint32_t slo = lds32(st + S::kW + g * (kChunk * 2) + j * 2);
+            const uint32_t shi = lds32(st + S::kW + (g + 8) * (kChunk * 2) + j * 2);
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
               const uint32_t ul = f[2 * jj] ^ 0x88888888u, uh = f[2 * jj + 1] ^ 0x88888888u;
               const uint32_t p0 = int4_pair(ul, 0), p1 = int4_pair(ul, 1), p2 = int4_pair(ul, 2),
                              p3 = int4_pair(ul, 3);
               const uint32_t h0 = int4_pair(uh, 0), h1 = int4_pair(uh, 1), h2 = int4_pair(uh, 2),
                              h3 = int4_pair(uh, 3);
-              const float sl = bf2f(ss[g * kChunk + j + jj]), sh = bf2f(ss[(g + 8) * kChunk + j + jj]);
+              const float sl = __uint_as_float(jj ? (slo & 0xFFFF0000u) : (slo << 16));
+              const float sh = __uint_as_float(jj ? (shi & 0xFFFF0000u) : (shi << 16));
+              const int gi = c * kChunk + j + jj;  // group within the slice
 #pragma unroll
               for (int t = 0; t < NT; ++t) {
-                const uint4 xv = ldg16(xrow[t] + int64_t(gi) * 32 + 8 * q);
+                const uint4 xv = ldg16(xbase[t] + gi * 32);
                 float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
                 mma_bf16(d, p0, h0, p1, h1, prmt(xv.x, xv.z, 0x5410), prmt(xv.x, xv.z, 0x7632));
                 mma_bf16(d, p2, h2, p3, h3, prmt(xv.y, xv.w, 0x5410), prmt(xv.y, xv.w, 0x7632));
@@ -326,42 +364,39 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_cons
               }
             }
           }
-        } else {
+        }
+      } else {
+        const int swr = (rr >> 2) & 1;
 #pragma unroll
-          for (int jj = 0; jj < 2; ++jj) {
-            if (j + jj < nj) {
-              const int gi = c * kChunk + j + jj;
-              // int8: a group is 32 B per row = two 16 B halves, one k16 step each.
-              uint32_t f[4];
-              ldsm_x4(f, st + (((j + jj) * kTileRows + (mi & 1) * 8 + rr) * BPG) + (mi >> 1) * 16);
+        for (int j = 0; j < kChunk; ++j) {
+          if (j < nj) {
+            const int gi = c * kChunk + j;
+            // int8: a group is 32 B per row = two 16 B halves, one k16 step each.
+            uint32_t f[4];
+            ldsm_x4(f, st + (j * kTileRows + (mi & 1) * 8 + rr) * 32 + (((mi >> 1) ^ swr) * 16));
 #pragma unroll
-              for (int s = 0; s < 2; ++s) {
-                const uint32_t ul = f[2 * s] ^ 0x80808080u, uh = f[2 * s + 1] ^ 0x80808080u;
-                const uint32_t a0 = pack_bf16x2(int8_code(ul, 0), int8_code(ul, 2));
-                const uint32_t a2 = pack_bf16x2(int8_code(ul, 1), int8_code(ul, 3));
-                const uint32_t a1 = pack_bf16x2(int8_code(uh, 0), int8_code(uh, 2));
-                const uint32_t a3 = pack_bf16x2(int8_code(uh, 1), int8_code(uh, 3));
+            for (int s2 = 0; s2 < 2; ++s2) {
+              const uint32_t ul = f[2 * s2] ^ 0x80808080u, uh = f[2 * s2 + 1] ^ 0x80808080u;
+              const uint32_t a0 = pack_bf16x2(int8_code(ul, 0), int8_code(ul, 2));
+              const uint32_t a2 = pack_bf16x2(int8_code(ul, 1), int8_code(ul, 3));
+              const uint32_t a1 = pack_bf16x2(int8_code(uh, 0), int8_code(uh, 2));
+              const uint32_t a3 = pack_bf16x2(int8_code(uh, 1), int8_code(uh, 3));
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                  const uint2 xv =
-                      __ldg(reinterpret_cast<const uint2*>(xrow[t] + int64_t(gi) * 32 + 16 * s + 4 * q));
-                  mma_bf16(acc[t], a0, a1, a2, a3, prmt(xv.x, xv.y, 0x5410), prmt(xv.x, xv.y, 0x7632));
-                }
+              for (int t = 0; t < NT; ++t) {
+                const uint2 xv = __ldg(reinterpret_cast<const uint2*>(xbase[t] + gi * 32 + 16 * s2));
+                mma_bf16(acc[t], a0, a1, a2, a3, prmt(xv.x, xv.y, 0x5410), prmt(xv.x, xv.y, 0x7632));
               }
             }
           }
         }
       }
+      __syncwarp();
+      issue();  // refills the stage just read
+      slot = (slot + 1) & (S::kDepth - 1);
     }
-    __syncwarp();
-    issue(it + kStages);  // keeps the ring full across tile boundaries
-    if (c == nchunks - 1) {
-      finish_tile<FMT, NT, MODE>(p, y, red, acc, warp, g, q, tid);
-#pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
-    }
+    finish_tile<FMT, NT, MODE>(p, tile_rows<MODE>(p, y), red, acc, warp, g, q, tid);
   }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  cp_async_wait<0>();
 }
 
 template <int FMT, int NT, int MODE>
@@ -401,6 +436,15 @@ int dispatch_mode(GemvMode mode, const Params& p, int blocks, bool pdl, cudaStre
     case GemvMode::QkvRope: return launch_one<FMT, NT, 2>(p, blocks, pdl, st);
   }
   return SB_INVALID_ARGUMENT;
+}
+
+// x rows per launch: n-tiles of 8 (1, 2, 4 or 8 of them).
+template <int FMT>
+int dispatch_nt(const Params& p, GemvMode mode, int blocks, bool pdl, cudaStream_t st) {
+  if (p.m <= 8) return dispatch_mode<FMT, 1>(mode, p, blocks, pdl, st);
+  if (p.m <= 16) return dispatch_mode<FMT, 2>(mode, p, blocks, pdl, st);
+  if (p.m <= 32) return dispatch_mode<FMT, 4>(mode, p, blocks, pdl, st);
+  return dispatch_mode<FMT, 8>(mode, p, blocks, pdl, st);
 }
 
 }  // namespace
@@ -459,9 +503,9 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
   }
   const int blocks = rows / kTileRows;
 
-  for (int m0 = 0; m0 < b.m; m0 += 16) {
+  for (int m0 = 0; m0 < b.m; m0 += kMaxRows) {
     Params p{};
-    p.m = b.m - m0 < 16 ? b.m - m0 : 16;
+    p.m = b.m - m0 < kMaxRows ? b.m - m0 : kMaxRows;
     p.x = b.x + int64_t(m0) * b.k;
     p.k = b.k;
     p.groups = groups;
@@ -485,12 +529,11 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
       p.qkv.k_out = e.k_out ? e.k_out + int64_t(m0) * e.hkv * e.head_dim : nullptr;
       p.qkv.v_out = e.v_out ? e.v_out + int64_t(m0) * e.hkv * e.head_dim : nullptr;
     }
-    const bool two = p.m > 8;
     int rc;
     if (fmt == 0)
-      rc = two ? dispatch_mode<0, 2>(a.mode, p, blocks, a.pdl, st) : dispatch_mode<0, 1>(a.mode, p, blocks, a.pdl, st);
+      rc = dispatch_nt<0>(p, a.mode, blocks, a.pdl, st);
     else
-      rc = two ? dispatch_mode<1, 2>(a.mode, p, blocks, a.pdl, st) : dispatch_mode<1, 1>(a.mode, p, blocks, a.pdl, st);
+      rc = dispatch_nt<1>(p, a.mode, blocks, a.pdl, st);
     if (rc) return rc;
   }
   return SB_OK;

@@ -116,6 +116,33 @@ def test_linear_w4g32_matches_oracle(cuda, lib, m):
     assert_close(got[rows], want, TOL_BF16, f"w4g32 m={m}")
 
 
+@pytest.mark.parametrize("fmt", ["w4g32", "w8pc"])
+@pytest.mark.parametrize("m", [1, 5, 24, 64, 65])
+@pytest.mark.parametrize("n,k", [(256, 11008), (48, 2752), (16, 96), (32, 4128)])
+def test_linear_ragged_shapes(cuda, lib, fmt, m, n, k):
+    """K-slices that end in partial chunks or hold no groups, and 1..9 n-tiles of x rows."""
+    torch = cuda
+    if fmt == "w4g32" and (k // 32) % 2:
+        pytest.skip("odd group counts take the CUDA-core path")
+    x = _x_bf16(m, k, seed=3)
+    w = ora.normal(4, (n, k), std=0.02)
+    xd = dev(torch, x.view(np.int16))
+    y = torch.empty((m, n), dtype=torch.int16, device="cuda")
+    if fmt == "w4g32":
+        packed, s = ora.quant_w4g32(w)
+        pd, sd = dev(torch, packed), dev(torch, s.view(np.int16))
+        ok(lib.strata_b200_linear_w4g32(ptr(xd), m, k, ptr(pd), ptr(sd), n, None, ptr(y), stream(torch)))
+        want = ora.linear_w4g32(ora.from_bf16(x), packed, s, threads=ora.max_threads())
+    else:
+        q, s = ora.quant_w8pc(w)
+        qd, sd = dev(torch, q), dev(torch, s)
+        ok(lib.strata_b200_linear_w8pc(ptr(xd), m, k, ptr(qd), ptr(sd), n, None, ptr(y), stream(torch)))
+        want = ora.linear_w8pc(ora.from_bf16(x), q, s, threads=ora.max_threads())
+    torch.cuda.synchronize()
+    got = ora.from_bf16(y.cpu().numpy().view(np.uint16))
+    assert_close(got, ora.round_bf16(want), TOL_BF16, f"{fmt} m={m} n={n} k={k}")
+
+
 @pytest.mark.parametrize("m", [1, 16, 128])
 def test_linear_w8pc_matches_oracle(cuda, lib, m):
     torch = cuda
