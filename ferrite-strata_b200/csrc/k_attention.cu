@@ -16,7 +16,12 @@
 // coalesced, for all G heads.  With one split the block normalises and writes
 // the output; with several it writes (max, sum, unnormalised acc) partials
 // and attn_merge_kernel combines them (flash-decoding).
+#include <algorithm>
+#include <cstdlib>
+#include <string>
+
 #include "common.cuh"
+#include "k_elem.cuh"
 
 namespace sb {
 
@@ -310,8 +315,6 @@ __global__ void __launch_bounds__(kThreads)
                    int tokens_per_seq, int heads, int kv_heads, int max_len, int splits,
                    float scale, int pos_external, float* __restrict__ partial,
                    uint16_t* __restrict__ out, int* err) {
-  pdl_trigger();
-  pdl_wait();
   using L = AttnV2Smem<D, CH>;
   constexpr int kPairs = D / 2;
   constexpr int kPhases = kThreads / kPairs;
@@ -473,7 +476,10 @@ int attention_v2_splits(int64_t rows, int64_t kv_heads, int64_t max_len) {
 
 uint64_t attention_v2_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
                                     int64_t max_len) {
-  const int s = attention_v2_splits(rows, kv_heads, max_len);
+  // Room for whichever kernel runs (the CUDA-core or the tensor-core one).
+  const int64_t span = attention_tc_span(rows, kv_heads, max_len);
+  const int64_t s_tc = (max_len + span - 1) / span;
+  const int64_t s = std::max<int64_t>(attention_v2_splits(rows, kv_heads, max_len), s_tc);
   if (s == 1) return 0;
   return uint64_t(rows) * heads * s * (head_dim + 2) * sizeof(float);
 }
@@ -509,11 +515,40 @@ static int launch_v2(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, 
   return SB_OK;
 }
 
+int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t heads, int64_t head_dim, int splits,
+                                uint16_t* out, cudaStream_t st) {
+  const unsigned nb = unsigned(rows * heads);
+  cudaError_t e;
+  if (head_dim == 128)
+    e = launch_pdl(attn_merge_kernel<uint16_t, 128>, dim3(nb), dim3(128), splits * sizeof(float), st, scratch,
+                   int(heads), splits, out);
+  else if (head_dim == 64)
+    e = launch_pdl(attn_merge_kernel<uint16_t, 64>, dim3(nb), dim3(64), splits * sizeof(float), st, scratch,
+                   int(heads), splits, out);
+  else
+    return SB_INVALID_ARGUMENT;
+  if (e != cudaSuccess) return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
+
+// STRATA_B200_ATTN=v2 keeps bf16 decode attention on the CUDA-core kernel (for A/B measurements).
+static bool tensor_core_attention_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STRATA_B200_ATTN");
+    return !(v && std::string(v) == "v2");
+  }();
+  return on;
+}
+
 int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                         const int32_t* pos, int64_t rows, int64_t tokens_per_seq, int64_t heads,
                         int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
                         float* scratch, uint16_t* out, int* err, cudaStream_t st) {
   if (rows == 0) return SB_OK;
+  if (tensor_core_attention_enabled() && attention_tc_supported(heads, kv_heads, head_dim))
+    return launch_attention_tc(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim, max_len,
+                               pos_external, scratch, out, err, st);
   if (kv_heads <= 0 || heads % kv_heads || heads / kv_heads > kMaxGroup) return SB_INVALID_ARGUMENT;
   const int splits = attention_v2_splits(rows, kv_heads, max_len);
   if (splits > 1 && scratch == nullptr) return SB_INVALID_ARGUMENT;

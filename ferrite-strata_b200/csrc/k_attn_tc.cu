@@ -1,0 +1,326 @@
+// Tensor-core decode attention: bf16 KV cache, head_dim 64 or 128, up to 8
+// query heads per kv head (MHA and GQA).
+//
+// Grid (split, kv head, query row).  A CTA owns `span` consecutive cache
+// positions of one (row, kv head) and its 4 warps take 16-position slabs of
+// that span in turn (slab w, w + 4, ...).  Each warp streams its slabs
+// through its own 3-deep cp.async ring (K and V rows, padded so that ldmatrix
+// rows land in distinct banks) and runs, per slab,
+//
+//   S^T[16 heads x 16 positions] = Q[16 x D] . K^T        (mma.sync m16n8k16)
+//   online softmax per head row, in base 2
+//   O[16 heads x D] += P[16 x 16] . V[16 x D]              (V via ldmatrix.trans)
+//
+// Q rows beyond the group size are zero, so one m16 tile covers any group of
+// up to 8 heads.  Computing S transposed makes the score accumulators exactly
+// the A fragment of P . V, so P never leaves registers.  At the end the warps
+// merge their (max, sum, O) through shared memory and the CTA writes the same
+// (max, sum, unnormalised O) partial as the CUDA-core kernel, which
+// attn_merge_kernel combines across splits.
+//
+// Cache rows below the row's position are final before this kernel starts,
+// so when positions are a graph input the first slabs below the position are
+// requested before griddepcontrol.wait and stream in while the previous kernel
+// (the q/k/v projection that writes row `pos`) finishes.
+#include "common.cuh"
+#include "k_elem.cuh"
+
+namespace sb {
+
+namespace {
+
+constexpr int kTcWarps = 4;
+constexpr int kSlab = 16;    // positions per warp step
+constexpr int kTcDepth = 3;  // slabs in flight per warp
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct TcLayout {
+  static constexpr int kRow = D * 2 + 16;              // padded row bytes
+  static constexpr int kSlabBytes = 2 * kSlab * kRow;  // K rows, then V rows
+  static constexpr int kWarpBytes = kTcDepth * kSlabBytes;
+  static constexpr int kBytes = kTcWarps * kWarpBytes;
+  // The final cross-warp merge reuses the ring: O [warps][8][D], max and sum [warps][8].
+  static_assert(kTcWarps * 8 * D * 4 + 2 * kTcWarps * 8 * 4 <= kBytes, "merge area");
+};
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  // Rows 8..15 of A are zero (a1 = a3 = 0).
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], const void* p) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+// 16-byte copy that reads `src_bytes` (16 or 0) and zero-fills the rest.
+__device__ __forceinline__ void cp16z(void* smem, const void* gmem, int src_bytes) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(a), "l"(gmem), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kTcWarps * 32)
+    attn_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
+                   const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos, int tokens_per_seq,
+                   int heads, int kv_heads, int max_len, int span, int splits, int pos_external,
+                   float* __restrict__ partial, uint16_t* __restrict__ out, int* err) {
+  using Lay = TcLayout<D>;
+  constexpr int kCpr = D / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+  const int G = heads / kv_heads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, qd = lane & 3;
+  uint8_t* ring = smem + warp * Lay::kWarpBytes;
+  const int seq = row / tokens_per_seq;
+  const int64_t head_off = (int64_t(seq) * kv_heads + kvh) * int64_t(max_len) * D;
+  const uint8_t* kb = reinterpret_cast<const uint8_t*>(kc + head_off);
+  const uint8_t* vb = reinterpret_cast<const uint8_t*>(vc + head_off);
+  const int t0 = split * span;
+
+  pdl_trigger();
+
+  // Copy slab i of this warp (global slab warp + 4 i of the span): rows below
+  // `valid` are read, the rest zero-filled (their scores are masked and their
+  // V rows must be finite zeros).  Always commits one group.
+  auto issue = [&](int i, int lim) {
+    const int s = t0 + (warp + kTcWarps * i) * kSlab;
+    const int valid = min(kSlab, max(0, lim - s));
+    if (valid > 0) {
+      uint8_t* dst = ring + (i % kTcDepth) * Lay::kSlabBytes;
+#pragma unroll
+      for (int j = 0; j < 2 * kSlab * kCpr / 32; ++j) {
+        const int c = lane + 32 * j;             // chunk: K rows first, then V rows
+        const int isv = c >= kSlab * kCpr;
+        const int cc = c - isv * kSlab * kCpr;
+        const int r = cc / kCpr, col = cc % kCpr;
+        const int rr = r < valid ? r : 0;        // a readable address for zero-filled rows
+        const uint8_t* src = (isv ? vb : kb) + int64_t(s + rr) * (D * 2) + col * 16;
+        cp16z(dst + (isv * kSlab + r) * Lay::kRow + col * 16, src, r < valid ? 16 : 0);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  // Before the wait: slabs entirely below the row's position.
+  int issued = 0;
+  if (pos_external) {
+    const int p_early = pos[row];
+    if (p_early > 0 && p_early < max_len) {
+      const int lim_pre = min(p_early, t0 + span);
+      while (issued < kTcDepth && t0 + (warp + kTcWarps * issued + 1) * kSlab <= lim_pre) {
+        issue(issued, lim_pre);
+        ++issued;
+      }
+    }
+  }
+  pdl_wait();
+  const int p = pos[row];
+  const bool bad = p < 0 || p >= max_len;
+  if (bad && tid == 0 && err) atomicExch(err, 2);
+  const int lim = bad ? t0 : min(p + 1, t0 + span);  // positions [t0, lim) of this CTA
+  const int slabs = (max(0, lim - t0) + kSlab - 1) / kSlab;
+  const int mine = max(0, (slabs - warp + kTcWarps - 1) / kTcWarps);
+  for (int i = issued; i < kTcDepth; ++i) issue(i, lim);
+
+  // Q as the A fragment (head row g of the group; rows >= G are zero).
+  uint32_t qa0[D / 16], qa2[D / 16];
+  {
+    const bool live = g < G;
+    const uint32_t* qr =
+        reinterpret_cast<const uint32_t*>(q + int64_t(row) * heads * D + int64_t(kvh * G + (live ? g : 0)) * D);
+#pragma unroll
+    for (int k = 0; k < D / 16; ++k) {
+      qa0[k] = live ? qr[k * 8 + qd] : 0u;
+      qa2[k] = live ? qr[k * 8 + 4 + qd] : 0u;
+    }
+  }
+  const float scale = kLog2e * (D == 128 ? 0.08838834764831845f : 0.125f);  // log2(e) / sqrt(D)
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
+  const int mi = lane >> 3, rr = lane & 7;
+
+  for (int i = 0; i < mine; ++i) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kTcDepth - 1) : "memory");
+    __syncwarp();
+    const uint8_t* sK = ring + (i % kTcDepth) * Lay::kSlabBytes;
+    const uint8_t* sV = sK + kSlab * Lay::kRow;
+    const int s0 = t0 + (warp + kTcWarps * i) * kSlab;
+
+    float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+    for (int k = 0; k < D / 16; ++k) {
+      uint32_t b[4];
+      ldsm4(b, sK + ((mi >> 1) * 8 + rr) * Lay::kRow + k * 32 + (mi & 1) * 16);
+      mma16816(sc[0], qa0[k], qa2[k], b[0], b[1]);
+      mma16816(sc[1], qa0[k], qa2[k], b[2], b[3]);
+    }
+    // sc[n][0..1]: head g, positions s0 + 8n + 2qd + {0, 1}.
+    float pv[2][2];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = s0 + 8 * n + 2 * qd + e;
+        pv[n][e] = t < lim ? sc[n][e] * scale : -INFINITY;
+        mx = fmaxf(mx, pv[n][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+    const float corr = exp2f(m_run - m_use);
+    float psum = 0.0f;
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        pv[n][e] = exp2f(pv[n][e] - m_use);
+        psum += pv[n][e];
+      }
+    l_run = l_run * corr + psum;
+    m_run = m_new;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= corr;
+      o[n][1] *= corr;
+    }
+    const uint32_t pa0 = pack2(pv[0][0], pv[0][1]), pa2 = pack2(pv[1][0], pv[1][1]);
+#pragma unroll
+    for (int nb = 0; nb < D / 16; ++nb) {
+      uint32_t v[4];
+      ldsm4t(v, sV + ((mi & 1) * 8 + rr) * Lay::kRow + (2 * nb + (mi >> 1)) * 16);
+      mma16816(o[2 * nb], pa0, pa2, v[0], v[1]);
+      mma16816(o[2 * nb + 1], pa0, pa2, v[2], v[3]);
+    }
+    __syncwarp();
+    issue(i + kTcDepth, lim);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  __syncthreads();  // every warp is done with its ring
+
+  float* sO = reinterpret_cast<float*>(smem);     // [warps][8][D]
+  float* sM = sO + kTcWarps * 8 * D;              // [warps][8]
+  float* sL = sM + kTcWarps * 8;                  // [warps][8]
+  if (g < G) {
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      sO[(warp * 8 + g) * D + n * 8 + 2 * qd] = o[n][0];
+      sO[(warp * 8 + g) * D + n * 8 + 2 * qd + 1] = o[n][1];
+    }
+    if (qd == 0) {
+      sM[warp * 8 + g] = m_run;
+      sL[warp * 8 + g] = l_run;
+    }
+  }
+  __syncthreads();
+  for (int it = tid; it < G * D; it += kTcWarps * 32) {
+    const int h = it / D, d = it % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, sM[w * 8 + h]);
+    float acc = 0.0f, L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kTcWarps; ++w) {
+      const float mw = sM[w * 8 + h];
+      const float wt = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+      acc = fmaf(wt, sO[(w * 8 + h) * D + d], acc);
+      L = fmaf(wt, sL[w * 8 + h], L);
+    }
+    const int hh = kvh * G + h;
+    if (splits == 1) {
+      out[int64_t(row) * heads * D + int64_t(hh) * D + d] = f2bf(L > 0.0f ? acc / L : 0.0f);
+    } else {
+      float* pp = partial + ((int64_t(row) * heads + hh) * splits + split) * (D + 2);
+      pp[2 + d] = acc;
+      if (d == 0) {
+        pp[0] = M == -INFINITY ? -INFINITY : M / kLog2e;  // natural-log units for the merge
+        pp[1] = L;
+      }
+    }
+  }
+}
+
+template <int D>
+int launch_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos, int64_t rows,
+              int64_t tps, int64_t heads, int64_t kv_heads, int64_t max_len, bool pos_external, float* scratch,
+              uint16_t* out, int* err, cudaStream_t st) {
+  using Lay = TcLayout<D>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) !=
+        cudaSuccess)
+      return SB_INTERNAL;
+    configured = true;
+  }
+  const int span = attention_tc_span(rows, kv_heads, max_len);
+  const int splits = int((max_len + span - 1) / span);
+  if (splits > 1 && scratch == nullptr) return SB_INVALID_ARGUMENT;
+  const dim3 grid{unsigned(splits), unsigned(kv_heads), unsigned(rows)};
+  if (launch_pdl(attn_tc_kernel<D>, grid, dim3(kTcWarps * 32), size_t(Lay::kBytes), st, q, kc, vc, pos, int(tps),
+                 int(heads), int(kv_heads), int(max_len), span, splits, pos_external ? 1 : 0, scratch, out,
+                 err) != cudaSuccess)
+    return SB_INTERNAL;
+  count_launch();
+  if (splits > 1) return launch_attention_merge_bf16(scratch, rows, heads, D, splits, out, st);
+  return SB_OK;
+}
+
+}  // namespace
+
+int attention_tc_span(int64_t rows, int64_t kv_heads, int64_t max_len) {
+  // About four CTAs per SM, whole slabs of 64 positions per CTA.
+  const int64_t pairs = rows * kv_heads;
+  const int64_t most = (max_len + 63) / 64;
+  int64_t splits = (4 * kNumSMs + pairs - 1) / pairs;
+  if (splits > most) splits = most;
+  if (splits < 1) splits = 1;
+  const int64_t per = (max_len + splits - 1) / splits;
+  return int((per + 63) / 64 * 64);
+}
+
+bool attention_tc_supported(int64_t heads, int64_t kv_heads, int64_t head_dim) {
+  return kv_heads > 0 && heads % kv_heads == 0 && heads / kv_heads <= 8 && (head_dim == 64 || head_dim == 128);
+}
+
+int launch_attention_tc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
+                        int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                        int64_t max_len, bool pos_external, float* scratch, uint16_t* out, int* err,
+                        cudaStream_t st) {
+  if (rows == 0) return SB_OK;
+  if (!attention_tc_supported(heads, kv_heads, head_dim) || rows > 65535 || kv_heads > 65535)
+    return SB_INVALID_ARGUMENT;
+  if (head_dim == 128)
+    return launch_tc<128>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, max_len, pos_external,
+                          scratch, out, err, st);
+  return launch_tc<64>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, max_len, pos_external,
+                       scratch, out, err, st);
+}
+
+}  // namespace sb

@@ -77,6 +77,17 @@ int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16
                         int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
                         float* scratch, uint16_t* out, int* err, cudaStream_t st);
 
+// Tensor-core bf16 decode attention (k_attn_tc.cu); launch_attention_v2 uses
+// it when supported.  Positions per split and the split-KV merge.
+int attention_tc_span(int64_t rows, int64_t kv_heads, int64_t max_len);
+bool attention_tc_supported(int64_t heads, int64_t kv_heads, int64_t head_dim);
+int launch_attention_tc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
+                        int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                        int64_t max_len, bool pos_external, float* scratch, uint16_t* out, int* err,
+                        cudaStream_t st);
+int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t heads, int64_t head_dim, int splits,
+                                uint16_t* out, cudaStream_t st);
+
 // Quantisation (k_quant.cu).
 int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, uint16_t* scale,
                        cudaStream_t st);

@@ -20,9 +20,9 @@
 // which is the fragment the dequantisation below needs.
 //
 // Dequantisation.  Thread (g, q) holds, per row and group, the word q: eight
-// int4 codes at k offsets 8q..8q+7.  XOR 0x88888888 turns each code c into
-// c + 8; OR-ing nibble pairs (j, j+4) into the mantissa of bf16 128.0 and
-// subtracting 136.0 gives the exact codes as bf16x2 pairs.  The MMA's k order
+// int4 codes at k offsets 8q..8q+7.  Flipping each code's sign bit turns c
+// into c + 8; placing nibble pairs (j, j+4) in the mantissa of bf16 128.0 and
+// subtracting 136.0 gives the exact codes as bf16x2 pairs (int4_pair).  The MMA's k order
 // inside a group is permuted to match (virtual k 2q,2q+1 <-> real 8q+2s,
 // 8q+2s+4 for k16 step s) and the activations are permuted the same way with
 // byte permutes, so the dot product is unchanged.  Each group's two MMAs
@@ -39,7 +39,7 @@ namespace {
 
 constexpr int kWarps = 8;      // K-slices per block
 constexpr int kTileRows = 16;  // output rows per block
-constexpr int kChunk = 8;      // groups per pipeline stage
+constexpr int kChunk = 4;      // groups per pipeline stage
 constexpr int kMaxRows = 64;  // x rows per launch
 
 struct Params {
@@ -73,15 +73,24 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+// a * 1 - 136 on both bf16 halves (exact: a is 136 + code).
+__device__ __forceinline__ uint32_t bf16x2_minus136(uint32_t a) {
   uint32_t r;
-  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(0x3F803F80u), "r"(0xC308C308u));
   return r;
 }
 
-// Nibble pair (j, j+4) of a code word already XOR-ed with 0x88888888.
+// Nibbles j and j + 4 of the raw code word u as the bf16 pair (code_j,
+// code_j+4).  One lop3 computes (a & 0x000F000F) ^ 0x43084308: it keeps the
+// two nibbles, flips their sign bits (two's-complement c becomes c + 8) and
+// sets the exponent of bf16 128, giving 136 + c; the fma removes the 136.
+// The right shift is a high multiply so that it issues on the FMA pipe, which
+// leaves the ALU pipe (the busiest in this loop) to the lop3 and permutes.
 __device__ __forceinline__ uint32_t int4_pair(uint32_t u, int j) {
-  return bf16x2_sub(((u >> (4 * j)) & 0x000F000Fu) | 0x43004300u, 0x43084308u);
+  uint32_t a = u, v;
+  if (j) asm("mul.hi.u32 %0, %1, %2;" : "=r"(a) : "r"(u), "r"(1u << (32 - 4 * j)));
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(v) : "r"(a), "r"(0x000F000Fu), "r"(0x43084308u));
+  return bf16x2_minus136(v);
 }
 
 __device__ __forceinline__ float int8_code(uint32_t u, int j) {
@@ -234,7 +243,7 @@ struct Stage {
   static constexpr int kW = kChunk * kTileRows * kBPG;                // weight bytes
   static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;    // scale bytes
   static constexpr int kBytes = kW + kS;
-  static constexpr int kDepth = FMT == 0 ? 4 : 2;                     // stages per warp (power of two)
+  static constexpr int kDepth = 4;                                    // stages per warp (power of two)
 };
 
 __host__ __device__ constexpr size_t warp_smem_bytes(int fmt) {
@@ -242,7 +251,7 @@ __host__ __device__ constexpr size_t warp_smem_bytes(int fmt) {
 }
 
 template <int FMT, int NT, int MODE>
-__global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) gemv_mma_kernel(const __grid_constant__ Params p) {
   using S = Stage<FMT>;
   __shared__ __align__(16) float red[kWarps][kTileRows][8 * NT];
   extern __shared__ __align__(128) uint8_t dsm[];
@@ -286,7 +295,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_cons
         // Scales as bf16 pairs (the slice start and nj are even).
         const uint8_t* ssrc = srow + i_c * (kChunk * 2);
 #pragma unroll
-        for (int i = 0; i < kChunk / 4; ++i) {
+        for (int i = 0; i < (kChunk / 2 + 1) / 2; ++i) {
           const int pr = ch + 2 * i;
           if (2 * pr < nj) cp_async4(dst + S::kW + cr * (kChunk * 2) + pr * 4, ssrc + pr * 4);
         }
@@ -343,7 +352,7 @@ __global__ void __launch_bounds__(kWarps * 32) gemv_mma_kernel(const __grid_cons
             const uint32_t shi = lds32(st + S::kW + (g + 8) * (kChunk * 2) + j * 2);
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
-              const uint32_t ul = f[2 * jj] ^ 0x88888888u, uh = f[2 * jj + 1] ^ 0x88888888u;
+              const uint32_t ul = f[2 * jj], uh = f[2 * jj + 1];
               const uint32_t p0 = int4_pair(ul, 0), p1 = int4_pair(ul, 1), p2 = int4_pair(ul, 2),
                              p3 = int4_pair(ul, 3);
               const uint32_t h0 = int4_pair(uh, 0), h1 = int4_pair(uh, 1), h2 = int4_pair(uh, 2),

@@ -196,15 +196,17 @@ def test_rms_norm_rope_swiglu(cuda, lib):
     assert_close(ora.from_bf16(ys.cpu().numpy().view(np.uint16)), ora.round_bf16(ora.swiglu(xf, uf)), TOL_BF16, "swiglu")
 
 
-@pytest.mark.parametrize("batch,heads,kv_heads,max_len,fill", [
-    (1, 32, 32, 2112, 2048),   # 7B decode, KV 2048 prefilled
-    (4, 32, 32, 2112, 2048),
-    (2, 64, 8, 4160, 4096),    # 70B GQA, KV 4096
-    (3, 8, 2, 300, 17),        # ragged short caches
+@pytest.mark.parametrize("batch,heads,kv_heads,max_len,fill,d", [
+    (1, 32, 32, 2112, 2048, 128),   # 7B decode, KV 2048 prefilled
+    (4, 32, 32, 2112, 2048, 128),
+    (2, 64, 8, 4160, 4096, 128),    # 70B GQA, KV 4096
+    (3, 8, 2, 300, 17, 128),        # ragged short caches
+    (1, 8, 2, 16, 0, 128),          # the first token: position 0, cache of one slab
+    (5, 16, 4, 530, 515, 64),       # head_dim 64, 4 query heads per kv head
+    (2, 8, 8, 40, 33, 64),          # positions ending inside a 16-position slab
 ])
-def test_attention_decode_matches_oracle(cuda, lib, batch, heads, kv_heads, max_len, fill):
+def test_attention_decode_matches_oracle(cuda, lib, batch, heads, kv_heads, max_len, fill, d):
     torch = cuda
-    d = 128
     kc = np.zeros((batch, kv_heads, max_len, d), np.float32)
     kc[:, :, :fill] = ora.normal(11, (batch, kv_heads, fill, d))
     vc = np.zeros_like(kc)

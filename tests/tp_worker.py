@@ -1,0 +1,84 @@
+"""One rank of the multi-GPU tensor-parallel parity check, started under
+torchrun by tests/test_gpu_tp.py.
+
+Every rank builds the same full (unsharded) weights of a small GQA decoder
+from fixed seeds, keeps its own shard (column-parallel q/k/v/gate/up,
+row-parallel o/down), joins the plugin's NCCL group and runs one decode step
+through the plugin.  Rank 0 writes its logits and the oracle's logits of the
+unsharded step to the path given on the command line."""
+import datetime
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "ferrite-strata_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch.distributed as dist  # noqa: E402
+
+from oracle import graph_eval, oracle as ora  # noqa: E402
+from strata_host import BF16, Device, Plugin  # noqa: E402
+from strata_host.blocks import DecoderShape, decoder_graph, shard_layer  # noqa: E402
+from tests.helpers import seeded_graph_inputs, to_device_bytes  # noqa: E402
+
+# 16 query / 8 kv heads of 128, FFN 5632: every tensor splits evenly over 2, 4 or 8 ranks.
+SHAPE = DecoderShape(2048, 16, 8, 128, 5632, 512, 2)
+BATCH, MAX_LEN, FILL = 4, 136, 128
+
+
+def main(out_path):
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    os.environ["STRATA_B200_DEVICE"] = str(local)
+
+    full_g, full_hd = decoder_graph(SHAPE, batch=BATCH, seq=1, max_len=MAX_LEN, fmt="w4g32", head="logits")
+    full = seeded_graph_inputs(full_g, cache_fill=FILL)
+    full[full_hd.tokens] = ora.uniform_i32(2, BATCH, 0, SHAPE.vocab)
+    full[full_hd.pos] = np.array([FILL - i for i in range(BATCH)], np.int32)
+
+    g, hd = decoder_graph(SHAPE, batch=BATCH, seq=1, max_len=MAX_LEN, fmt="w4g32", head="logits",
+                          tp_rank=rank, tp_world=world)
+    host = {hd.tokens: full[full_hd.tokens], hd.pos: full[full_hd.pos],
+            hd.embed_table: full[full_hd.embed_table], hd.final_norm: full[full_hd.final_norm],
+            hd.lm_w: full[full_hd.lm_w], hd.lm_s: full[full_hd.lm_s]}
+    for li in range(SHAPE.layers):
+        shard = shard_layer({k: full[v] for k, v in full_hd.layers[li].ids.items()}, SHAPE, "w4g32", rank, world)
+        for k, v in hd.layers[li].ids.items():
+            host[v] = shard[k]
+
+    plugin = Plugin(os.path.join(PKG, "libstrata_b200.so"))
+    uid = [plugin.tp_unique_id() if rank == 0 else b""]
+    dist.broadcast_object_list(uid, 0)
+    plugin.tp_init(rank, world, uid[0])
+
+    arena, bufs = {}, []
+    for i, v in enumerate(g.values):
+        if v.producer is None and i in host:
+            b = plugin.upload(v.dtype, v.dims, to_device_bytes(v, host[i]))
+            bufs.append(b)
+            arena[i] = Device(b)
+    exe = plugin.compile(g)
+    assert exe is not None, "the plugin declined the shard graph"
+    exe.run(arena)
+    got = np.asarray(arena[hd.out])
+    if g.values[hd.out].dtype == BF16:
+        got = ora.from_bf16(got.view(np.uint16))
+    exe.free()
+    for b in bufs:
+        b.release()
+    plugin.close()
+
+    if rank == 0:
+        want = graph_eval.evaluate(full_g, full)[full_hd.out]
+        np.save(out_path, np.stack([np.asarray(got, np.float32), np.asarray(want, np.float32)]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])
