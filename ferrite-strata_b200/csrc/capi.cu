@@ -56,12 +56,36 @@ static int32_t linear_common(WFormat fmt, const uint16_t* x, int64_t m, int64_t 
   b.epi = residual ? Epilogue::Residual : Epilogue::None;
   b.njobs = 1;
   b.jobs[0] = LinearJob{w, s, int(n), y, int(n), residual, int(n)};
+  if (m > kGemvMaxRows && gemm_tc_supported(m, n, k, x, w)) {
+    // Prefill-sized batches: tcgen05 GEMM over bf16 weights.  Quantized
+    // weights are first expanded into a stream-ordered temporary (int8: the
+    // exact codes, scaled per channel in the GEMM epilogue; int4: code * group
+    // scale rounded to bf16).
+    const cudaStream_t st = S(stream);
+    if (fmt == WFormat::BF16)
+      return launch_gemm_tc_bf16(x, m, k, static_cast<const uint16_t*>(w), n, nullptr, residual, n, y, n, nullptr,
+                                 st);
+    void* tmp = nullptr;
+    if (cudaMallocAsync(&tmp, size_t(n) * size_t(k) * 2, st) != cudaSuccess) return SB_RESOURCE_EXHAUSTED;
+    int rc = launch_codes_to_bf16(w, s, fmt == WFormat::W8PC ? 1 : 0, n, k, static_cast<uint16_t*>(tmp), st);
+    if (rc == SB_OK)
+      rc = launch_gemm_tc_bf16(x, m, k, static_cast<const uint16_t*>(tmp), n,
+                               fmt == WFormat::W8PC ? static_cast<const float*>(s) : nullptr, residual, n, y, n,
+                               nullptr, st);
+    cudaFreeAsync(tmp, st);
+    return rc;
+  }
   GemvMmaArgs ga{};
   ga.lb = b;
   ga.mode = GemvMode::Plain;
   ga.pdl = pdl_enabled();
   if (gemv_mma_supported(ga)) return launch_gemv_mma(ga, S(stream));
   return launch_linear(b, S(stream));
+}
+
+int32_t strata_b200_linear_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int64_t n,
+                                const uint16_t* residual, uint16_t* y, void* stream) {
+  return linear_common(WFormat::BF16, x, m, k, w, nullptr, n, residual, y, stream);
 }
 
 int32_t strata_b200_linear_w4g32(const uint16_t* x, int64_t m, int64_t k, const uint8_t* packed,

@@ -250,13 +250,41 @@ __global__ void argmax_kernel(const T* __restrict__ x, int64_t cols, int32_t* __
   __shared__ float sv[32];
   __shared__ int32_t si[32];
   const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
   float bv = -INFINITY;
   int32_t bi = INT32_MAX;
-  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
-    const float v = ld(x, row * cols + c);
-    if (v != v) continue;
-    if (bi == INT32_MAX || v > bv) bv = v, bi = int32_t(c);
+  // Each thread visits its columns in increasing order and keeps the first
+  // maximum (strict >); NaNs are skipped.
+  auto take = [&](float v, int64_t c) {
+    if (v == v && (bi == INT32_MAX || v > bv)) bv = v, bi = int32_t(c);
+  };
+  constexpr int kVec = 16 / int(sizeof(T));
+  int64_t c0 = 0;  // first column of the scalar tail
+  if ((reinterpret_cast<uintptr_t>(xr) & 15) == 0) {
+    // 16-byte loads, four in flight per thread.
+    const int64_t nv = cols / kVec, step = blockDim.x;
+    const uint4* xv = reinterpret_cast<const uint4*>(xr);
+    int64_t i = threadIdx.x;
+    for (; i + 3 * step < nv; i += 4 * step) {
+      uint4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = __ldg(xv + i + u * step);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const T* e = reinterpret_cast<const T*>(&a[u]);
+#pragma unroll
+        for (int k = 0; k < kVec; ++k) take(ld(e, k), (i + u * step) * kVec + k);
+      }
+    }
+    for (; i < nv; i += step) {
+      const uint4 a = __ldg(xv + i);
+      const T* e = reinterpret_cast<const T*>(&a);
+#pragma unroll
+      for (int k = 0; k < kVec; ++k) take(ld(e, k), i * kVec + k);
+    }
+    c0 = nv * kVec;
   }
+  for (int64_t c = c0 + threadIdx.x; c < cols; c += blockDim.x) take(ld(xr, c), c);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);

@@ -88,6 +88,16 @@ int launch_attention_tc(const uint16_t* q, const uint16_t* k_cache, const uint16
 int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t heads, int64_t head_dim, int splits,
                                 uint16_t* out, cudaStream_t st);
 
+// tcgen05 bf16 GEMM for prefill-sized batches (k_gemm_tc.cu).  Linear layers
+// with more than kGemvMaxRows rows of x use it; fewer rows stay on the GEMV.
+constexpr int64_t kGemvMaxRows = 64;
+bool gemm_tc_supported(int64_t m, int64_t n, int64_t k, const void* x, const void* w);
+int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int64_t n, const float* scale,
+                        const uint16_t* residual, int64_t ldr, uint16_t* y, int64_t ldy, int* err, cudaStream_t st);
+// Weights as bf16 [n, k]: fmt 1 = int8 codes (exact), fmt 0 = int4 code * bf16 group scale.
+int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, int64_t k, uint16_t* out,
+                         cudaStream_t st);
+
 // Quantisation (k_quant.cu).
 int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, uint16_t* scale,
                        cudaStream_t st);

@@ -1,0 +1,388 @@
+// Tensor-core GEMM on the 5th-generation tensor cores (tcgen05, TMEM, TMA)
+// for prefill-sized batches:
+//
+//   y[m, n] = scale[n] * sum_k x[m, k] * w[n, k]   (+ residual[m, n])
+//
+// x and w are bf16 and K-major (row-major [M, K] and [N, K]); int8 weights
+// reach this kernel as their exact bf16 codes (prepared once per launch by
+// launch_codes_to_bf16), so the per-channel scale is applied in f32 in the
+// epilogue and the product matches the oracle's code * scale.
+//
+// One CTA computes a 128 x 256 tile of y (tokens x features):
+//   warp 0      one thread issues TMA loads of the x tile (128 x 64) and the
+//               w tile (256 x 64), 128-byte swizzled, into a 4-stage ring;
+//   warp 1      allocates 256 TMEM columns (the f32 accumulator: TMEM lane =
+//               token row, column = feature) and one thread issues
+//               tcgen05.mma (M 128, N 256, K 16; four per stage) and
+//               tcgen05.commit to release each stage and, at the end, the
+//               accumulator;
+//   warps 2-5   the epilogue: tcgen05.ld 32 columns at a time from their
+//               TMEM lane quarter, scale, add the residual, round to bf16.
+// Every mbarrier wait is bounded; a wait that runs out records error code 4
+// in *err and the CTA winds down (the TMEM owner still frees its columns).
+#include <cuda.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "k_elem.cuh"
+
+namespace sb {
+
+namespace {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64, kGStages = 4;
+constexpr int kGThreads = 192;
+constexpr int kABytes = kBM * kBK * 2;            // 16 KB
+constexpr int kBBytes = kBN * kBK * 2;            // 32 KB
+constexpr int kGStageBytes = kABytes + kBBytes;   // 48 KB
+constexpr int kGSmem = kGStages * kGStageBytes + 1024 + 256;  // ring + alignment + barriers
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kWaitLimit = 1u << 22;         // bounded mbarrier polls
+
+// Instruction descriptor, kind::f16: f32 accumulate (bits 4-5 = 1), bf16 A
+// and B (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
+// bit 17, M >> 4 at bit 24.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
+                            (uint32_t(kBM >> 4) << 24);
+
+struct GemmArgs {
+  int m, n, k;
+  const float* scale;        // [n] or null
+  const uint16_t* residual;  // [m, ldr] or null
+  int ldr;
+  uint16_t* y;               // [m, ldy]
+  int ldy;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+}
+
+// Wait for the phase with parity `parity` to complete; false when the poll
+// limit runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = su32(bar);
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
+// rows are 128 bytes (64 bf16): 8-row core groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint32_t a = su32(tile);
+  uint64_t d = uint64_t((a & 0x3FFFF) >> 4);  // start address
+  d |= uint64_t(1) << 16;                      // leading byte offset (unused when swizzled)
+  d |= uint64_t(1024 >> 4) << 32;              // stride byte offset
+  d |= uint64_t(1) << 46;                      // descriptor version
+  d |= uint64_t(2) << 61;                      // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kGThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                   const GemmArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGStages * kGStageBytes);
+  uint64_t* empty = full + kGStages;
+  uint64_t* acc_full = empty + kGStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  __shared__ int s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  const int nk = (p.k + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    s_fail = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();  // x comes from the previous kernel
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kGStages;
+        if (kb >= kGStages && !mbar_wait(&empty[s], ((kb / kGStages) - 1) & 1)) {
+          atomicExch(&s_fail, 1);
+          break;
+        }
+        uint8_t* sa = smem + s * kGStageBytes;
+        mbar_expect_tx(&full[s], kGStageBytes);
+        tma_load_2d(sa, &tmap_x, &full[s], kb * kBK, m0);
+        tma_load_2d(sa + kABytes, &tmap_w, &full[s], kb * kBK, n0);
+        issued = kb + 1;
+      }
+      // Let the copies still in flight land before the CTA can exit.
+      for (int kb = issued - kGStages < 0 ? 0 : issued - kGStages; kb < issued; ++kb)
+        mbar_wait(&full[kb % kGStages], (kb / kGStages) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kGStages;
+        if (!mbar_wait(&full[s], (kb / kGStages) & 1)) {
+          ok = false;
+          atomicExch(&s_fail, 1);
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint8_t* sa = smem + s * kGStageBytes;
+        const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K per step
+          umma_bf16(tmem, da + uint64_t(2 * kk), db + uint64_t(2 * kk), (kb | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+  } else {
+    // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    if (!mbar_wait(acc_full, 0)) {
+      atomicExch(&s_fail, 1);
+    } else {
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c * 32), r);
+        const int nb = n0 + c * 32;
+        if (row < p.m && nb < p.n) {
+          uint16_t* yr = p.y + int64_t(row) * p.ldy + nb;
+          const uint16_t* rr = p.residual ? p.residual + int64_t(row) * p.ldr + nb : nullptr;
+          if (nb + 32 <= p.n && (reinterpret_cast<uintptr_t>(yr) & 15) == 0 &&
+              (!rr || (reinterpret_cast<uintptr_t>(rr) & 15) == 0)) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint32_t w[4];
+              uint4 res = rr ? *reinterpret_cast<const uint4*>(rr + 8 * v) : make_uint4(0, 0, 0, 0);
+              const uint32_t rw[4] = {res.x, res.y, res.z, res.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = 8 * v + 2 * e;
+                float lo = __uint_as_float(r[j]), hi = __uint_as_float(r[j + 1]);
+                if (p.scale) {
+                  lo *= p.scale[nb + j];
+                  hi *= p.scale[nb + j + 1];
+                }
+                if (rr) {
+                  lo = bf2f(f2bf(lo)) + bf_lo(rw[e]);
+                  hi = bf2f(f2bf(hi)) + bf_hi(rw[e]);
+                }
+                w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
+              }
+              *reinterpret_cast<uint4*>(yr + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          } else {
+            for (int j = 0; j < 32 && nb + j < p.n; ++j) {
+              float v = __uint_as_float(r[j]);
+              if (p.scale) v *= p.scale[nb + j];
+              if (rr) v = bf2f(f2bf(v)) + bf2f(rr[j]);
+              yr[j] = f2bf(v);
+            }
+          }
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+  if (threadIdx.x == 0 && s_fail && p.err) atomicExch(p.err, 4);
+}
+
+// int8 codes (or int4 codes times their bf16 group scale) as bf16 [n, k].
+__global__ void codes_i8_to_bf16_kernel(const int8_t* __restrict__ q, int64_t count, uint16_t* __restrict__ out) {
+  pdl_trigger();
+  const int64_t n8 = count / 8;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(q) + i);
+    const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      w[e] = uint32_t(f2bf(float(b[2 * e]))) | (uint32_t(f2bf(float(b[2 * e + 1]))) << 16);
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  for (int64_t i = n8 * 8 + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < count;
+       i += int64_t(gridDim.x) * blockDim.x)
+    out[i] = f2bf(float(q[i]));
+}
+
+__global__ void w4g32_to_bf16_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scale,
+                                     int64_t n, int64_t k, uint16_t* __restrict__ out) {
+  pdl_trigger();
+  const int64_t words = n * k / 8;  // 8 codes per 32-bit word
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < words; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(packed) + i);
+    const int64_t e0 = i * 8, row = e0 / k, col = e0 % k;
+    const float s = bf2f(scale[row * (k / 32) + col / 32]);
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int lo = int((u >> (8 * e)) & 0xF), hi = int((u >> (8 * e + 4)) & 0xF);
+      const float clo = float(lo >= 8 ? lo - 16 : lo), chi = float(hi >= 8 ? hi - 16 : hi);
+      w[e] = uint32_t(f2bf(clo * s)) | (uint32_t(f2bf(chi * s)) << 16);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+  static EncodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiled>(p);
+  });
+  return fn;
+}
+
+// A bf16 [rows, k] row-major operand as 64 x box_rows tiles, 128-byte swizzled.
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t k, uint32_t box_rows) {
+  EncodeTiled enc = encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {cuuint64_t(k), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(k) * 2};
+  const cuuint32_t box[2] = {uint32_t(kBK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int64_t m, int64_t n, int64_t k, const void* x, const void* w) {
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return m > 0 && n > 0 && k > 0 && k % 8 == 0 && a16(x) && a16(w) && m <= int64_t(65535) * kBM &&
+         encode_fn() != nullptr;
+}
+
+int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int64_t n, const float* scale,
+                        const uint16_t* residual, int64_t ldr, uint16_t* y, int64_t ldy, int* err, cudaStream_t st) {
+  if (!gemm_tc_supported(m, n, k, x, w)) return SB_INVALID_ARGUMENT;
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, x, m, k, kBM) || !make_map(&mw, w, n, k, kBN)) return SB_INTERNAL;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) != cudaSuccess)
+      return SB_INTERNAL;
+    configured = true;
+  }
+  GemmArgs a;
+  a.m = int(m);
+  a.n = int(n);
+  a.k = int(k);
+  a.scale = scale;
+  a.residual = residual;
+  a.ldr = int(ldr);
+  a.y = y;
+  a.ldy = int(ldy);
+  a.err = err;
+  const dim3 grid{unsigned((n + kBN - 1) / kBN), unsigned((m + kBM - 1) / kBM), 1u};
+  if (launch_pdl(gemm_tc_kernel, grid, dim3(kGThreads), size_t(kGSmem), st, mx, mw, a) != cudaSuccess)
+    return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
+
+int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, int64_t k, uint16_t* out,
+                         cudaStream_t st) {
+  const int threads = 256, blocks = 4 * kNumSMs;
+  cudaError_t e;
+  if (fmt == 1) {  // int8 per channel: the codes themselves
+    e = launch_pdl(codes_i8_to_bf16_kernel, dim3(blocks), dim3(threads), 0, st, static_cast<const int8_t*>(w),
+                   n * k, out);
+  } else if (fmt == 0) {  // int4 group 32: code * bf16 scale, rounded to bf16
+    if (k % 32) return SB_INVALID_ARGUMENT;
+    e = launch_pdl(w4g32_to_bf16_kernel, dim3(blocks), dim3(threads), 0, st, static_cast<const uint8_t*>(w),
+                   static_cast<const uint16_t*>(scale), n, k, out);
+  } else {
+    return SB_INVALID_ARGUMENT;
+  }
+  if (e != cudaSuccess) return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
+
+}  // namespace sb

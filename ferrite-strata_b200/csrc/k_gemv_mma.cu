@@ -39,7 +39,7 @@ namespace {
 
 constexpr int kWarps = 8;      // K-slices per block
 constexpr int kTileRows = 16;  // output rows per block
-constexpr int kChunk = 4;      // groups per pipeline stage
+constexpr int kChunk = 8;      // groups per pipeline stage
 constexpr int kMaxRows = 64;  // x rows per launch
 
 struct Params {
@@ -55,6 +55,7 @@ struct Params {
   const uint16_t* res[3];
   int m_base;        // absolute row of this launch's first x row (sequence index)
   int tiles;         // 16-row output tiles
+  int scale16;       // int4: slices are whole 8-group chunks, scales copied 16 B per row
   QkvExtra qkv;
 };
 
@@ -158,7 +159,7 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Sum the 8 K-slice partials of one tile through shared memory and run the
 // epilogue.  Every thread of the block calls this once per tile.
-template <int FMT, int NT, int MODE>
+template <int FMT, int NT, int MODE, bool kTrailingSync>
 __device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
                                             float (&red)[kWarps][kTileRows][8 * NT],
                                             const float (&acc)[NT][4], int warp, int g, int q, int tid) {
@@ -229,31 +230,65 @@ __device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
       }
     }
   }
-  __syncthreads();  // red is reused by the next tile
+  // A single buffer is rewritten by the next tile; with two buffers the next
+  // tile's barrier already orders this tile's reads before the reuse.
+  if (kTrailingSync) __syncthreads();
 }
 
-// One pipeline stage of one warp: kChunk groups of the tile's 16 rows, laid
-// out [group][row][bytes per group] so that an ldmatrix 8x8 matrix (8 rows of
-// one group) is 8 x 16 contiguous bytes; int4 stages also hold the bf16
-// scales [row][kChunk].  int8 rows are 32 B: the two 16-byte halves of rows
-// 4..7 (mod 8) are swapped so that ldmatrix reads are free of bank conflicts.
+// One pipeline stage of one warp: kChunk groups of the tile's 16 rows, stored
+// row-major (16 rows x kChunk * bytes per group) with the 16-byte pieces of
+// row r XOR-swizzled by r & 7: copies write whole rows and an ldmatrix 8x8
+// matrix (8 rows of one piece) lands in 8 different bank groups.  int4
+// stages also hold the bf16 scales [16 rows][kChunk].
 template <int FMT>
 struct Stage {
   static constexpr int kBPG = FMT == 0 ? 16 : 32;                    // bytes per row per group
-  static constexpr int kW = kChunk * kTileRows * kBPG;                // weight bytes
-  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;    // scale bytes
+  static constexpr int kRowBytes = kChunk * kBPG;                    // 128 / 256
+  static constexpr int kPieces = kRowBytes / 16;                     // 8 / 16
+  static constexpr int kW = kTileRows * kRowBytes;                   // weight bytes
+  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;   // scale bytes
   static constexpr int kBytes = kW + kS;
-  static constexpr int kDepth = 4;                                    // stages per warp (power of two)
+  static constexpr int kDepth = 2;                                   // stages per warp
 };
+
+// Byte offset of 16-byte piece `piece` of tile row `row` in a stage.
+template <int FMT>
+__device__ __forceinline__ int piece_off(int row, int piece) {
+  return row * Stage<FMT>::kRowBytes + ((piece ^ (row & 7)) << 4);
+}
 
 __host__ __device__ constexpr size_t warp_smem_bytes(int fmt) {
   return fmt == 0 ? size_t(Stage<0>::kDepth) * Stage<0>::kBytes : size_t(Stage<1>::kDepth) * Stage<1>::kBytes;
 }
 
+// One int4 group of the tile for every n-tile: dequantise the words of rows
+// g (ul) and g + 8 (uh), two MMAs into a fresh fragment, scale by the group's
+// bf16 scales (half `hi` of the scale pairs slo / shi), accumulate.
+template <int NT, int J>
+__device__ __forceinline__ void int4_group(float (&acc)[NT][4], uint32_t ul, uint32_t uh, uint32_t slo, uint32_t shi,
+                                           int hi, const uint4 (&xv)[NT][J], int j) {
+  const uint32_t p0 = int4_pair(ul, 0), p1 = int4_pair(ul, 1), p2 = int4_pair(ul, 2), p3 = int4_pair(ul, 3);
+  const uint32_t h0 = int4_pair(uh, 0), h1 = int4_pair(uh, 1), h2 = int4_pair(uh, 2), h3 = int4_pair(uh, 3);
+  const float sl = __uint_as_float(hi ? (slo & 0xFFFF0000u) : (slo << 16));
+  const float sh = __uint_as_float(hi ? (shi & 0xFFFF0000u) : (shi << 16));
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const uint4 x = xv[t][j];
+    float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    mma_bf16(d, p0, h0, p1, h1, prmt(x.x, x.z, 0x5410), prmt(x.x, x.z, 0x7632));
+    mma_bf16(d, p2, h2, p3, h3, prmt(x.y, x.w, 0x5410), prmt(x.y, x.w, 0x7632));
+    acc[t][0] = fmaf(d[0], sl, acc[t][0]);
+    acc[t][1] = fmaf(d[1], sl, acc[t][1]);
+    acc[t][2] = fmaf(d[2], sh, acc[t][2]);
+    acc[t][3] = fmaf(d[3], sh, acc[t][3]);
+  }
+}
+
 template <int FMT, int NT, int MODE>
-__global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) gemv_mma_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kWarps * 32, NT <= 2 ? 3 : 2) gemv_mma_kernel(const __grid_constant__ Params p) {
   using S = Stage<FMT>;
-  __shared__ __align__(16) float red[kWarps][kTileRows][8 * NT];
+  constexpr int kRedBufs = NT <= 2 ? 2 : 1;  // partial-sum buffers (alternate tiles)
+  __shared__ __align__(16) float red[kRedBufs][kWarps][kTileRows][8 * NT];
   extern __shared__ __align__(128) uint8_t dsm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -264,49 +299,54 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) 
   const int ng = max(0, min(p.groups, gb + p.gpw) - gb);     // groups in the slice
   const int nchunks = max(1, (ng + kChunk - 1) / kChunk);    // a warp with no groups still steps
 
-  // Copy side.  Lane l always copies tile row cr = l & 15; lanes 0-15 and
-  // 16-31 take alternate 16-byte pieces of the row's chunk, so each copy
-  // instruction writes 512 contiguous bytes of shared memory.  The copy runs
-  // kDepth items ahead of the math and crosses tile boundaries.
-  const int cr = lane & 15, ch = lane >> 4;
+  // Copy side.  Copy instruction i moves rows r = rs + R * i of the chunk
+  // (rs = lane / kPieces, R = 32 / kPieces rows per instruction), lane piece
+  // h = lane % kPieces: every instruction reads whole 128-byte lines.  The
+  // copy runs kDepth items ahead of the math and crosses tile boundaries.
+  constexpr int kRowsPerCopy = 32 / S::kPieces;                  // 4 (int4) or 2 (int8)
+  const int h = lane % S::kPieces, rs = lane / S::kPieces;
   int i_tile = blockIdx.x, i_c = 0, i_slot = 0;
-  const uint8_t* wrow = nullptr;
-  const uint8_t* srow = nullptr;
+  const uint8_t* wlo = nullptr;  // row rs of the tile's low half, at this warp's slice
+  const uint8_t* whi = nullptr;  // row rs of the high half
+  const uint8_t* srow = nullptr; // int4 scales of row (lane & 15)
   auto set_rows = [&](int y) {
     const TileRows tr = tile_rows<MODE>(p, y);
-    const int job = cr < 8 ? tr.job_lo : tr.job_hi;
-    const int row = cr < 8 ? tr.row_lo + cr : tr.row_hi + cr - 8;
-    wrow = p.w[job] + int64_t(row) * row_bytes + int64_t(gb) * S::kBPG;
-    if constexpr (FMT == 0)
+    wlo = p.w[tr.job_lo] + int64_t(tr.row_lo + rs) * row_bytes + int64_t(gb) * S::kBPG;
+    whi = p.w[tr.job_hi] + int64_t(tr.row_hi + rs) * row_bytes + int64_t(gb) * S::kBPG;
+    if constexpr (FMT == 0) {
+      const int r = lane & 15;
+      const int job = r < 8 ? tr.job_lo : tr.job_hi;
+      const int row = r < 8 ? tr.row_lo + r : tr.row_hi + r - 8;
       srow = static_cast<const uint8_t*>(p.s[job]) + (int64_t(row) * p.groups + gb) * 2;
+    }
   };
   if (i_tile < p.tiles) set_rows(i_tile);
   auto issue = [&]() {
     if (i_tile < p.tiles) {
       const int nj = min(kChunk, ng - i_c * kChunk);  // <= 0 for a warp with no groups
       uint8_t* dst = ring + i_slot * S::kBytes;
+      const int64_t coff = int64_t(i_c) * S::kRowBytes + h * 16;
+      if ((h * 16) / S::kBPG < nj) {
+#pragma unroll
+        for (int i = 0; i < kTileRows / kRowsPerCopy; ++i) {
+          const int r = rs + kRowsPerCopy * i;
+          const int rh = i < kTileRows / kRowsPerCopy / 2 ? kRowsPerCopy * i : kRowsPerCopy * i - 8;
+          const uint8_t* base = i < kTileRows / kRowsPerCopy / 2 ? wlo : whi;
+          cp_async16(dst + piece_off<FMT>(r, h), base + int64_t(rh) * row_bytes + coff);
+        }
+      }
       if constexpr (FMT == 0) {
-        const uint8_t* src = wrow + i_c * (kChunk * 16);
-#pragma unroll
-        for (int i = 0; i < kChunk / 2; ++i) {
-          const int h = ch + 2 * i;
-          if (h < nj) cp_async16(dst + (h * kTileRows + cr) * 16, src + h * 16);
-        }
-        // Scales as bf16 pairs (the slice start and nj are even).
         const uint8_t* ssrc = srow + i_c * (kChunk * 2);
+        uint8_t* sdst = dst + S::kW + (lane & 15) * (kChunk * 2);
+        if (p.scale16) {
+          if (lane < 16 && nj > 0) cp_async16(sdst, ssrc);
+        } else {
+          // bf16 pairs: the slice start and nj are even.
 #pragma unroll
-        for (int i = 0; i < (kChunk / 2 + 1) / 2; ++i) {
-          const int pr = ch + 2 * i;
-          if (2 * pr < nj) cp_async4(dst + S::kW + cr * (kChunk * 2) + pr * 4, ssrc + pr * 4);
-        }
-      } else {
-        const uint8_t* src = wrow + i_c * (kChunk * 32);
-        const int sw = (cr >> 2) & 1;
-#pragma unroll
-        for (int i = 0; i < kChunk; ++i) {
-          const int pc = ch + 2 * i;
-          if ((pc >> 1) < nj)
-            cp_async16(dst + ((pc >> 1) * kTileRows + cr) * 32 + (((pc & 1) ^ sw) * 16), src + pc * 16);
+          for (int i = 0; i < kChunk / 4; ++i) {
+            const int pr = (lane >> 4) + 2 * i;
+            if (2 * pr < nj) cp_async4(sdst + pr * 4, ssrc + pr * 4);
+          }
         }
       }
       if (++i_c == nchunks) {
@@ -316,7 +356,7 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) 
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
-    i_slot = (i_slot + 1) & (S::kDepth - 1);
+    i_slot = i_slot + 1 == S::kDepth ? 0 : i_slot + 1;
   };
 
   pdl_trigger();
@@ -331,7 +371,7 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) 
   for (int t = 0; t < NT; ++t)
     xbase[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k + int64_t(gb) * 32 + (FMT == 0 ? 8 * q : 4 * q);
   const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix mi, row rr
-  int slot = 0;
+  int slot = 0, buf = 0;
 
   for (int y = blockIdx.x; y < p.tiles; y += gridDim.x) {
     float acc[NT][4];
@@ -343,46 +383,55 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) 
       const uint8_t* st = ring + slot * S::kBytes;
       const int nj = min(kChunk, ng - c * kChunk);
       if constexpr (FMT == 0) {
+        if (NT == 1 && nj == kChunk) {
+          // Full chunk, in halves of four groups: every shared-memory and x
+          // load of the half first, then the math with no branches, so that
+          // the groups' chains interleave.
 #pragma unroll
-        for (int j = 0; j < kChunk; j += 2) {
-          if (j < nj) {  // nj is even
-            uint32_t f[4];
-            ldsm_x4(f, st + ((j + (mi >> 1)) * kTileRows + (mi & 1) * 8 + rr) * 16);
-            const uint32_t slo = lds32(st + S::kW + g * (kChunk * 2) + j * 2);
-            const uint32_t shi = lds32(st + S::kW + (g + 8) * (kChunk * 2) + j * 2);
+          for (int hb = 0; hb < kChunk; hb += 4) {
+            uint32_t f[2][4], sp[2][2];
+            uint4 xv[NT][4];
 #pragma unroll
-            for (int jj = 0; jj < 2; ++jj) {
-              const uint32_t ul = f[2 * jj], uh = f[2 * jj + 1];
-              const uint32_t p0 = int4_pair(ul, 0), p1 = int4_pair(ul, 1), p2 = int4_pair(ul, 2),
-                             p3 = int4_pair(ul, 3);
-              const uint32_t h0 = int4_pair(uh, 0), h1 = int4_pair(uh, 1), h2 = int4_pair(uh, 2),
-                             h3 = int4_pair(uh, 3);
-              const float sl = __uint_as_float(jj ? (slo & 0xFFFF0000u) : (slo << 16));
-              const float sh = __uint_as_float(jj ? (shi & 0xFFFF0000u) : (shi << 16));
-              const int gi = c * kChunk + j + jj;  // group within the slice
+            for (int j2 = 0; j2 < 2; ++j2) {
+              ldsm_x4(f[j2], st + piece_off<0>((mi & 1) * 8 + rr, hb + 2 * j2 + (mi >> 1)));
+              sp[j2][0] = lds32(st + S::kW + g * (kChunk * 2) + (hb + 2 * j2) * 2);
+              sp[j2][1] = lds32(st + S::kW + (g + 8) * (kChunk * 2) + (hb + 2 * j2) * 2);
+            }
 #pragma unroll
-              for (int t = 0; t < NT; ++t) {
-                const uint4 xv = ldg16(xbase[t] + gi * 32);
-                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                mma_bf16(d, p0, h0, p1, h1, prmt(xv.x, xv.z, 0x5410), prmt(xv.x, xv.z, 0x7632));
-                mma_bf16(d, p2, h2, p3, h3, prmt(xv.y, xv.w, 0x5410), prmt(xv.y, xv.w, 0x7632));
-                acc[t][0] = fmaf(d[0], sl, acc[t][0]);
-                acc[t][1] = fmaf(d[1], sl, acc[t][1]);
-                acc[t][2] = fmaf(d[2], sh, acc[t][2]);
-                acc[t][3] = fmaf(d[3], sh, acc[t][3]);
+            for (int t = 0; t < NT; ++t)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) xv[t][j] = ldg16(xbase[t] + (c * kChunk + hb + j) * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              int4_group<NT>(acc, f[j >> 1][2 * (j & 1)], f[j >> 1][2 * (j & 1) + 1], sp[j >> 1][0],
+                             sp[j >> 1][1], j & 1, xv, j);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < kChunk; j += 2) {
+            if (j < nj) {  // nj is even
+              uint32_t f[4];
+              ldsm_x4(f, st + piece_off<0>((mi & 1) * 8 + rr, j + (mi >> 1)));
+              const uint32_t slo = lds32(st + S::kW + g * (kChunk * 2) + j * 2);
+              const uint32_t shi = lds32(st + S::kW + (g + 8) * (kChunk * 2) + j * 2);
+#pragma unroll
+              for (int jj = 0; jj < 2; ++jj) {
+                uint4 xg[NT][1];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) xg[t][0] = ldg16(xbase[t] + (c * kChunk + j + jj) * 32);
+                int4_group<NT>(acc, f[2 * jj], f[2 * jj + 1], slo, shi, jj, xg, 0);
               }
             }
           }
         }
       } else {
-        const int swr = (rr >> 2) & 1;
 #pragma unroll
         for (int j = 0; j < kChunk; ++j) {
           if (j < nj) {
             const int gi = c * kChunk + j;
             // int8: a group is 32 B per row = two 16 B halves, one k16 step each.
             uint32_t f[4];
-            ldsm_x4(f, st + (j * kTileRows + (mi & 1) * 8 + rr) * 32 + (((mi >> 1) ^ swr) * 16));
+            ldsm_x4(f, st + piece_off<1>((mi & 1) * 8 + rr, 2 * j + (mi >> 1)));
 #pragma unroll
             for (int s2 = 0; s2 < 2; ++s2) {
               const uint32_t ul = f[2 * s2] ^ 0x80808080u, uh = f[2 * s2 + 1] ^ 0x80808080u;
@@ -401,9 +450,10 @@ __global__ void __launch_bounds__(kWarps * 32, NT == 1 ? 4 : (NT == 2 ? 3 : 2)) 
       }
       __syncwarp();
       issue();  // refills the stage just read
-      slot = (slot + 1) & (S::kDepth - 1);
+      slot = slot + 1 == S::kDepth ? 0 : slot + 1;
     }
-    finish_tile<FMT, NT, MODE>(p, tile_rows<MODE>(p, y), red, acc, warp, g, q, tid);
+    finish_tile<FMT, NT, MODE, kRedBufs == 1>(p, tile_rows<MODE>(p, y), red[buf], acc, warp, g, q, tid);
+    buf = kRedBufs == 1 ? 0 : buf ^ 1;
   }
   cp_async_wait<0>();
 }
@@ -502,6 +552,10 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
   const int groups = b.k / 32;
   int gpw = (groups + kWarps - 1) / kWarps;
   gpw += gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
+  // Whole 8-group slices (K a multiple of 2048): each row's scales of a chunk
+  // are one aligned 16-byte copy.
+  bool scale16 = fmt == 0 && groups % (8 * kWarps) == 0;
+  for (int j = 0; j < b.njobs && scale16; ++j) scale16 = (reinterpret_cast<uintptr_t>(b.jobs[j].s) & 15) == 0;
   int rows = 0;
   switch (a.mode) {
     case GemvMode::Plain:
@@ -531,6 +585,7 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
     p.qkv = a.qkv;
     p.m_base = m0;
     p.tiles = blocks;
+    p.scale16 = scale16 ? 1 : 0;
     if (a.mode == GemvMode::QkvRope) {
       const QkvExtra& e = a.qkv;
       p.qkv.pos = e.pos + m0;

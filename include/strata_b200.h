@@ -98,6 +98,17 @@ int32_t strata_b200_linear_w8pc(const uint16_t *x, int64_t m, int64_t k,
                                 int64_t n, const uint16_t *residual,
                                 uint16_t *y, void *stream);
 
+/* y[m, n] = sum_k x[m, k] * w[n, k]  (+ residual[m, n] when non-null) with
+ * bf16 weights [n, k]: the reference's f32 `linear` (crates/ferrite-strata-cpu/
+ * src/backend.rs:607-637) in bf16 storage with f32 accumulation.  k must be a
+ * multiple of 8.  Batches of more than 64 rows run on the tcgen05 tensor cores
+ * (so do the int4 and int8 entry points above, after expanding the weights
+ * into a stream-ordered temporary). */
+int32_t strata_b200_linear_bf16(const uint16_t *x, int64_t m, int64_t k,
+                                const uint16_t *w, int64_t n,
+                                const uint16_t *residual, uint16_t *y,
+                                void *stream);
+
 int32_t strata_b200_rms_norm_bf16(const uint16_t *x, const uint16_t *gamma,
                                   int64_t rows, int64_t cols, float eps,
                                   uint16_t *y, void *stream);

@@ -24,6 +24,7 @@ def lib(cuda):
         "strata_b200_dequant_w8pc": [P, P, I64, I64, P, P],
         "strata_b200_linear_w4g32": [P, I64, I64, P, P, I64, P, P, P],
         "strata_b200_linear_w8pc": [P, I64, I64, P, P, I64, P, P, P],
+        "strata_b200_linear_bf16": [P, I64, I64, P, I64, P, P, P],
         "strata_b200_rms_norm_bf16": [P, P, I64, I64, F, P, P],
         "strata_b200_rope_bf16": [P, P, I64, I64, I64, F, P, P],
         "strata_b200_swiglu_bf16": [P, P, I64, P, P],
@@ -141,6 +142,28 @@ def test_linear_ragged_shapes(cuda, lib, fmt, m, n, k):
     torch.cuda.synchronize()
     got = ora.from_bf16(y.cpu().numpy().view(np.uint16))
     assert_close(got, ora.round_bf16(want), TOL_BF16, f"{fmt} m={m} n={n} k={k}")
+
+
+@pytest.mark.parametrize("m,n,k", [(65, 256, 64), (128, 4096, 4096), (1000, 300, 136), (2048, 512, 4096),
+                                   (300, 2560, 1000)])
+@pytest.mark.parametrize("residual", [False, True])
+def test_linear_bf16_tensor_core_gemm(cuda, lib, m, n, k, residual):
+    """More than 64 rows: the tcgen05 GEMM (ragged M, N and K tails, residual epilogue),
+    against a float64 product of the same bf16 inputs."""
+    torch = cuda
+    x = ora.to_bf16(ora.normal(31, (m, k)))
+    w = ora.to_bf16(ora.normal(32, (n, k), std=0.05))
+    r = ora.to_bf16(ora.normal(33, (m, n))) if residual else None
+    xd, wd = dev(torch, x.view(np.int16)), dev(torch, w.view(np.int16))
+    rd = dev(torch, r.view(np.int16)) if residual else None
+    y = torch.empty((m, n), dtype=torch.int16, device="cuda")
+    ok(lib.strata_b200_linear_bf16(ptr(xd), m, k, ptr(wd), n, ptr(rd), ptr(y), stream(torch)))
+    torch.cuda.synchronize()
+    got = ora.from_bf16(y.cpu().numpy().view(np.uint16))
+    want = ora.from_bf16(x).astype(np.float64) @ ora.from_bf16(w).astype(np.float64).T
+    if residual:
+        want = ora.round_bf16(want.astype(np.float32)) + ora.from_bf16(r)
+    assert_close(got, ora.round_bf16(np.asarray(want, np.float32)), TOL_BF16, f"bf16 gemm m={m} n={n} k={k}")
 
 
 @pytest.mark.parametrize("m", [1, 16, 128])
