@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(kThreads)
 
   int pre = 0;  // rows staged before the wait
   int p_early = -1;
-  if (pos_external) {
+  if (pos_external && tokens_per_seq == 1) {
     p_early = pos[row];
     if (p_early >= 0 && p_early < max_len) {
       pre = min(CH, max(0, p_early - t_begin));
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   pdl_wait();
-  const int p = pos_external ? p_early : pos[row];
+  const int p = pos_external && tokens_per_seq == 1 ? p_early : pos[row];
   const bool bad = p < 0 || p >= max_len;
   if (bad && tid == 0 && err) atomicExch(err, 2);
   const int len = bad ? 0 : p + 1;
@@ -546,6 +546,9 @@ int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16
                         int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
                         float* scratch, uint16_t* out, int* err, cudaStream_t st) {
   if (rows == 0) return SB_OK;
+  if (tensor_core_attention_enabled() && attention_prefill_supported(rows, tokens_per_seq, heads, kv_heads, head_dim))
+    return launch_attention_prefill(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim,
+                                    max_len, out, err, st);
   if (tensor_core_attention_enabled() && attention_tc_supported(heads, kv_heads, head_dim))
     return launch_attention_tc(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim, max_len,
                                pos_external, scratch, out, err, st);

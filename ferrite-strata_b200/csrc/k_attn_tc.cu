@@ -18,10 +18,11 @@
 // (max, sum, unnormalised O) partial as the CUDA-core kernel, which
 // attn_merge_kernel combines across splits.
 //
-// Cache rows below the row's position are final before this kernel starts,
-// so when positions are a graph input the first slabs below the position are
-// requested before griddepcontrol.wait and stream in while the previous kernel
-// (the q/k/v projection that writes row `pos`) finishes.
+// In a decode step (one token per sequence) the cache rows below the row's
+// position were written by earlier steps, so when positions are a graph input
+// the first slabs below the position are requested before griddepcontrol.wait
+// and stream in while the previous kernel (the q/k/v projection that writes
+// row `pos`) finishes.
 #include "common.cuh"
 #include "k_elem.cuh"
 
@@ -124,7 +125,7 @@ __global__ void __launch_bounds__(kTcWarps * 32)
 
   // Before the wait: slabs entirely below the row's position.
   int issued = 0;
-  if (pos_external) {
+  if (pos_external && tokens_per_seq == 1) {
     const int p_early = pos[row];
     if (p_early > 0 && p_early < max_len) {
       const int lim_pre = min(p_early, t0 + span);

@@ -476,6 +476,27 @@ int launch_argmax(const T* x, int64_t rows, int64_t cols, int32_t* out, cudaStre
   return SB_OK;
 }
 
+template <typename T>
+__global__ void last_rows_kernel(const T* __restrict__ x, int64_t batch, int64_t tps, int64_t cols,
+                                 T* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t total = batch * cols;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t b = i / cols, c = i - b * cols;
+    out[i] = x[(b * tps + tps - 1) * cols + c];
+  }
+}
+
+template <typename T>
+int launch_last_rows(const T* x, int64_t batch, int64_t tokens_per_seq, int64_t cols, T* out, cudaStream_t st) {
+  if (batch == 0 || cols == 0) return SB_OK;
+  launch_pdl(last_rows_kernel<T>, dim3(grid_for(batch * cols)), dim3(256), 0, st, x, batch, tokens_per_seq, cols,
+             out);
+  SB_LAUNCH_CHECK();
+  return SB_OK;
+}
+
 int launch_gemm_f32(const float* a, const float* b, const float* bias, int64_t m, int64_t k,
                     int64_t n, bool b_is_nk, float* c, cudaStream_t st) {
   if (m == 0 || n == 0) return SB_OK;
@@ -495,6 +516,7 @@ int launch_convert(int dir, const void* x, int64_t n, void* y, cudaStream_t st) 
 }
 
 #define SB_INST(T)                                                                              \
+  template int launch_last_rows<T>(const T*, int64_t, int64_t, int64_t, T*, cudaStream_t);       \
   template int launch_rms_norm<T>(const T*, const T*, int64_t, int64_t, float, T*, cudaStream_t); \
   template int launch_rope<T>(const T*, const int32_t*, int64_t, int64_t, int64_t, double, T*,  \
                               cudaStream_t);                                                   \

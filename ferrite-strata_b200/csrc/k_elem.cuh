@@ -48,6 +48,9 @@ int launch_embed(const int32_t* ids, int64_t rows, const T* table, int64_t vocab
                  T* out, int* err, cudaStream_t st);
 template <typename T>
 int launch_argmax(const T* x, int64_t rows, int64_t cols, int32_t* out, cudaStream_t st);
+// out[b] = x[b * tokens_per_seq + tokens_per_seq - 1]: each sequence's last row.
+template <typename T>
+int launch_last_rows(const T* x, int64_t batch, int64_t tokens_per_seq, int64_t cols, T* out, cudaStream_t st);
 int launch_gemm_f32(const float* a, const float* b, const float* bias, int64_t m, int64_t k,
                     int64_t n, bool b_is_nk, float* c, cudaStream_t st);
 // dir 0: f32 -> bf16, dir 1: bf16 -> f32
@@ -85,6 +88,13 @@ int launch_attention_tc(const uint16_t* q, const uint16_t* k_cache, const uint16
                         int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
                         int64_t max_len, bool pos_external, float* scratch, uint16_t* out, int* err,
                         cudaStream_t st);
+// Prefill attention (k_attn_prefill.cu): 64-row query tiles of one sequence;
+// launch_attention_v2 uses it for 16 or more tokens per sequence.
+bool attention_prefill_supported(int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads,
+                                 int64_t head_dim);
+int launch_attention_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
+                             int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                             int64_t max_len, uint16_t* out, int* err, cudaStream_t st);
 int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t heads, int64_t head_dim, int splits,
                                 uint16_t* out, cudaStream_t st);
 

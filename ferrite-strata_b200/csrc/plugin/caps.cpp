@@ -43,6 +43,7 @@ const PatternRule kRules[] = {
     {"fused::embed", true, true, true, false, false, false},
     {"fused::argmax", true, false, false, true, false, false},
     {"fused::all_reduce", true, true, true, false, false, false},
+    {"fused::last_token", true, true, true, false, false, false},
     {"fused::quantize_w4g32", true, false, false, false, true, false},
     {"fused::quantize_w8pc", true, false, false, false, false, true},
     {"fused::dequantize_w4g32", true, true, false, false, false, false},

@@ -211,7 +211,27 @@ struct Lowerer {
       if (!lower_node(int(i))) return false;
     }
     fuse_qkv_rope();
+    plan_gemm_scratch();
     return true;
+  }
+
+  // Linear steps over more than kGemvMaxRows rows run as tcgen05 GEMMs over
+  // bf16 weights: scratch for one job's expanded weights [n, k] and, for a
+  // SwiGLU pair, the gate and up products [m, n] that the SwiGLU kernel joins.
+  void plan_gemm_scratch() {
+    for (Step& st : exe.steps) {
+      if (st.kind != SK::Linear || st.i[0] <= sb::kGemvMaxRows) continue;
+      uint64_t wmax = 0, n0 = 0;
+      for (int j = 0; j < st.njobs; ++j) {
+        const Value& wv = g.values[st.v[1 + 4 * j]];
+        const uint64_t n = uint64_t(wv.dims[0]);
+        if (j == 0) n0 = n;
+        wmax = std::max<uint64_t>(wmax, n * uint64_t(st.i[1]) * 2);
+      }
+      uint64_t bytes = (wmax + 255) / 256 * 256;
+      if (st.epi == sb::Epilogue::SwiGLU) bytes += 2 * ((uint64_t(st.i[0]) * n0 * 2 + 255) / 256 * 256);
+      st.scratch_bytes = bytes;
+    }
   }
 
   // q/k/v linears of one x whose outputs feed only rope(q), rope(k) and one
@@ -229,8 +249,8 @@ struct Lowerer {
     for (size_t si = 0; si < exe.steps.size(); ++si) {
       Step& L = exe.steps[si];
       if (L.kind != SK::Linear || L.njobs != 3 || L.epi != sb::Epilogue::None ||
-          (L.fmt != sb::WFormat::W4G32 && L.fmt != sb::WFormat::W8PC))
-        continue;
+          (L.fmt != sb::WFormat::W4G32 && L.fmt != sb::WFormat::W8PC) || L.i[0] > sb::kGemvMaxRows)
+        continue;  // prefill-sized batches keep separate GEMM, rope and append steps
       const uint32_t yq = L.v[3], yk = L.v[7], yv = L.v[11];
       if (cons[yq].size() != 1 || cons[yk].size() != 1 || cons[yv].size() != 1) continue;
       const int rq = cons[yq][0], rk = cons[yk][0], an = cons[yv][0];
@@ -659,7 +679,11 @@ struct Lowerer {
       st.i[3] = KVH;
       st.i[4] = D;
       st.i[5] = L;
-      st.i[6] = V(pos).producer < 0 ? 1 : 0;  // positions come from the host, not a kernel
+      // Positions from the host and one token per sequence: cache rows below
+      // the position were written by earlier steps, so the attention kernel may
+      // stream them before the previous kernel finishes.  With several tokens
+      // per sequence this step's own append writes those rows.
+      st.i[6] = V(pos).producer < 0 && rows / B == 1 ? 1 : 0;
       st.scratch_bytes = is_bf16(dt) ? sb::attention_v2_scratch_bytes(rows, H, KVH, D, L)
                                      : sb::attention_scratch_bytes(rows, H, KVH, D, L);
       st.v = {q, kc, vc, pos, out};
@@ -689,6 +713,21 @@ struct Lowerer {
       st.bf16 = is_bf16(V(x).dt);
       st.i[0] = rows_of(V(x));
       st.i[1] = last_dim(V(x));
+      st.v = {x, out};
+      st.reads = {x};
+      st.writes = {out};
+    } else if (p == "fused::last_token") {
+      const uint32_t x = in(n, 0);
+      if (!float_unary_ok(x, out)) return decline("last_token needs f32 or bf16");
+      const int64_t R = rows_of(V(x)), B = rows_of(V(out));
+      if (B <= 0 || R % B || last_dim(V(x)) != last_dim(V(out)) ||
+          n.attr_int("tokens_per_seq", R / B) != R / B)
+        fail(STRATA_INVALID_ARGUMENT, "last_token maps [batch * tokens, C] to [batch, C]");
+      st.kind = SK::LastToken;
+      st.bf16 = is_bf16(V(x).dt);
+      st.i[0] = B;
+      st.i[1] = R / B;
+      st.i[2] = last_dim(V(x));
       st.v = {x, out};
       st.reads = {x};
       st.writes = {out};
@@ -894,6 +933,8 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
                                  P<T>(p, st.v[2]), ctx.d_err, s);
     case SK::Argmax:
       return sb::launch_argmax<T>(P<T>(p, st.v[0]), st.i[0], st.i[1], P<int32_t>(p, st.v[1]), s);
+    case SK::LastToken:
+      return sb::launch_last_rows<T>(P<T>(p, st.v[0]), st.i[0], st.i[1], st.i[2], P<T>(p, st.v[1]), s);
     case SK::KvAppend:
       return sb::launch_kv_append<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]), P<T>(p, st.v[3]),
                                      P<int32_t>(p, st.v[4]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
@@ -912,6 +953,37 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
     default:
       return SB_INTERNAL;
   }
+}
+
+// A prefill-sized Linear step: per job, expand the weights to bf16 in the
+// step's scratch and run the tcgen05 GEMM (int8 scales in its epilogue); a
+// SwiGLU pair writes gate and up to scratch and joins them with the SwiGLU
+// kernel.
+int enqueue_gemm(Ctx& ctx, Exe& exe, const Step& st, const sb::LinearBatch& b, cudaStream_t s) {
+  char* base = static_cast<char*>(exe.ws) + st.scratch_off;
+  uint64_t wmax = 0;
+  for (int j = 0; j < b.njobs; ++j) wmax = std::max<uint64_t>(wmax, uint64_t(b.jobs[j].n) * uint64_t(b.k) * 2);
+  uint16_t* wbf = reinterpret_cast<uint16_t*>(base);
+  char* tmp = base + (wmax + 255) / 256 * 256;
+  const uint64_t prod = (uint64_t(b.m) * uint64_t(b.jobs[0].n) * 2 + 255) / 256 * 256;
+  uint16_t* outs[sb::kMaxJobs] = {};
+  for (int j = 0; j < b.njobs; ++j) {
+    const sb::LinearJob& J = b.jobs[j];
+    outs[j] = st.epi == sb::Epilogue::SwiGLU ? reinterpret_cast<uint16_t*>(tmp + j * prod) : J.y;
+    if (!outs[j]) continue;
+    if (!sb::gemm_tc_supported(b.m, J.n, b.k, b.x, wbf))
+      fail(STRATA_INTERNAL, "linear `" + st.label + "` has a layout the tensor-core GEMM cannot take");
+    int rc = sb::launch_codes_to_bf16(J.w, J.s, b.fmt == sb::WFormat::W8PC ? 1 : 0, J.n, b.k, wbf, s);
+    if (rc) return rc;
+    rc = sb::launch_gemm_tc_bf16(b.x, b.m, b.k, wbf, J.n,
+                                 b.fmt == sb::WFormat::W8PC ? static_cast<const float*>(J.s) : nullptr,
+                                 st.epi == sb::Epilogue::SwiGLU ? nullptr : J.residual, J.ldr, outs[j], J.ldy,
+                                 ctx.d_err, s);
+    if (rc) return rc;
+  }
+  if (st.epi == sb::Epilogue::SwiGLU)
+    return sb::launch_swiglu<uint16_t>(outs[0], outs[1], int64_t(b.m) * b.jobs[0].n, b.jobs[0].y, s);
+  return SB_OK;
 }
 
 }  // namespace
@@ -935,6 +1007,10 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
           const Value& wv = exe.g.values[w];
           const int n = int(wv.dims[0]);
           b.jobs[j] = sb::LinearJob{p.at(w), p.at(sc), n, P<uint16_t>(p, y), n, P<uint16_t>(p, r), n};
+        }
+        if (st.scratch_bytes) {
+          rc = enqueue_gemm(ctx, exe, st, b, s);
+          break;
         }
         sb::GemvMmaArgs ga{};
         ga.lb = b;

@@ -159,6 +159,8 @@ void Ctx::check_device_error(const char* where) {
   cuda_check(cudaMemcpy(&word, d_err, sizeof(int), cudaMemcpyDeviceToHost), "reading the error word");
   if (word) {
     cuda_check(cudaMemset(d_err, 0, sizeof(int)), "clearing the error word");
+    if (word == 4)
+      fail(STRATA_INTERNAL, std::string(where) + ": a tensor-core pipeline wait ran out (the kernel stopped early)");
     const char* what = word == 2 ? "a position is outside the KV cache"
                      : word == 3 ? "a token id is outside the embedding table"
                                  : "a kernel rejected its input";

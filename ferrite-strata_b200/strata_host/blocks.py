@@ -19,6 +19,7 @@ fused::attention            q [R,H*d], k [R,G*d], v [R,G*d],           num_heads
 fused::embed                ids I32 [R], table [V,D]
 fused::argmax               x [R,C] -> I32 [R] (lowest index on ties)
 fused::all_reduce           x -> sum of x over the tensor-parallel group
+fused::last_token           x [B*S,C] -> [B,C], each sequence's last row  tokens_per_seq
 ==========================  =========================================  ====================
 
 ``fused::attention`` appends row r's k/v at ``pos[r]`` of sequence
@@ -109,12 +110,13 @@ def _linear(b: GraphBuilder, x: int, W: dict, key: str, m: int, n: int, fmt: str
 def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fmt: str = "w4g32",
                   layers: int | None = None, embed: bool = True, head: str = "argmax",
                   lm_fmt: str | None = None, tp_rank: int = 0, tp_world: int = 1,
-                  name: str = "decoder"):
+                  last_token: bool = False, name: str = "decoder"):
     """One forward step of ``layers`` decoder blocks over ``batch * seq`` rows.
 
     ``seq == 1`` is a decode step; ``seq > 1`` a prefill from position 0 (the
     caller fills ``pos``).  ``head``: "argmax" (next-token ids), "logits", or
-    "none" (the last hidden state is the output).
+    "none" (the last hidden state is the output).  ``last_token`` runs the
+    head on each sequence's last row only (prefill logits for the next token).
     """
     layers = shape.layers if layers is None else layers
     act = F32 if fmt == "f32" else BF16
@@ -183,14 +185,19 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
     if head == "none":
         hd.out = h
     else:
-        hf = b.node(Op.custom("fused::rms_norm"), [h, hd.final_norm], [(act, (R, D))],
+        Rh = R
+        if last_token:
+            h = b.node(Op.custom("fused::last_token"), [h], [(act, (batch, D))], {"tokens_per_seq": seq},
+                       "last_token")[0]
+            Rh = batch
+        hf = b.node(Op.custom("fused::rms_norm"), [h, hd.final_norm], [(act, (Rh, D))],
                     {"eps": float(shape.eps)}, "final_norm_op")[0]
         W = {"wlm": hd.lm_w, "slm": hd.lm_s}
-        logits = _linear(b, hf, W, "lm", R, shape.vocab, lm_fmt or fmt, act, "lm_head")
+        logits = _linear(b, hf, W, "lm", Rh, shape.vocab, lm_fmt or fmt, act, "lm_head")
         if head == "logits":
             hd.out = logits
         else:
-            hd.out = b.node(Op.custom("fused::argmax"), [logits], [(I32, (R,))], {}, "argmax")[0]
+            hd.out = b.node(Op.custom("fused::argmax"), [logits], [(I32, (Rh,))], {}, "argmax")[0]
     b.output(hd.out)
     return b.build(), hd
 

@@ -110,6 +110,10 @@ def evaluate(graph, inputs: dict, all_reduce=None) -> dict:
             res, _rc = ora.embed(ins[0], ins[1])
         elif pid == "fused::argmax":
             res = ora.argmax(ins[0])
+        elif pid == "fused::last_token":
+            B = graph.values[n.outputs[0]].dims[0]
+            x = ins[0].reshape(B, -1, ins[0].shape[-1])
+            res = x[:, -1, :]
         elif pid == "fused::all_reduce":
             res = ins[0] if all_reduce is None else all_reduce(n.name, ins[0])
         elif pid == "fused::quantize_w4g32":

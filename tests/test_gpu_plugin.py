@@ -8,7 +8,7 @@ import pytest
 
 from oracle import graph_eval, oracle as ora
 from strata_host import BF16, F32, I32, W4G32, Device, GraphBuilder, Op, StrataError, w8pc
-from strata_host.blocks import BLOCK_512, LLAMA_7B, LLAMA_70B, decoder_graph
+from strata_host.blocks import BLOCK_512, LLAMA_7B, LLAMA_70B, DecoderShape, decoder_graph
 from tests.helpers import TOL_BF16, TOL_F32, assert_close, seeded_graph_inputs, to_device_bytes
 
 pytestmark = pytest.mark.gpu
@@ -172,6 +172,46 @@ def test_llama7b_shape_argmax_is_exact_on_device_logits(cuda, plugin):
     assert np.array_equal(np.asarray(res[hd.out]), ora.argmax(logits))
     ref = graph_eval.evaluate(g, host)
     assert_close(logits, ref[logits_id], TOL_BF16, "lm_head logits")
+
+
+@pytest.mark.parametrize("fmt,kv_heads", [("w8pc", 8), ("w4g32", 8), ("w8pc", 2)])
+def test_prefill_runs_tensor_core_gemms_and_matches_oracle(cuda, plugin, fmt, kv_heads):
+    """A prefill step (2 sequences x 96 tokens from position 0 = 192 rows): the
+    linears run as tcgen05 GEMMs, rope / KV append as their own steps, causal
+    attention on the prefill kernel (a partial second 64-row query tile; MHA and
+    4:1 GQA).  A narrower decoder than 7B (hidden 1024, 8 heads x 128, FFN 2816)
+    keeps the oracle's run short; the layer structure is the same."""
+    shape = DecoderShape(1024, 8, kv_heads, 128, 2816, 512, 2)
+    batch, seq = 2, 96
+    g, hd = decoder_graph(shape, batch=batch, seq=seq, max_len=128, fmt=fmt, head="logits")
+    host = seeded_graph_inputs(g, cache_fill=0)
+    host[hd.tokens] = ora.uniform_i32(2, batch * seq, 0, shape.vocab)
+    host[hd.pos] = np.tile(np.arange(seq, dtype=np.int32), batch)
+    res, caches = run_graph(plugin, g, host)
+    ref = graph_eval.evaluate(g, {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in host.items()})
+    assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, f"prefill logits ({fmt})")
+    for i, raw in caches.items():
+        got = ora.from_bf16(np.frombuffer(raw, np.uint16).reshape(g.values[i].dims))
+        assert_close(got, ref[i], TOL_BF16, g.values[i].name)
+
+
+def test_prefill_last_token_head_runs_on_each_sequence_last_row(cuda, plugin):
+    """fused::last_token: the prefill head (final norm, lm_head, argmax) runs on
+    each sequence's last row only, giving the next token of every prompt."""
+    shape = DecoderShape(1024, 8, 8, 128, 2816, 512, 1)
+    batch, seq = 3, 80
+    g, hd = decoder_graph(shape, batch=batch, seq=seq, max_len=96, fmt="w8pc", head="argmax", last_token=True)
+    logits_id = g.nodes[-1].inputs[0]
+    g.outputs.append(logits_id)
+    host = seeded_graph_inputs(g, cache_fill=0)
+    host[hd.tokens] = ora.uniform_i32(2, batch * seq, 0, shape.vocab)
+    host[hd.pos] = np.tile(np.arange(seq, dtype=np.int32), batch)
+    res, _ = run_graph(plugin, g, host)
+    ref = graph_eval.evaluate(g, {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in host.items()})
+    assert g.values[logits_id].dims == (batch, shape.vocab)
+    logits = as_f32(g.values[logits_id], res[logits_id])
+    assert_close(logits, ref[logits_id], TOL_BF16, "last-token logits")
+    assert np.array_equal(np.asarray(res[hd.out]), ora.argmax(logits))
 
 
 def test_llama70b_gqa_shard_decode(cuda, plugin):
