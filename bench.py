@@ -124,16 +124,21 @@ class ClockSampler:
 class Model:
     """A 7B-shape int4 stack resident on one GPU (one tensor-parallel shard)."""
 
-    def __init__(self, plugin, torch, batch, rank, world, layers):
+    def __init__(self, plugin, torch, batch, rank, world, layers, fmt="w4g32", seq=1, head="argmax"):
         from strata_host import Device
-        self.plugin, self.torch, self.batch = plugin, torch, batch
-        g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=1, max_len=MAX_LEN, fmt="w4g32", layers=layers,
-                              head="argmax", tp_rank=rank, tp_world=world)
+        self.plugin, self.torch, self.batch, self.seq = plugin, torch, batch, seq
+        prefill = seq > 1
+        max_len = seq if prefill else MAX_LEN
+        g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=seq, max_len=max_len, fmt=fmt, layers=layers,
+                              head=head, tp_rank=rank, tp_world=world, last_token=prefill)
         self.graph, self.hd = g, hd
         lib = C.CDLL(plugin.path)
         q4 = lib.strata_b200_quant_w4g32
         q4.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
         q4.restype = C.c_int32
+        q8 = lib.strata_b200_quant_w8pc
+        q8.argtypes = [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]
+        q8.restype = C.c_int32
         dev = torch.device("cuda", torch.cuda.current_device())
         gen = torch.Generator(device=dev)
         gen.manual_seed(1234 + rank)
@@ -151,21 +156,34 @@ class Model:
                 assert rc == 0, rc
                 del w
                 self.tensors[i], self.tensors[i + 1] = codes, scales
+            elif v.dtype.element == 6:  # int8 codes: quantise N(0, 0.02) f32 per output channel
+                n, k = v.dims
+                w = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32) * 0.02
+                codes = torch.empty((n, k), dtype=torch.int8, device=dev)
+                scales = torch.empty((n,), dtype=torch.float32, device=dev)
+                rc = q8(w.data_ptr(), n, k, codes.data_ptr(), scales.data_ptr(), stream)
+                assert rc == 0, rc
+                del w
+                self.tensors[i], self.tensors[i + 1] = codes, scales
             elif i in self.tensors:
                 continue
             elif v.dtype.element == 8:  # ids / positions
                 self.tensors[i] = torch.zeros(v.dims, dtype=torch.int32, device=dev)
             elif v.name.endswith("cache"):
                 c = torch.zeros(v.dims, dtype=torch.bfloat16, device=dev)
-                c[:, :, :KV_FILL].normal_(generator=gen)
+                if not prefill:
+                    c[:, :, :KV_FILL].normal_(generator=gen)
                 self.tensors[i] = c
             elif "norm" in v.name:
                 self.tensors[i] = (1 + 0.02 * torch.randn(v.dims, generator=gen, device=dev)).to(torch.bfloat16)
             else:
                 self.tensors[i] = torch.randn(v.dims, generator=gen, device=dev).to(torch.bfloat16)
         torch.cuda.synchronize()
-        self.tensors[hd.pos].fill_(KV_FILL)
-        ids = torch.randint(0, LLAMA_7B.vocab, (batch,), generator=gen, device=dev, dtype=torch.int32)
+        if prefill:  # each prompt from position 0
+            self.tensors[hd.pos].copy_(torch.arange(seq, device=dev, dtype=torch.int32).repeat(batch))
+        else:
+            self.tensors[hd.pos].fill_(KV_FILL)
+        ids = torch.randint(0, LLAMA_7B.vocab, (batch * seq,), generator=gen, device=dev, dtype=torch.int32)
         self.tensors[hd.tokens].copy_(ids)
         for i, t in self.tensors.items():
             b = plugin.wrap(t.data_ptr(), t.numel() * t.element_size())
@@ -173,7 +191,7 @@ class Model:
             self.arena[i] = Device(b)
         self.exe = plugin.compile(g)
         if self.exe is None:
-            raise RuntimeError("the plugin declined the decode step")
+            raise RuntimeError("the plugin declined the step")
         self.bound = self.exe.bind(self.arena)
         self.ids_buf = self.arena[hd.tokens].buffer
         self.pos_buf = self.arena[hd.pos].buffer
@@ -308,6 +326,100 @@ def run_reference(args):
     return 0
 
 
+PREFILL_METRIC = "prefill tokens/s, 7B-shape int8 per-channel stack"
+
+
+def prefill_flops(shape, batch, seq, layers):
+    """FLOPs of one prefill step: the linears (2 M K N each), causal attention
+    (QK^T and PV over positions 0..t for each token t), the last-token lm_head."""
+    D, H, G, d, F = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn
+    M = batch * seq
+    lin = 2 * M * (D * H * d + 2 * D * G * d + H * d * D + 2 * D * F + F * D) * layers
+    attn = 2 * 2 * batch * H * d * (seq * (seq + 1) // 2) * layers
+    return lin + attn + 2 * batch * D * shape.vocab
+
+
+def run_prefill(args):
+    """Config 4: batch x seq prompt tokens through every layer (int8 per-channel
+    linears on the tcgen05 GEMM, causal prefill attention), logits for each
+    sequence's last position."""
+    import torch
+    from strata_host import Plugin
+    torch.cuda.set_device(0)
+    plugin = Plugin(os.path.join(PKG, "libstrata_b200.so"))
+    model = Model(plugin, torch, args.batch, 0, 1, args.layers, fmt="w8pc", seq=args.seq, head="logits")
+    stream = torch.cuda.ExternalStream(plugin.stream())
+
+    def sync():
+        torch.cuda.synchronize()
+        plugin.synchronize()
+
+    for _ in range(args.warmup):
+        model.bound.run_async()
+    sync()
+    launches0 = plugin.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        sync()
+        e0.record(stream)
+        for _ in range(args.steps):
+            model.bound.run_async()
+        e1.record(stream)
+        sync()
+    launches = plugin.launch_count() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    tokens = args.batch * args.seq
+    # End to end: ids and positions from pinned host memory in, last-token logits out.
+    n_in = tokens * 4
+    ids_h = torch.randint(0, LLAMA_7B.vocab, (tokens,), dtype=torch.int32).pin_memory()
+    pos_h = torch.arange(args.seq, dtype=torch.int32).repeat(args.batch).pin_memory()
+    out_b = model.bound.outputs[model.hd.out]
+    n_out = args.batch * LLAMA_7B.vocab * 2
+    out_h = torch.empty(n_out, dtype=torch.uint8).pin_memory()
+
+    def e2e_step():
+        model.ids_buf.write_ptr(ids_h.data_ptr(), n_in)
+        model.pos_buf.write_ptr(pos_h.data_ptr(), n_in)
+        model.bound.run()
+        out_b.read_into(out_h.data_ptr(), n_out)
+
+    e2e_step()
+    sync()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    sync()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    flops = prefill_flops(LLAMA_7B, args.batch, args.seq, args.layers)
+    try:
+        with open(PEAKS_PATH) as f:
+            peak, peak_kind = float(json.load(f)["bf16_tflops_sustained"]), "measured (sustained)"
+    except Exception:
+        peak, peak_kind = 1400.0, "fallback (sustained)"
+    tf = flops / (ms / 1e3) / 1e12
+    line = {
+        "metric": PREFILL_METRIC, "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 weights (per-channel f32 scale), bf16 activations, f32 accumulate",
+        "data": "synthetic: device-generated N(0,0.02) weights quantised by the plugin, uniform token ids",
+        "config": {"workload": f"7B-shape int8 prefill ({args.layers} layers), batch {args.batch} x "
+                               f"{args.seq} tokens, logits for the last position only",
+                   "batch": args.batch, "seq_len": args.seq, "layers": args.layers, "parallelism": "tp1",
+                   "l2": "inputs larger than L2"},
+        "e2e": {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 2 * n_in,
+                "d2h_bytes_per_step": n_out},
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                     "peak_kind": peak_kind, "flops_per_step": flops},
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line))
+    model.close()
+    plugin.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -317,10 +429,15 @@ def main():
     ap.add_argument("--layers", type=int, default=LLAMA_7B.layers)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", action="store_true",
+                    help="time the int8 prefill configuration instead of decode")
+    ap.add_argument("--seq", type=int, default=2048, help="tokens per prompt with --prefill")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.prefill:
+        return run_prefill(args)
 
     import torch
     import torch.distributed as dist

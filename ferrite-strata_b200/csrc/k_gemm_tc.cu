@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
 // int8 codes (or int4 codes times their bf16 group scale) as bf16 [n, k].
 __global__ void codes_i8_to_bf16_kernel(const int8_t* __restrict__ q, int64_t count, uint16_t* __restrict__ out) {
   pdl_trigger();
+  pdl_wait();  // `out` may still be read by the previous GEMM
   const int64_t n8 = count / 8;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
     const uint2 v = __ldg(reinterpret_cast<const uint2*>(q) + i);
@@ -284,6 +285,7 @@ __global__ void codes_i8_to_bf16_kernel(const int8_t* __restrict__ q, int64_t co
 __global__ void w4g32_to_bf16_kernel(const uint8_t* __restrict__ packed, const uint16_t* __restrict__ scale,
                                      int64_t n, int64_t k, uint16_t* __restrict__ out) {
   pdl_trigger();
+  pdl_wait();  // `out` may still be read by the previous GEMM
   const int64_t words = n * k / 8;  // 8 codes per 32-bit word
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < words; i += int64_t(gridDim.x) * blockDim.x) {
     const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(packed) + i);
