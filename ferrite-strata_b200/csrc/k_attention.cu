@@ -85,6 +85,19 @@ __global__ void kv_append_kernel(const T* __restrict__ k_new, const T* __restric
   }
   const int seq = row / tokens_per_seq;
   const int width = kv_heads * head_dim;
+  constexpr int kVec = 16 / int(sizeof(T));  // elements per 16-byte copy
+  const bool vec = head_dim % kVec == 0 &&
+                   ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new) |
+                     reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15) == 0;
+  if (vec) {
+    for (int c = threadIdx.x; c < width / kVec; c += blockDim.x) {
+      const int i = c * kVec, h = i / head_dim, d = i - h * head_dim;
+      const int64_t dst = ((int64_t(seq) * kv_heads + h) * max_len + p) * head_dim + d;
+      *reinterpret_cast<uint4*>(k_cache + dst) = *reinterpret_cast<const uint4*>(k_new + int64_t(row) * width + i);
+      *reinterpret_cast<uint4*>(v_cache + dst) = *reinterpret_cast<const uint4*>(v_new + int64_t(row) * width + i);
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < width; i += blockDim.x) {
     const int h = i / head_dim, d = i % head_dim;
     const int64_t dst = ((int64_t(seq) * kv_heads + h) * max_len + p) * head_dim + d;

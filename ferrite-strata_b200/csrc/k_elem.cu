@@ -54,6 +54,46 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * cols;
+  if constexpr (sizeof(T) == 2) {
+    // bf16 rows of up to blockDim * 32 columns: the row stays in registers as
+    // 16-byte chunks (read once), gamma is read in 16-byte chunks.
+    constexpr int kMax = 4;  // chunks per thread
+    const int64_t chunks = cols / 8;
+    if (cols % 8 == 0 && chunks <= int64_t(kMax) * blockDim.x &&
+        ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(y)) & 15) ==
+            0) {
+      uint4 v[kMax];
+      float ss = 0.0f;
+#pragma unroll
+      for (int u = 0; u < kMax; ++u) {
+        const int64_t c = threadIdx.x + int64_t(u) * blockDim.x;
+        v[u] = c < chunks ? __ldg(reinterpret_cast<const uint4*>(xr) + c) : make_uint4(0, 0, 0, 0);
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          ss = fmaf(bf_lo(w[e]), bf_lo(w[e]), ss);
+          ss = fmaf(bf_hi(w[e]), bf_hi(w[e]), ss);
+        }
+      }
+      ss = block_sum(ss, red);
+      const float inv = 1.0f / sqrtf(ss / float(cols) + eps);
+#pragma unroll
+      for (int u = 0; u < kMax; ++u) {
+        const int64_t c = threadIdx.x + int64_t(u) * blockDim.x;
+        if (c < chunks) {
+          const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(g) + c);
+          const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, gw[4] = {g4.x, g4.y, g4.z, g4.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            o[e] = uint32_t(f2bf((bf_lo(w[e]) * inv) * bf_lo(gw[e]))) |
+                   (uint32_t(f2bf((bf_hi(w[e]) * inv) * bf_hi(gw[e]))) << 16);
+          reinterpret_cast<uint4*>(y + row * cols)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      return;
+    }
+  }
   float ss = 0.0f;
   for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
     const float v = ld(xr, c);
@@ -71,20 +111,28 @@ __global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__
                             int heads, int head_dim, double theta, T* __restrict__ y) {
   pdl_trigger();
   pdl_wait();
+  // One row at a time per block: the row's cos/sin for each frequency are
+  // computed once (in double, as the oracle does) and shared by every head.
+  extern __shared__ double cs[];  // [half] cos, then [half] sin
   const int half = head_dim / 2;
-  const int64_t total = rows * heads * half;
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += int64_t(gridDim.x) * blockDim.x) {
-    const int j = int(i % half);
-    const int64_t rh = i / half;
-    const int64_t row = rh / heads;
-    const int64_t base = rh * head_dim;
-    const double inv = pow(theta, -2.0 * double(j) / double(head_dim));
-    double s, c;
-    sincos(double(pos[row]) * inv, &s, &c);
-    const double x1 = ld(x, base + j), x2 = ld(x, base + j + half);
-    st(y, base + j, float(x1 * c - x2 * s));
-    st(y, base + j + half, float(x2 * c + x1 * s));
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    __syncthreads();  // the previous row's table is no longer read
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+      const double inv = pow(theta, -2.0 * double(j) / double(head_dim));
+      double s, c;
+      sincos(double(pos[row]) * inv, &s, &c);
+      cs[j] = c;
+      cs[half + j] = s;
+    }
+    __syncthreads();
+    const int64_t base = row * int64_t(heads) * head_dim;
+    for (int i = threadIdx.x; i < heads * half; i += blockDim.x) {
+      const int h = i / half, j = i - h * half;
+      const int64_t b = base + int64_t(h) * head_dim;
+      const double x1 = ld(x, b + j), x2 = ld(x, b + j + half), c = cs[j], s = cs[half + j];
+      st(y, b + j, float(x1 * c - x2 * s));
+      st(y, b + j + half, float(x2 * c + x1 * s));
+    }
   }
 }
 
@@ -93,7 +141,30 @@ __global__ void swiglu_kernel(const T* __restrict__ gate, const T* __restrict__ 
                               T* __restrict__ y) {
   pdl_trigger();
   pdl_wait();
-  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+  int64_t start = 0;
+  if constexpr (sizeof(T) == 2) {
+    // Eight bf16 per 16-byte load when all three arrays are 16-byte aligned.
+    if (((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(y)) &
+         15) == 0) {
+      const int64_t n8 = n / 8;
+      for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += int64_t(gridDim.x) * blockDim.x) {
+        const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(gate) + i);
+        const uint4 u4 = __ldg(reinterpret_cast<const uint4*>(up) + i);
+        const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w}, uw[4] = {u4.x, u4.y, u4.z, u4.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float g0 = bf_lo(gw[e]), g1 = bf_hi(gw[e]);
+          const float r0 = (g0 / (1.0f + expf(-g0))) * bf_lo(uw[e]);
+          const float r1 = (g1 / (1.0f + expf(-g1))) * bf_hi(uw[e]);
+          o[e] = uint32_t(f2bf(r0)) | (uint32_t(f2bf(r1)) << 16);
+        }
+        reinterpret_cast<uint4*>(y)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      start = n8 * 8;
+    }
+  }
+  for (int64_t i = start + int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += int64_t(gridDim.x) * blockDim.x) {
     const float gv = ld(gate, i);
     st(y, i, (gv / (1.0f + expf(-gv))) * ld(up, i));
@@ -385,9 +456,10 @@ template <typename T>
 int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int64_t head_dim,
                 double theta, T* y, cudaStream_t st) {
   if (head_dim % 2) return SB_INVALID_ARGUMENT;
-  const int64_t n = rows * heads * (head_dim / 2);
-  if (n == 0) return SB_OK;
-  launch_pdl(rope_kernel<T>, dim3(grid_for(n)), dim3(256), 0, st, x, pos, rows, int(heads), int(head_dim), theta, y);
+  if (rows * heads * (head_dim / 2) == 0) return SB_OK;
+  const unsigned blocks = unsigned(rows < 8 * kNumSMs ? rows : 8 * kNumSMs);
+  launch_pdl(rope_kernel<T>, dim3(blocks), dim3(256), size_t(head_dim) * sizeof(double), st, x, pos, rows,
+             int(heads), int(head_dim), theta, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
