@@ -39,6 +39,9 @@ METRIC = "decode tokens/s, 7B-shape int4 g32 stack"
 KV_FILL = 2048            # prefilled cache entries; the new token sits at position 2048
 MAX_LEN = 2112            # cache capacity per sequence
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+# DRAM bytes read + written by one gate/up GEMV launch (M = 1), from the ncu
+# capture summarised in profiles/gemv_w4g32_swiglu_m1.md.
+GATEUP_TRAFFIC_BYTES = 50_759_168 + 21_248
 
 
 def step_bytes(shape, batch, tp=1):
@@ -549,7 +552,7 @@ def main():
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nb, "d2h_bytes_per_step": nb},
             "roofline": {"bound": "hbm", "kernel": "w4g32 gate/up GEMV + SwiGLU epilogue, M=1, N=2x11008, K=4096",
                          "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
-                         "peak_kind": peak_kind, "traffic": None,
+                         "peak_kind": peak_kind, "traffic": GATEUP_TRAFFIC_BYTES,
                          "bytes_per_launch": k_bytes, "us_per_launch": k_s * 1e6},
             "step_roofline": {"bytes_per_step": sb, "achieved_gbs_per_gpu": step_gbs, "frac": step_gbs / peak,
                               "frac_of_8tbs": step_gbs / 8000.0},
