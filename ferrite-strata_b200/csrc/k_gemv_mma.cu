@@ -341,7 +341,8 @@ __global__ void __launch_bounds__(kWarps * 32, NT <= 2 ? 3 : 2) gemv_mma_kernel(
         if (p.scale16) {
           if (lane < 16 && nj > 0) cp_async16(sdst, ssrc);
         } else {
-          // bf16 pairs: the slice start and nj are even.
+          // bf16 pairs: the group count and the slice start are even, so every
+          // pair starts on a 4-byte boundary.
 #pragma unroll
           for (int i = 0; i < kChunk / 4; ++i) {
             const int pr = (lane >> 4) + 2 * i;
@@ -522,11 +523,15 @@ bool gemv_mma_supported(const GemvMmaArgs& a) {
   const LinearBatch& b = a.lb;
   if (b.fmt != WFormat::W4G32 && b.fmt != WFormat::W8PC) return false;
   if (b.k % 32 || b.m <= 0) return false;
-  if (b.fmt == WFormat::W4G32 && (b.k / 32) % 2) return false;  // scales copied as bf16 pairs
+  // int4 scales are copied as 4-byte bf16 pairs: rows of an even number of
+  // groups keep every pair aligned (an odd count goes to the CUDA-core GEMV).
+  if (b.fmt == WFormat::W4G32 && (b.k / 32) % 2) return false;
   auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!aligned(b.x)) return false;
-  for (int j = 0; j < b.njobs; ++j)
+  for (int j = 0; j < b.njobs; ++j) {
     if (!aligned(b.jobs[j].w)) return false;
+    if (b.fmt == WFormat::W4G32 && (reinterpret_cast<uintptr_t>(b.jobs[j].s) & 3)) return false;
+  }
   switch (a.mode) {
     case GemvMode::Plain:
       if (b.epi == Epilogue::SwiGLU) return false;

@@ -119,13 +119,12 @@ def test_linear_w4g32_matches_oracle(cuda, lib, m):
 
 @pytest.mark.parametrize("fmt", ["w4g32", "w8pc"])
 @pytest.mark.parametrize("m", [1, 5, 24, 64, 65])
-@pytest.mark.parametrize("n,k", [(256, 11008), (48, 2752), (16, 96), (32, 4128)])
+@pytest.mark.parametrize("n,k", [(256, 11008), (48, 2752), (16, 96), (32, 4128), (64, 1376)])
 def test_linear_ragged_shapes(cuda, lib, fmt, m, n, k):
-    """K-slices that end in partial chunks or hold no groups, and 1..9 n-tiles of x rows."""
+    """K-slices that end in partial chunks, odd group counts (K = 96, 4128, and 1376 = the
+    7B down_proj at 8-way tensor parallelism) or empty slices, and 1..9 n-tiles of x rows."""
     torch = cuda
-    if fmt == "w4g32" and (k // 32) % 2:
-        pytest.skip("odd group counts take the CUDA-core path")
-    x = _x_bf16(m, k, seed=3)
+    x = _x_bf16(m, k, seed=3)  # odd int4 group counts take the CUDA-core GEMV
     w = ora.normal(4, (n, k), std=0.02)
     xd = dev(torch, x.view(np.int16))
     y = torch.empty((m, n), dtype=torch.int16, device="cuda")
