@@ -1065,7 +1065,10 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
       case SK::AllReduce: {
         void* src = p.at(st.v[0]);
         void* dst = p.at(st.v[1]);
-        if (ctx.comm && ctx.world > 1) {
+        if (ctx.ar_ready && st.bf16 && sb::allreduce_bf16_supported(st.i[0], src, dst, ctx.world)) {
+          rc = sb::launch_allreduce_bf16(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), st.i[0],
+                                         ctx.rank, ctx.world, ctx.ar_peers, ctx.ar_counters, ctx.d_err, s);
+        } else if (ctx.comm && ctx.world > 1) {
           const ncclResult_t r = ctx.nccl.all_reduce(src, dst, size_t(st.i[0]),
                                                      st.bf16 ? ncclBfloat16 : ncclFloat32, ncclSum,
                                                      ctx.comm, s);

@@ -161,6 +161,8 @@ void Ctx::check_device_error(const char* where) {
     cuda_check(cudaMemset(d_err, 0, sizeof(int)), "clearing the error word");
     if (word == 4)
       fail(STRATA_INTERNAL, std::string(where) + ": a tensor-core pipeline wait ran out (the kernel stopped early)");
+    if (word == 5)
+      fail(STRATA_INTERNAL, std::string(where) + ": a tensor-parallel peer did not reach the all-reduce in time");
     const char* what = word == 2 ? "a position is outside the KV cache"
                      : word == 3 ? "a token id is outside the embedding table"
                                  : "a kernel rejected its input";
@@ -182,12 +184,76 @@ bool Nccl::load(std::string* why) {
   comm_init_rank = reinterpret_cast<decltype(comm_init_rank)>(dlsym(lib, "ncclCommInitRank"));
   all_reduce = reinterpret_cast<decltype(all_reduce)>(dlsym(lib, "ncclAllReduce"));
   comm_destroy = reinterpret_cast<decltype(comm_destroy)>(dlsym(lib, "ncclCommDestroy"));
+  all_gather = reinterpret_cast<decltype(all_gather)>(dlsym(lib, "ncclAllGather"));
   error_string = reinterpret_cast<decltype(error_string)>(dlsym(lib, "ncclGetErrorString"));
-  if (!get_unique_id || !comm_init_rank || !all_reduce || !comm_destroy || !error_string) {
+  if (!get_unique_id || !comm_init_rank || !all_reduce || !comm_destroy || !error_string || !all_gather) {
     *why = "libnccl.so.2 lacks an expected symbol";
     return false;
   }
   return true;
+}
+
+// The exchange regions of the NVLink all-reduce: allocate and zero this
+// rank's region, gather every rank's IPC handle over NCCL and map the peers'
+// regions.  Any failure leaves ar_ready false and NCCL carries every
+// all-reduce.  STRATA_B200_NVLINK_ALLREDUCE=0 turns the custom path off.
+void Ctx::setup_allreduce() {
+  const char* env = std::getenv("STRATA_B200_NVLINK_ALLREDUCE");
+  if ((env && *env == '0') || world < 2 || world > 8 || !comm) return;
+  if (cudaMalloc(&ar_region, sb::allreduce_region_bytes()) != cudaSuccess ||
+      cudaMalloc(reinterpret_cast<void**>(&ar_counters), sb::allreduce_counter_bytes()) != cudaSuccess ||
+      cudaMemset(ar_region, 0, sb::allreduce_region_bytes()) != cudaSuccess ||
+      cudaMemset(ar_counters, 0, sb::allreduce_counter_bytes()) != cudaSuccess) {
+    cudaGetLastError();
+    teardown_allreduce();
+    return;
+  }
+  cudaIpcMemHandle_t mine;
+  if (cudaIpcGetMemHandle(&mine, ar_region) != cudaSuccess) {
+    cudaGetLastError();
+    teardown_allreduce();
+    return;
+  }
+  constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+  void* d_handles = nullptr;
+  std::vector<cudaIpcMemHandle_t> all(world);
+  bool ok = cudaMalloc(&d_handles, kH * world) == cudaSuccess &&
+            cudaMemcpy(static_cast<char*>(d_handles) + kH * rank, &mine, kH, cudaMemcpyHostToDevice) == cudaSuccess;
+  // Every rank reaches the all-gather with its region already zeroed.
+  ok = ok && cudaDeviceSynchronize() == cudaSuccess &&
+       nccl.all_gather(static_cast<char*>(d_handles) + kH * rank, d_handles, kH, ncclUint8, comm, stream) ==
+           ncclSuccess &&
+       cudaStreamSynchronize(stream) == cudaSuccess &&
+       cudaMemcpy(all.data(), d_handles, kH * world, cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (d_handles) cudaFree(d_handles);
+  for (int r = 0; ok && r < world; ++r) {
+    if (r == rank) {
+      ar_peers.base[r] = ar_region;
+      continue;
+    }
+    void* p = nullptr;
+    ok = cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    ar_peers.base[r] = p;
+  }
+  if (!ok) {
+    cudaGetLastError();
+    teardown_allreduce();
+    return;
+  }
+  ar_ready = true;
+}
+
+void Ctx::teardown_allreduce() {
+  for (int r = 0; r < 8; ++r) {
+    if (ar_peers.base[r] && ar_peers.base[r] != ar_region) cudaIpcCloseMemHandle(ar_peers.base[r]);
+    ar_peers.base[r] = nullptr;
+  }
+  if (ar_region) cudaFree(ar_region);
+  if (ar_counters) cudaFree(ar_counters);
+  ar_region = nullptr;
+  ar_counters = nullptr;
+  ar_ready = false;
+  cudaGetLastError();
 }
 
 }  // namespace sbp
@@ -585,6 +651,7 @@ static void sb_plugin_free(void* ctx) {
   if (c->device_ready) {
     cudaSetDevice(c->device);
     cudaStreamSynchronize(c->stream);
+    c->teardown_allreduce();
     if (c->comm) c->nccl.comm_destroy(c->comm);
     g_pool.drain();
     cudaFree(c->d_err);
@@ -666,6 +733,7 @@ static int32_t ext_tp_init(void* ctx, int32_t rank, int32_t world, const uint8_t
     c->comm = comm;
     c->rank = rank;
     c->world = world;
+    c->setup_allreduce();
     return STRATA_OK;
   });
 }

@@ -39,6 +39,7 @@ struct Nccl {
   ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   bool load(std::string* why);
@@ -57,6 +58,14 @@ struct Ctx {
   Nccl nccl;
   ncclComm_t comm = nullptr;
   int rank = 0, world = 1;
+  // NVLink all-reduce: this rank's IPC exchange region, the peers' regions as
+  // mapped here, and the per-block call counters (set up by tp_init).
+  bool ar_ready = false;
+  void* ar_region = nullptr;
+  uint32_t* ar_counters = nullptr;
+  sb::ArPeers ar_peers{};
+  void setup_allreduce();
+  void teardown_allreduce();
 
   void ensure_device();  // lazily select the device and create the stream
   void check_device_error(const char* where);
