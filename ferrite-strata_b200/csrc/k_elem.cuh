@@ -104,6 +104,11 @@ constexpr int64_t kGemvMaxRows = 64;
 bool gemm_tc_supported(int64_t m, int64_t n, int64_t k, const void* x, const void* w);
 int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int64_t n, const float* scale,
                         const uint16_t* residual, int64_t ldr, uint16_t* y, int64_t ldy, int* err, cudaStream_t st);
+// y[m, n] = silu(x w_gate^T * s_gate) * (x w_up^T * s_up): gate and up of the
+// same output features in one tcgen05 GEMM (bf16 weights, optional f32 scales).
+int launch_gemm_tc_swiglu(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w_gate, const uint16_t* w_up,
+                          int64_t n, const float* s_gate, const float* s_up, uint16_t* y, int64_t ldy, int* err,
+                          cudaStream_t st);
 // Weights as bf16 [n, k]: fmt 1 = int8 codes (exact), fmt 0 = int4 code * bf16 group scale.
 int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, int64_t k, uint16_t* out,
                          cudaStream_t st);

@@ -8,16 +8,18 @@
 // launch_codes_to_bf16), so the per-channel scale is applied in f32 in the
 // epilogue and the product matches the oracle's code * scale.
 //
-// One CTA computes a 128 x 256 tile of y (tokens x features):
+// Persistent: one CTA per SM walks 128 x 256 tiles of y (tokens x features):
 //   warp 0      one thread issues TMA loads of the x tile (128 x 64) and the
-//               w tile (256 x 64), 128-byte swizzled, into a 4-stage ring;
-//   warp 1      allocates 256 TMEM columns (the f32 accumulator: TMEM lane =
+//               w tile (256 x 64), 128-byte swizzled, into a 4-stage ring
+//               that runs continuously across the CTA's tiles;
+//   warp 1      allocates 512 TMEM columns (two f32 accumulators: TMEM lane =
 //               token row, column = feature) and one thread issues
 //               tcgen05.mma (M 128, N 256, K 16; four per stage) and
-//               tcgen05.commit to release each stage and, at the end, the
+//               tcgen05.commit to release each stage and each finished
 //               accumulator;
 //   warps 2-5   the epilogue: tcgen05.ld 32 columns at a time from their
-//               TMEM lane quarter, scale, add the residual, round to bf16.
+//               TMEM lane quarter, scale, residual or SwiGLU, bf16 -- while
+//               the MMA thread already fills the other accumulator.
 // Every mbarrier wait is bounded; a wait that runs out records error code 4
 // in *err and the CTA winds down (the TMEM owner still frees its columns).
 #include <cuda.h>
@@ -37,7 +39,7 @@ constexpr int kABytes = kBM * kBK * 2;            // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;            // 32 KB
 constexpr int kGStageBytes = kABytes + kBBytes;   // 48 KB
 constexpr int kGSmem = kGStages * kGStageBytes + 1024 + 256;  // ring + alignment + barriers
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 2 * kBN;        // two accumulators of 256 f32 columns
 constexpr uint32_t kWaitLimit = 1u << 22;         // bounded mbarrier polls
 
 // Instruction descriptor, kind::f16: f32 accumulate (bits 4-5 = 1), bf16 A
@@ -47,8 +49,9 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >
                             (uint32_t(kBM >> 4) << 24);
 
 struct GemmArgs {
-  int m, n, k;
-  const float* scale;        // [n] or null
+  int m, n, k;               // n: output features (for SwiGLU: of the gate and of the up matrix)
+  const float* scale;        // [n] or null (SwiGLU: gate scales)
+  const float* scale2;       // SwiGLU: up scales [n] or null
   const uint16_t* residual;  // [m, ldr] or null
   int ldr;
   uint16_t* y;               // [m, ldy]
@@ -128,19 +131,116 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+
+// Epilogue of one tile for one token row: TMEM columns [col0, col0 + 256) of
+// this warp's lane quarter.  EPI 0: y = scale * acc (+ residual); EPI 1: the
+// gate in columns 0..127 and the up in 128..255, each rounded to bf16 as the
+// graph's gate and up values are, then silu(gate) * up.
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, uint32_t taddr, int row, int n0) {
+  if constexpr (EPI == 1) {
+    for (int c = 0; c < kBN / 64; ++c) {
+      uint32_t gr[32], ur[32];
+      tmem_ld32(taddr + uint32_t(c * 32), gr);
+      tmem_ld32(taddr + uint32_t(kBN / 2 + c * 32), ur);
+      const int nb = n0 + c * 32;
+      if (row >= p.m || nb >= p.n) continue;
+      uint16_t* yr = p.y + int64_t(row) * p.ldy + nb;
+      float out[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = nb + j < p.n ? nb + j : p.n - 1;
+        float g = __uint_as_float(gr[j]), u = __uint_as_float(ur[j]);
+        if (p.scale) g *= p.scale[n];
+        if (p.scale2) u *= p.scale2[n];
+        g = bf2f(f2bf(g));
+        u = bf2f(f2bf(u));
+        out[j] = (g / (1.0f + expf(-g))) * u;
+      }
+      if (nb + 32 <= p.n && (reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = uint32_t(f2bf(out[8 * v + 2 * e])) | (uint32_t(f2bf(out[8 * v + 2 * e + 1])) << 16);
+          *reinterpret_cast<uint4*>(yr + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+        for (int j = 0; j < 32 && nb + j < p.n; ++j) yr[j] = f2bf(out[j]);
+      }
+    }
+  } else {
+    for (int c = 0; c < kBN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + uint32_t(c * 32), r);
+      const int nb = n0 + c * 32;
+      if (row >= p.m || nb >= p.n) continue;
+      uint16_t* yr = p.y + int64_t(row) * p.ldy + nb;
+      const uint16_t* rr = p.residual ? p.residual + int64_t(row) * p.ldr + nb : nullptr;
+      if (nb + 32 <= p.n && (reinterpret_cast<uintptr_t>(yr) & 15) == 0 &&
+          (!rr || (reinterpret_cast<uintptr_t>(rr) & 15) == 0)) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint32_t w[4];
+          const uint4 res = rr ? *reinterpret_cast<const uint4*>(rr + 8 * v) : make_uint4(0, 0, 0, 0);
+          const uint32_t rw[4] = {res.x, res.y, res.z, res.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = 8 * v + 2 * e;
+            float lo = __uint_as_float(r[j]), hi = __uint_as_float(r[j + 1]);
+            if (p.scale) {
+              lo *= p.scale[nb + j];
+              hi *= p.scale[nb + j + 1];
+            }
+            if (rr) {
+              lo = bf2f(f2bf(lo)) + bf_lo(rw[e]);
+              hi = bf2f(f2bf(hi)) + bf_hi(rw[e]);
+            }
+            w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
+          }
+          *reinterpret_cast<uint4*>(yr + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+        for (int j = 0; j < 32 && nb + j < p.n; ++j) {
+          float v = __uint_as_float(r[j]);
+          if (p.scale) v *= p.scale[nb + j];
+          if (rr) v = bf2f(f2bf(v)) + bf2f(rr[j]);
+          yr[j] = f2bf(v);
+        }
+      }
+    }
+  }
+}
+
+// Persistent: CTA b computes tiles b, b + grid, ... (features fastest, so a
+// wave of CTAs shares its x rows and walks all of W).  Two TMEM accumulators
+// of 256 columns alternate between tiles: the epilogue warps drain tile i
+// while the MMA thread fills the other accumulator with tile i + 1.
+//
+// EPI 0: y = scale * (x W^T) (+ residual).  EPI 1 (SwiGLU): the B tile is
+// 128 rows of the gate matrix over 128 rows of the up matrix for the same
+// output features, and y = silu(gate) * up for those 128 features.
+template <int EPI>
 __global__ void __launch_bounds__(kGThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                   const GemmArgs p) {
+                   const __grid_constant__ CUtensorMap tmap_w2, const GemmArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGStages * kGStageBytes);
   uint64_t* empty = full + kGStages;
-  uint64_t* acc_full = empty + kGStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + kGStages;   // [2]: accumulator b holds a finished tile
+  uint64_t* acc_empty = acc_full + 2;      // [2]: the epilogue has drained accumulator b
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+  constexpr int kOutCols = EPI == 1 ? kBN / 2 : kBN;  // output features per tile
+  const int tiles_n = (p.n + kOutCols - 1) / kOutCols;
+  const int tiles = tiles_n * ((p.m + kBM - 1) / kBM);
   const int nk = (p.k + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -148,7 +248,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kGThreads / 32 - 2);  // one arrival per epilogue warp
+    }
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -167,91 +270,82 @@ __global__ void __launch_bounds__(kGThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kGStages;
-        if (kb >= kGStages && !mbar_wait(&empty[s], ((kb / kGStages) - 1) & 1)) {
-          atomicExch(&s_fail, 1);
-          break;
+      // Producer: one continuous ring over every (tile, k-block) of this CTA.
+      uint32_t c = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kOutCols;
+        for (int kb = 0; kb < nk; ++kb, ++c) {
+          const int s = int(c % kGStages);
+          if (!mbar_wait(&empty[s], ((c / kGStages) & 1) ^ 1)) {  // first pass: free
+            atomicExch(&s_fail, 1);
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * kGStageBytes;
+          mbar_expect_tx(&full[s], kGStageBytes);
+          tma_load_2d(sa, &tmap_x, &full[s], kb * kBK, m0);
+          if constexpr (EPI == 1) {
+            tma_load_2d(sa + kABytes, &tmap_w, &full[s], kb * kBK, n0);
+            tma_load_2d(sa + kABytes + kBBytes / 2, &tmap_w2, &full[s], kb * kBK, n0);
+          } else {
+            tma_load_2d(sa + kABytes, &tmap_w, &full[s], kb * kBK, n0);
+          }
         }
-        uint8_t* sa = smem + s * kGStageBytes;
-        mbar_expect_tx(&full[s], kGStageBytes);
-        tma_load_2d(sa, &tmap_x, &full[s], kb * kBK, m0);
-        tma_load_2d(sa + kABytes, &tmap_w, &full[s], kb * kBK, n0);
-        issued = kb + 1;
       }
       // Let the copies still in flight land before the CTA can exit.
-      for (int kb = issued - kGStages < 0 ? 0 : issued - kGStages; kb < issued; ++kb)
-        mbar_wait(&full[kb % kGStages], (kb / kGStages) & 1);
+      for (uint32_t d = c >= kGStages ? c - kGStages : 0; d < c; ++d)
+        mbar_wait(&full[d % kGStages], (d / kGStages) & 1);
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // MMA issuer.
+      uint32_t c = 0;
       bool ok = true;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kGStages;
-        if (!mbar_wait(&full[s], (kb / kGStages) & 1)) {
-          ok = false;
+      int i = 0;
+      for (int t = blockIdx.x; ok && t < tiles; t += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (!mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) {  // first use of each accumulator: free
           atomicExch(&s_fail, 1);
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint8_t* sa = smem + s * kGStageBytes;
-        const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kABytes);
+        const uint32_t acc = tmem + uint32_t(b * kBN);
+        for (int kb = 0; kb < nk; ++kb, ++c) {
+          const int s = int(c % kGStages);
+          if (!mbar_wait(&full[s], (c / kGStages) & 1)) {
+            atomicExch(&s_fail, 1);
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint8_t* sa = smem + s * kGStageBytes;
+          const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kABytes);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K per step
-          umma_bf16(tmem, da + uint64_t(2 * kk), db + uint64_t(2 * kk), (kb | kk) != 0);
-        umma_commit(&empty[s]);
+          for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K per step
+            umma_bf16(acc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), (kb | kk) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[b]);
       }
-      if (ok) umma_commit(acc_full);
     }
   } else {
     // Epilogue warps 2..5: TMEM lane quarter = warp % 4.
     const int quarter = warp & 3;
-    const int row = m0 + quarter * 32 + lane;
-    if (!mbar_wait(acc_full, 0)) {
-      atomicExch(&s_fail, 1);
-    } else {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + (uint32_t(quarter * 32) << 16) + uint32_t(c * 32), r);
-        const int nb = n0 + c * 32;
-        if (row < p.m && nb < p.n) {
-          uint16_t* yr = p.y + int64_t(row) * p.ldy + nb;
-          const uint16_t* rr = p.residual ? p.residual + int64_t(row) * p.ldr + nb : nullptr;
-          if (nb + 32 <= p.n && (reinterpret_cast<uintptr_t>(yr) & 15) == 0 &&
-              (!rr || (reinterpret_cast<uintptr_t>(rr) & 15) == 0)) {
-#pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              uint32_t w[4];
-              uint4 res = rr ? *reinterpret_cast<const uint4*>(rr + 8 * v) : make_uint4(0, 0, 0, 0);
-              const uint32_t rw[4] = {res.x, res.y, res.z, res.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j = 8 * v + 2 * e;
-                float lo = __uint_as_float(r[j]), hi = __uint_as_float(r[j + 1]);
-                if (p.scale) {
-                  lo *= p.scale[nb + j];
-                  hi *= p.scale[nb + j + 1];
-                }
-                if (rr) {
-                  lo = bf2f(f2bf(lo)) + bf_lo(rw[e]);
-                  hi = bf2f(f2bf(hi)) + bf_hi(rw[e]);
-                }
-                w[e] = uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16);
-              }
-              *reinterpret_cast<uint4*>(yr + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-          } else {
-            for (int j = 0; j < 32 && nb + j < p.n; ++j) {
-              float v = __uint_as_float(r[j]);
-              if (p.scale) v *= p.scale[nb + j];
-              if (rr) v = bf2f(f2bf(v)) + bf2f(rr[j]);
-              yr[j] = f2bf(v);
-            }
-          }
-        }
+    int i = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
+      const int b = i & 1;
+      if (!mbar_wait(&acc_full[b], (i >> 1) & 1)) {
+        atomicExch(&s_fail, 1);
+        break;
       }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kOutCols;
+      gemm_epilogue<EPI>(p, tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN), m0 + quarter * 32 + lane,
+                         n0);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -340,18 +434,34 @@ bool gemm_tc_supported(int64_t m, int64_t n, int64_t k, const void* x, const voi
          encode_fn() != nullptr;
 }
 
+namespace {
+
+template <int EPI>
+int launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mw2, const GemmArgs& a, int tiles_n,
+                cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) !=
+        cudaSuccess)
+      return SB_INTERNAL;
+    configured = true;
+  }
+  const int tiles = tiles_n * ((a.m + kBM - 1) / kBM);
+  const dim3 grid{unsigned(tiles < kNumSMs ? tiles : kNumSMs), 1u, 1u};  // persistent: one CTA per SM
+  if (launch_pdl(gemm_tc_kernel<EPI>, grid, dim3(kGThreads), size_t(kGSmem), st, mx, mw, mw2, a) != cudaSuccess)
+    return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
+
+}  // namespace
+
 int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int64_t n, const float* scale,
                         const uint16_t* residual, int64_t ldr, uint16_t* y, int64_t ldy, int* err, cudaStream_t st) {
   if (!gemm_tc_supported(m, n, k, x, w)) return SB_INVALID_ARGUMENT;
   CUtensorMap mx, mw;
   if (!make_map(&mx, x, m, k, kBM) || !make_map(&mw, w, n, k, kBN)) return SB_INTERNAL;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) != cudaSuccess)
-      return SB_INTERNAL;
-    configured = true;
-  }
-  GemmArgs a;
+  GemmArgs a{};
   a.m = int(m);
   a.n = int(n);
   a.k = int(k);
@@ -361,11 +471,26 @@ int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t*
   a.y = y;
   a.ldy = int(ldy);
   a.err = err;
-  const dim3 grid{unsigned((n + kBN - 1) / kBN), unsigned((m + kBM - 1) / kBM), 1u};
-  if (launch_pdl(gemm_tc_kernel, grid, dim3(kGThreads), size_t(kGSmem), st, mx, mw, a) != cudaSuccess)
+  return launch_gemm<0>(mx, mw, mw, a, int((n + kBN - 1) / kBN), st);
+}
+
+int launch_gemm_tc_swiglu(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w_gate, const uint16_t* w_up,
+                          int64_t n, const float* s_gate, const float* s_up, uint16_t* y, int64_t ldy, int* err,
+                          cudaStream_t st) {
+  if (!gemm_tc_supported(m, n, k, x, w_gate) || !gemm_tc_supported(m, n, k, x, w_up)) return SB_INVALID_ARGUMENT;
+  CUtensorMap mx, mg, mu;
+  if (!make_map(&mx, x, m, k, kBM) || !make_map(&mg, w_gate, n, k, kBN / 2) || !make_map(&mu, w_up, n, k, kBN / 2))
     return SB_INTERNAL;
-  count_launch();
-  return SB_OK;
+  GemmArgs a{};
+  a.m = int(m);
+  a.n = int(n);
+  a.k = int(k);
+  a.scale = s_gate;
+  a.scale2 = s_up;
+  a.y = y;
+  a.ldy = int(ldy);
+  a.err = err;
+  return launch_gemm<1>(mx, mg, mu, a, int((n + kBN / 2 - 1) / (kBN / 2)), st);
 }
 
 int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, int64_t k, uint16_t* out,

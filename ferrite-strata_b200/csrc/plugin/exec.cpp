@@ -216,21 +216,21 @@ struct Lowerer {
   }
 
   // Linear steps over more than kGemvMaxRows rows run as tcgen05 GEMMs over
-  // bf16 weights: scratch for one job's expanded weights [n, k] and, for a
-  // SwiGLU pair, the gate and up products [m, n] that the SwiGLU kernel joins.
+  // bf16 weights: scratch for one job's expanded weights [n, k], or for both
+  // the gate and the up matrix of a SwiGLU pair (one GEMM with a SwiGLU
+  // epilogue).
   void plan_gemm_scratch() {
     for (Step& st : exe.steps) {
       if (st.kind != SK::Linear || st.i[0] <= sb::kGemvMaxRows) continue;
-      uint64_t wmax = 0, n0 = 0;
+      uint64_t wmax = 0;
       for (int j = 0; j < st.njobs; ++j) {
         const Value& wv = g.values[st.v[1 + 4 * j]];
         const uint64_t n = uint64_t(wv.dims[0]);
-        if (j == 0) n0 = n;
         wmax = std::max<uint64_t>(wmax, n * uint64_t(st.i[1]) * 2);
       }
-      uint64_t bytes = (wmax + 255) / 256 * 256;
-      if (st.epi == sb::Epilogue::SwiGLU) bytes += 2 * ((uint64_t(st.i[0]) * n0 * 2 + 255) / 256 * 256);
-      st.scratch_bytes = bytes;
+      // One expanded weight matrix; a SwiGLU pair keeps gate and up expanded at once.
+      const uint64_t bytes = (wmax + 255) / 256 * 256;
+      st.scratch_bytes = st.epi == sb::Epilogue::SwiGLU ? 2 * bytes : bytes;
     }
   }
 
@@ -957,32 +957,40 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
 
 // A prefill-sized Linear step: per job, expand the weights to bf16 in the
 // step's scratch and run the tcgen05 GEMM (int8 scales in its epilogue); a
-// SwiGLU pair writes gate and up to scratch and joins them with the SwiGLU
-// kernel.
+// SwiGLU pair expands gate and up side by side and runs one GEMM whose
+// epilogue writes silu(gate) * up.
 int enqueue_gemm(Ctx& ctx, Exe& exe, const Step& st, const sb::LinearBatch& b, cudaStream_t s) {
   char* base = static_cast<char*>(exe.ws) + st.scratch_off;
   uint64_t wmax = 0;
   for (int j = 0; j < b.njobs; ++j) wmax = std::max<uint64_t>(wmax, uint64_t(b.jobs[j].n) * uint64_t(b.k) * 2);
+  const uint64_t wslot = (wmax + 255) / 256 * 256;
+  const int fmt = b.fmt == sb::WFormat::W8PC ? 1 : 0;
+  auto scale_of = [&](const sb::LinearJob& J) {
+    return b.fmt == sb::WFormat::W8PC ? static_cast<const float*>(J.s) : nullptr;
+  };
+  if (st.epi == sb::Epilogue::SwiGLU) {
+    const sb::LinearJob &G = b.jobs[0], &U = b.jobs[1];
+    uint16_t* wg = reinterpret_cast<uint16_t*>(base);
+    uint16_t* wu = reinterpret_cast<uint16_t*>(base + wslot);
+    if (!sb::gemm_tc_supported(b.m, G.n, b.k, b.x, wg))
+      fail(STRATA_INTERNAL, "linear `" + st.label + "` has a layout the tensor-core GEMM cannot take");
+    int rc = sb::launch_codes_to_bf16(G.w, G.s, fmt, G.n, b.k, wg, s);
+    if (!rc) rc = sb::launch_codes_to_bf16(U.w, U.s, fmt, U.n, b.k, wu, s);
+    if (!rc)
+      rc = sb::launch_gemm_tc_swiglu(b.x, b.m, b.k, wg, wu, G.n, scale_of(G), scale_of(U), G.y, G.ldy, ctx.d_err, s);
+    return rc;
+  }
   uint16_t* wbf = reinterpret_cast<uint16_t*>(base);
-  char* tmp = base + (wmax + 255) / 256 * 256;
-  const uint64_t prod = (uint64_t(b.m) * uint64_t(b.jobs[0].n) * 2 + 255) / 256 * 256;
-  uint16_t* outs[sb::kMaxJobs] = {};
   for (int j = 0; j < b.njobs; ++j) {
     const sb::LinearJob& J = b.jobs[j];
-    outs[j] = st.epi == sb::Epilogue::SwiGLU ? reinterpret_cast<uint16_t*>(tmp + j * prod) : J.y;
-    if (!outs[j]) continue;
+    if (!J.y) continue;
     if (!sb::gemm_tc_supported(b.m, J.n, b.k, b.x, wbf))
       fail(STRATA_INTERNAL, "linear `" + st.label + "` has a layout the tensor-core GEMM cannot take");
-    int rc = sb::launch_codes_to_bf16(J.w, J.s, b.fmt == sb::WFormat::W8PC ? 1 : 0, J.n, b.k, wbf, s);
+    int rc = sb::launch_codes_to_bf16(J.w, J.s, fmt, J.n, b.k, wbf, s);
     if (rc) return rc;
-    rc = sb::launch_gemm_tc_bf16(b.x, b.m, b.k, wbf, J.n,
-                                 b.fmt == sb::WFormat::W8PC ? static_cast<const float*>(J.s) : nullptr,
-                                 st.epi == sb::Epilogue::SwiGLU ? nullptr : J.residual, J.ldr, outs[j], J.ldy,
-                                 ctx.d_err, s);
+    rc = sb::launch_gemm_tc_bf16(b.x, b.m, b.k, wbf, J.n, scale_of(J), J.residual, J.ldr, J.y, J.ldy, ctx.d_err, s);
     if (rc) return rc;
   }
-  if (st.epi == sb::Epilogue::SwiGLU)
-    return sb::launch_swiglu<uint16_t>(outs[0], outs[1], int64_t(b.m) * b.jobs[0].n, b.jobs[0].y, s);
   return SB_OK;
 }
 
