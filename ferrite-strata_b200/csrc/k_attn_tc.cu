@@ -14,15 +14,18 @@
 // Q rows beyond the group size are zero, so one m16 tile covers any group of
 // up to 8 heads.  Computing S transposed makes the score accumulators exactly
 // the A fragment of P . V, so P never leaves registers.  At the end the warps
-// merge their (max, sum, O) through shared memory and the CTA writes the same
-// (max, sum, unnormalised O) partial as the CUDA-core kernel, which
-// attn_merge_kernel combines across splits.
+// merge their (max, sum, O) through shared memory.  The splits of one
+// (row, kv head) -- at most 8 -- are launched as one thread-block cluster, and
+// CTA 0 of the cluster merges the splits through distributed shared memory
+// and writes the output: no partials reach HBM and no merge kernel runs.
 //
 // In a decode step (one token per sequence) the cache rows below the row's
 // position were written by earlier steps, so when positions are a graph input
 // the first slabs below the position are requested before griddepcontrol.wait
 // and stream in while the previous kernel (the q/k/v projection that writes
 // row `pos`) finishes.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "k_elem.cuh"
 
@@ -34,6 +37,7 @@ constexpr int kTcWarps = 4;
 constexpr int kSlab = 16;    // positions per warp step
 constexpr int kTcDepth = 3;  // slabs in flight per warp
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxSplits = 8;  // splits of one (row, kv head) form one thread-block cluster (portable size)
 
 template <int D>
 struct TcLayout {
@@ -41,8 +45,9 @@ struct TcLayout {
   static constexpr int kSlabBytes = 2 * kSlab * kRow;  // K rows, then V rows
   static constexpr int kWarpBytes = kTcDepth * kSlabBytes;
   static constexpr int kBytes = kTcWarps * kWarpBytes;
-  // The final cross-warp merge reuses the ring: O [warps][8][D], max and sum [warps][8].
-  static_assert(kTcWarps * 8 * D * 4 + 2 * kTcWarps * 8 * 4 <= kBytes, "merge area");
+  // The final merges reuse the ring: per warp O [warps][8][D], max and sum
+  // [warps][8]; then the CTA's merged O [8][D], max and sum [8].
+  static_assert((kTcWarps * 8 * D + 2 * kTcWarps * 8 + 8 * D + 16) * 4 <= kBytes, "merge area");
 };
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
@@ -84,7 +89,7 @@ __global__ void __launch_bounds__(kTcWarps * 32)
     attn_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
                    const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos, int tokens_per_seq,
                    int heads, int kv_heads, int max_len, int span, int splits, int pos_external,
-                   float* __restrict__ partial, uint16_t* __restrict__ out, int* err) {
+                   int cluster_merge, float* __restrict__ partial, uint16_t* __restrict__ out, int* err) {
   using Lay = TcLayout<D>;
   constexpr int kCpr = D / 8;  // 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
@@ -229,6 +234,9 @@ __global__ void __launch_bounds__(kTcWarps * 32)
   float* sO = reinterpret_cast<float*>(smem);     // [warps][8][D]
   float* sM = sO + kTcWarps * 8 * D;              // [warps][8]
   float* sL = sM + kTcWarps * 8;                  // [warps][8]
+  float* cO = sL + kTcWarps * 8;                  // [8][D]: this CTA's merged O (cluster merge)
+  float* cM = cO + 8 * D;                         // [8]
+  float* cL = cM + 8;                             // [8]
   if (g < G) {
 #pragma unroll
     for (int n = 0; n < D / 8; ++n) {
@@ -255,7 +263,13 @@ __global__ void __launch_bounds__(kTcWarps * 32)
       L = fmaf(wt, sL[w * 8 + h], L);
     }
     const int hh = kvh * G + h;
-    if (splits == 1) {
+    if (cluster_merge) {
+      cO[h * D + d] = acc;
+      if (d == 0) {
+        cM[h] = M;
+        cL[h] = L;
+      }
+    } else if (splits == 1) {
       out[int64_t(row) * heads * D + int64_t(hh) * D + d] = f2bf(L > 0.0f ? acc / L : 0.0f);
     } else {
       float* pp = partial + ((int64_t(row) * heads + hh) * splits + split) * (D + 2);
@@ -265,6 +279,31 @@ __global__ void __launch_bounds__(kTcWarps * 32)
         pp[1] = L;
       }
     }
+  }
+  if (cluster_merge) {
+    // The splits of this (row, kv head) are one cluster: after the cluster
+    // barrier CTA 0 reads every CTA's (max, sum, O) through distributed
+    // shared memory and writes the output; the second barrier keeps the
+    // other CTAs' shared memory alive until it has.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (split == 0) {
+      for (int it = tid; it < G * D; it += kTcWarps * 32) {
+        const int h = it / D, d = it % D;
+        float M = -INFINITY;
+        for (int r = 0; r < splits; ++r) M = fmaxf(M, cluster.map_shared_rank(cM, r)[h]);
+        float acc = 0.0f, L = 0.0f;
+        for (int r = 0; r < splits; ++r) {
+          const float mr = cluster.map_shared_rank(cM, r)[h];
+          const float wt = mr == -INFINITY ? 0.0f : exp2f(mr - M);
+          acc = fmaf(wt, cluster.map_shared_rank(cO, r)[h * D + d], acc);
+          L = fmaf(wt, cluster.map_shared_rank(cL, r)[h], L);
+        }
+        out[int64_t(row) * heads * D + int64_t(kvh * G + h) * D + d] = f2bf(L > 0.0f ? acc / L : 0.0f);
+      }
+    }
+    cluster.sync();
   }
 }
 
@@ -282,24 +321,46 @@ int launch_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
   }
   const int span = attention_tc_span(rows, kv_heads, max_len);
   const int splits = int((max_len + span - 1) / span);
-  if (splits > 1 && scratch == nullptr) return SB_INVALID_ARGUMENT;
-  const dim3 grid{unsigned(splits), unsigned(kv_heads), unsigned(rows)};
-  if (launch_pdl(attn_tc_kernel<D>, grid, dim3(kTcWarps * 32), size_t(Lay::kBytes), st, q, kc, vc, pos, int(tps),
-                 int(heads), int(kv_heads), int(max_len), span, splits, pos_external ? 1 : 0, scratch, out,
-                 err) != cudaSuccess)
+  // Splits merge inside their cluster; no partials reach memory.
+  const int cluster_merge = splits > 1 ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(splits), unsigned(kv_heads), unsigned(rows));
+  cfg.blockDim = dim3(kTcWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = size_t(Lay::kBytes);
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_merge) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = unsigned(splits);
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<D>, q, kc, vc, pos, int(tps), int(heads), int(kv_heads),
+                         int(max_len), span, splits, pos_external ? 1 : 0, cluster_merge, scratch, out, err) !=
+      cudaSuccess)
     return SB_INTERNAL;
   count_launch();
-  if (splits > 1) return launch_attention_merge_bf16(scratch, rows, heads, D, splits, out, st);
   return SB_OK;
 }
 
 }  // namespace
 
 int attention_tc_span(int64_t rows, int64_t kv_heads, int64_t max_len) {
-  // About four CTAs per SM, whole slabs of 64 positions per CTA.
+  // About four CTAs per SM, at most one cluster's worth of splits, whole
+  // slabs of 64 positions per CTA.
   const int64_t pairs = rows * kv_heads;
   const int64_t most = (max_len + 63) / 64;
   int64_t splits = (4 * kNumSMs + pairs - 1) / pairs;
+  if (splits > kMaxSplits) splits = kMaxSplits;
   if (splits > most) splits = most;
   if (splits < 1) splits = 1;
   const int64_t per = (max_len + splits - 1) / splits;
