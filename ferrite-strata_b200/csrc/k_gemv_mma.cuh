@@ -1,4 +1,4 @@
-// Tensor-core GEMV for decode-sized batches (M <= 16 per launch).
+// Tensor-core GEMV for decode-sized batches.
 #pragma once
 
 #include "k_linear.cuh"
@@ -33,5 +33,6 @@ struct GemvMmaArgs {
 // Whether the tensor-core path takes this batch (else the CUDA-core GEMV).
 bool gemv_mma_supported(const GemvMmaArgs& a);
 int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st);
+
 
 }  // namespace sb

@@ -206,7 +206,8 @@ def test_rms_norm_rope_swiglu(cuda, lib):
     ok(lib.strata_b200_rms_norm_bf16(ptr(xd), ptr(gd), rows, cols, 1e-5, ptr(y), stream(torch)))
     pos = np.array([0, 1, 5, 100, 2047, 2048, 4000, 7], np.int32)
     yr = torch.empty((rows, cols), dtype=torch.int16, device="cuda")
-    ok(lib.strata_b200_rope_bf16(ptr(xd), ptr(dev(torch, pos)), rows, 32, 128, 10000.0, ptr(yr), stream(torch)))
+    posd = dev(torch, pos)  # device tensors stay referenced until the kernels have run
+    ok(lib.strata_b200_rope_bf16(ptr(xd), ptr(posd), rows, 32, 128, 10000.0, ptr(yr), stream(torch)))
     u = ora.to_bf16(ora.normal(6, (rows, cols)))
     ys = torch.empty((rows, cols), dtype=torch.int16, device="cuda")
     ud = dev(torch, u.view(np.int16))
@@ -240,11 +241,12 @@ def test_attention_decode_matches_oracle(cuda, lib, batch, heads, kv_heads, max_
     pos = np.array([fill - b for b in range(batch)], np.int32)  # ragged lengths
     kcd, vcd = dev(torch, ora.to_bf16(kc).view(np.int16)), dev(torch, ora.to_bf16(vc).view(np.int16))
     qd, knd, vnd = (dev(torch, ora.to_bf16(a).view(np.int16)) for a in (q, kn, vn))
+    posd = dev(torch, pos)
     scratch_bytes = lib.strata_b200_attention_decode_scratch_bytes(batch, heads, d, max_len)
     scratch = torch.empty((max(scratch_bytes, 4),), dtype=torch.uint8, device="cuda")
     out = torch.empty((batch, heads * d), dtype=torch.int16, device="cuda")
     ok(lib.strata_b200_attention_decode_bf16(ptr(qd), ptr(knd), ptr(vnd), ptr(kcd), ptr(vcd),
-                                             ptr(dev(torch, pos)), batch, heads, kv_heads, d, max_len,
+                                             ptr(posd), batch, heads, kv_heads, d, max_len,
                                              ptr(scratch), ptr(out), stream(torch)))
     torch.cuda.synchronize()
     for b in range(batch):
@@ -264,14 +266,16 @@ def test_embed_and_argmax_are_exact(cuda, lib):
     table = ora.to_bf16(ora.normal(21, (vocab, dim)))
     ids = ora.uniform_i32(2, rows, 0, vocab)
     out = torch.empty((rows, dim), dtype=torch.int16, device="cuda")
-    ok(lib.strata_b200_embed_bf16(ptr(dev(torch, ids)), rows, ptr(dev(torch, table.view(np.int16))), vocab,
+    idsd, tabd = dev(torch, ids), dev(torch, table.view(np.int16))
+    ok(lib.strata_b200_embed_bf16(ptr(idsd), rows, ptr(tabd), vocab,
                                   dim, ptr(out), stream(torch)))
     logits = ora.to_bf16(ora.normal(22, (rows, vocab)))
     logits[0, 5] = logits[0, 900] = 0x4200  # tie at the maximum (32.0): lowest index wins
     logits[1, :] = 0x7FC0                   # all NaN
     logits[1, 77] = 0x3F80
     am = torch.empty((rows,), dtype=torch.int32, device="cuda")
-    ok(lib.strata_b200_argmax_bf16(ptr(dev(torch, logits.view(np.int16))), rows, vocab, ptr(am), stream(torch)))
+    lgd = dev(torch, logits.view(np.int16))
+    ok(lib.strata_b200_argmax_bf16(ptr(lgd), rows, vocab, ptr(am), stream(torch)))
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy().view(np.uint16), table[ids])
     got = am.cpu().numpy()
