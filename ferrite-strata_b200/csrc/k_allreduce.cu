@@ -4,7 +4,9 @@
 //
 // Every rank owns an exchange region (CUDA IPC memory, mapped by every other
 // rank of the node):
-//   [flags: kArBlocks x 8 ranks, uint32][slot 0: kArSlotBytes][slot 1: kArSlotBytes]
+//   [flags: 128 blocks x 8 ranks, uint32][slot 0][slot 1][slot 2][slot 3]
+// (slots of kArSlotBytes; 0 and 1 for the plain all-reduce, 2 and 3 for the
+// fused all-reduce + add + RMSNorm below)
 // Call g of block b (g counts the all-reduces this block has run, kept per
 // block on the device so CUDA-graph replays advance it):
 //   1. copy this block's slice of x into slot g & 1 of the own region;
@@ -102,11 +104,149 @@ __global__ void __launch_bounds__(kArThreads)
   if (tid == 0) counters[b] = gen;
 }
 
+// All-reduce of one row per block fused with the residual add and the
+// RMSNorm that follow it in a tensor-parallel decoder layer:
+//   h = bf16(bf16(sum over ranks of x) + r),  n = bf16(h * rsqrt(mean(h^2) + eps) * gamma).
+// The exchange is the one above with flags and counters at block index
+// kArBlocks + row and its own pair of slots (2 and 3), in which row r always
+// owns bytes [r * kArnRowBytes, (r + 1) * kArnRowBytes): only block r of
+// every rank touches them, whatever the row count or width of a call, so the
+// per-block double-buffer argument holds for each row on its own.  Every
+// rank sums in rank order and gets the same h and n.
+constexpr int kArnThreads = 512;
+constexpr int kArnChunks = 2;  // 16-byte chunks per thread: rows of up to 8192 columns
+constexpr size_t kArnRowBytes = size_t(kArnThreads) * kArnChunks * 16;
+static_assert(kArnRowBytes * kArMaxRows <= kArSlotBytes, "fused all-reduce rows overflow a slot");
+static_assert((kArBlocks + kArMaxRows) * 8 * 4 <= kArFlagBytes, "flag area too small");
+
+__global__ void __launch_bounds__(kArnThreads)
+    allreduce_add_norm_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ r,
+                                   const uint16_t* __restrict__ gamma, uint16_t* __restrict__ h_out,
+                                   uint16_t* __restrict__ n_out, int cols, float eps, int rank, int world,
+                                   ArPeers peers, uint32_t* __restrict__ counters, int* err) {
+  __shared__ uint32_t s_gen;
+  __shared__ int s_ok;
+  __shared__ float red[32];
+  const int row = blockIdx.x, fb = kArBlocks + row, tid = threadIdx.x;
+  if (tid == 0) {
+    s_gen = counters[fb] + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t gen = s_gen;
+  const int c8 = cols / 8;
+  const size_t slot = kArFlagBytes + size_t(2 + (gen & 1)) * kArSlotBytes + size_t(row) * kArnRowBytes;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + int64_t(row) * cols);
+  uint4* mine = reinterpret_cast<uint4*>(static_cast<char*>(peers.base[rank]) + slot);
+  for (int i = tid; i < c8; i += kArnThreads) mine[i] = __ldg(xr + i);
+  __syncthreads();
+  if (tid < world && tid != rank) {
+    __threadfence_system();
+    st_release_sys(static_cast<uint32_t*>(peers.base[tid]) + fb * 8 + rank, gen);
+  }
+  if (tid < world && tid != rank) {
+    const uint32_t* f = static_cast<const uint32_t*>(peers.base[rank]) + fb * 8 + tid;
+    uint32_t spins = 0;
+    while (ld_acquire_sys(f) < gen) {
+      if (++spins == kArSpinLimit) {
+        atomicExch(&s_ok, 0);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_ok) {
+    if (tid == 0) {
+      if (err) atomicExch(err, 5);
+      counters[fb] = gen;
+    }
+    return;
+  }
+  uint4 hv[kArnChunks];
+  float ss = 0.0f;
+#pragma unroll
+  for (int u = 0; u < kArnChunks; ++u) {
+    const int i = tid + u * kArnThreads;
+    hv[u] = make_uint4(0, 0, 0, 0);
+    if (i < c8) {
+      float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+      for (int q = 0; q < world; ++q) {
+        const uint4 v = __ldcv(reinterpret_cast<const uint4*>(static_cast<const char*>(peers.base[q]) + slot) + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          acc[2 * e] += bf_lo(w[e]);
+          acc[2 * e + 1] += bf_hi(w[e]);
+        }
+      }
+      const uint4 rv = __ldg(reinterpret_cast<const uint4*>(r + int64_t(row) * cols) + i);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float h0 = bf2f(f2bf(bf2f(f2bf(acc[2 * e])) + bf_lo(rw[e])));
+        const float h1 = bf2f(f2bf(bf2f(f2bf(acc[2 * e + 1])) + bf_hi(rw[e])));
+        ss = fmaf(h0, h0, ss);
+        ss = fmaf(h1, h1, ss);
+        o[e] = uint32_t(f2bf(h0)) | (uint32_t(f2bf(h1)) << 16);
+      }
+      hv[u] = make_uint4(o[0], o[1], o[2], o[3]);
+      reinterpret_cast<uint4*>(h_out + int64_t(row) * cols)[i] = hv[u];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float t = tid < kArnThreads / 32 ? red[tid] : 0.0f;
+    t = warp_sum(t);
+    if (tid == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = 1.0f / sqrtf(red[0] / float(cols) + eps);
+#pragma unroll
+  for (int u = 0; u < kArnChunks; ++u) {
+    const int i = tid + u * kArnThreads;
+    if (i < c8) {
+      const uint4 gv = __ldg(reinterpret_cast<const uint4*>(gamma) + i);
+      const uint32_t hw[4] = {hv[u].x, hv[u].y, hv[u].z, hv[u].w}, gw[4] = {gv.x, gv.y, gv.z, gv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        o[e] = uint32_t(f2bf((bf_lo(hw[e]) * inv) * bf_lo(gw[e]))) |
+               (uint32_t(f2bf((bf_hi(hw[e]) * inv) * bf_hi(gw[e]))) << 16);
+      reinterpret_cast<uint4*>(n_out + int64_t(row) * cols)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  if (tid == 0) counters[fb] = gen;
+}
+
 }  // namespace
 
-size_t allreduce_region_bytes() { return kArFlagBytes + 2 * kArSlotBytes; }
+size_t allreduce_region_bytes() { return kArFlagBytes + 4 * kArSlotBytes; }
 
-size_t allreduce_counter_bytes() { return kArBlocks * sizeof(uint32_t); }
+size_t allreduce_counter_bytes() { return (kArBlocks + kArMaxRows) * sizeof(uint32_t); }
+
+bool allreduce_add_norm_supported(int64_t rows, int64_t cols, const void* x, const void* r, const void* gamma,
+                                  const void* h, const void* n, int world) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(r) |
+                      reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(h) |
+                      reinterpret_cast<uintptr_t>(n);
+  return world >= 2 && world <= 8 && rows > 0 && rows <= kArMaxRows && cols > 0 && cols % 8 == 0 &&
+         size_t(cols) * 2 <= kArnRowBytes && (a & 15) == 0;
+}
+
+int launch_allreduce_add_norm_bf16(const uint16_t* x, const uint16_t* r, const uint16_t* gamma, uint16_t* h,
+                                   uint16_t* n, int64_t rows, int64_t cols, float eps, int rank, int world,
+                                   const ArPeers& peers, uint32_t* counters, int* err, cudaStream_t st) {
+  if (!allreduce_add_norm_supported(rows, cols, x, r, gamma, h, n, world) || rank < 0 || rank >= world)
+    return SB_INVALID_ARGUMENT;
+  allreduce_add_norm_bf16_kernel<<<unsigned(rows), kArnThreads, 0, st>>>(x, r, gamma, h, n, int(cols), eps, rank,
+                                                                          world, peers, counters, err);
+  if (cudaGetLastError() != cudaSuccess) return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
 
 bool allreduce_bf16_supported(int64_t n, const void* x, const void* y, int world) {
   return world >= 2 && world <= 8 && n > 0 && n % 8 == 0 && size_t(n) * 2 <= kArSlotBytes &&

@@ -114,18 +114,25 @@ int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, i
                          cudaStream_t st);
 
 // One-shot NVLink all-reduce (k_allreduce.cu).  Each rank's exchange region
-// (allreduce_region_bytes(), CUDA IPC memory) holds per-block flags and two
+// (allreduce_region_bytes(), CUDA IPC memory) holds per-block flags and four
 // message slots; `peers.base[r]` is rank r's region as mapped in this process.
 struct ArPeers {
   void* base[8];
 };
-constexpr size_t kArFlagBytes = 4096;
+constexpr size_t kArFlagBytes = 4096;              // flags of up to 128 blocks x 8 ranks
 constexpr size_t kArSlotBytes = size_t(1) << 20;  // largest message
+constexpr int kArMaxRows = 64;                    // rows of the fused all-reduce + add + RMSNorm
 size_t allreduce_region_bytes();
 size_t allreduce_counter_bytes();
 bool allreduce_bf16_supported(int64_t n, const void* x, const void* y, int world);
 int launch_allreduce_bf16(const uint16_t* x, uint16_t* y, int64_t n, int rank, int world, const ArPeers& peers,
                           uint32_t* counters, int* err, cudaStream_t st);
+// h = bf16(all-reduce(x) + r), n = rms_norm(h) * gamma, one row per block.
+bool allreduce_add_norm_supported(int64_t rows, int64_t cols, const void* x, const void* r, const void* gamma,
+                                  const void* h, const void* n, int world);
+int launch_allreduce_add_norm_bf16(const uint16_t* x, const uint16_t* r, const uint16_t* gamma, uint16_t* h,
+                                   uint16_t* n, int64_t rows, int64_t cols, float eps, int rank, int world,
+                                   const ArPeers& peers, uint32_t* counters, int* err, cudaStream_t st);
 
 // Quantisation (k_quant.cu).
 int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, uint16_t* scale,

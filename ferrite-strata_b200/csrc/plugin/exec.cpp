@@ -373,6 +373,51 @@ struct Lowerer {
     return true;
   }
 
+  // The residual of a tensor-parallel layer: all_reduce(x) -> add(r, .) ->
+  // rms_norm(., gamma) becomes one step that writes the sum h and its norm
+  // (h keeps its other readers, the next residual add).  bf16 only.
+  bool lower_allreduce_add_norm(int ni) {
+    const Node& n = g.nodes[ni];
+    const uint32_t x = n.inputs[0], a = n.outputs[0];
+    if (!is_bf16(V(x).dt) || cons[a].size() != 1 || is_output[a]) return false;
+    const int ai = cons[a][0];
+    const Node& A = g.nodes[ai];
+    if (absorbed[ai] || A.op != STRATA_OP_ADD || A.inputs.size() != 2 || A.outputs.size() != 1 ||
+        A.inputs[0] == A.inputs[1])
+      return false;
+    const uint32_t r = A.inputs[0] == a ? A.inputs[1] : A.inputs[0], h = A.outputs[0];
+    const int pr = producer(r);
+    if (!is_bf16(V(r).dt) || !is_bf16(V(h).dt) || !same_dims(r, a) || V(h).dims != V(a).dims ||
+        !(pr < 0 || pr < ni) || V(h).dims.empty())
+      return false;
+    for (int ri : cons[h]) {
+      const Node& R = g.nodes[size_t(ri)];
+      if (absorbed[size_t(ri)] || R.op != STRATA_OP_CUSTOM || R.pattern != "fused::rms_norm" ||
+          R.inputs.size() != 2 || R.outputs.size() != 1 || R.inputs[0] != h)
+        continue;
+      const uint32_t gm = R.inputs[1], y = R.outputs[0];
+      const int pg = producer(gm);
+      if (!is_bf16(V(gm).dt) || !is_bf16(V(y).dt) || V(y).dims != V(h).dims ||
+          V(gm).elements() != last_dim(V(h)) || !(pg < 0 || pg < ni))
+        continue;
+      Step st;
+      st.kind = SK::AllReduceAddNorm;
+      st.bf16 = true;
+      st.i[0] = rows_of(V(h));
+      st.i[1] = last_dim(V(h));
+      st.d = R.attr_float("eps", 1e-5);
+      if (!bcast(V(h).dims, a, r, st.bs)) return false;
+      st.v = {x, r, gm, h, y};
+      st.reads = {x, r, gm};
+      st.writes = {h, y};
+      st.label = n.name + "+" + A.name + "+" + R.name;
+      push(std::move(st));
+      absorbed[size_t(ni)] = absorbed[size_t(ai)] = absorbed[size_t(ri)] = true;
+      return true;
+    }
+    return false;
+  }
+
   // Whether linear node j will take the SwiGLU or residual path itself.
   bool would_fuse(int j) const {
     const Node& n = g.nodes[j];
@@ -734,6 +779,7 @@ struct Lowerer {
     } else if (p == "fused::all_reduce") {
       const uint32_t x = in(n, 0);
       if (!float_unary_ok(x, out) || !same_dims(x, out)) return decline("all_reduce needs f32 or bf16");
+      if (lower_allreduce_add_norm(ni)) return true;
       st.kind = SK::AllReduce;
       st.bf16 = is_bf16(V(x).dt);
       st.i[0] = V(x).elements();
@@ -1086,6 +1132,32 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
           const size_t bytes = size_t(st.i[0]) * (st.bf16 ? 2 : 4);
           if (cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s) != cudaSuccess) rc = SB_INTERNAL;
         }
+        break;
+      }
+      case SK::AllReduceAddNorm: {
+        // v = {x, r, gamma, h, y}: h = all_reduce(x) + r, y = rms_norm(h) * gamma.
+        const auto* x = P<uint16_t>(p, st.v[0]);
+        const auto* r = P<uint16_t>(p, st.v[1]);
+        const auto* gm = P<uint16_t>(p, st.v[2]);
+        auto* h = P<uint16_t>(p, st.v[3]);
+        auto* y = P<uint16_t>(p, st.v[4]);
+        const int64_t rows = st.i[0], cols = st.i[1];
+        if (ctx.ar_ready && sb::allreduce_add_norm_supported(rows, cols, x, r, gm, h, y, ctx.world)) {
+          rc = sb::launch_allreduce_add_norm_bf16(x, r, gm, h, y, rows, cols, float(st.d), ctx.rank, ctx.world,
+                                                  ctx.ar_peers, ctx.ar_counters, ctx.d_err, s);
+          break;
+        }
+        // Otherwise: the sum into y (free until the norm writes it), the add
+        // into h, the norm into y.
+        const uint16_t* sum = x;
+        if (ctx.comm && ctx.world > 1) {
+          const ncclResult_t e = ctx.nccl.all_reduce(x, y, size_t(rows * cols), ncclBfloat16, ncclSum, ctx.comm, s);
+          if (e != ncclSuccess)
+            fail(STRATA_INTERNAL, std::string("ncclAllReduce failed: ") + ctx.nccl.error_string(e));
+          sum = y;
+        }
+        rc = sb::launch_binary<uint16_t>(0, sum, r, h, st.bs, s);
+        if (rc == 0) rc = sb::launch_rms_norm<uint16_t>(h, gm, rows, cols, float(st.d), y, s);
         break;
       }
       case SK::Quant4:

@@ -22,17 +22,30 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_multi_gpu_tensor_parallel_decode_matches_unsharded(tmp_path, world):
+def _run_tp(tmp_path, world, mode):
     import torch
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     out = tmp_path / "tp.npy"
     cmd = ["timeout", "-k", "20", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(ROOT, "tests", "tp_worker.py"), str(out)]
+           os.path.join(ROOT, "tests", "tp_worker.py"), str(out), mode]
     r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     got, want = np.load(out)
     err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
-    assert err <= TOL_BF16, f"{world}-GPU tensor-parallel logits differ from unsharded by {err:.3e}"
+    assert err <= TOL_BF16, f"{world}-GPU tensor-parallel {mode} logits differ from unsharded by {err:.3e}"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_multi_gpu_tensor_parallel_decode_matches_unsharded(tmp_path, world):
+    """Decode rows: the residual all-reduces run as the fused NVLink
+    all-reduce + add + RMSNorm kernel."""
+    _run_tp(tmp_path, world, "decode")
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_multi_gpu_tensor_parallel_prefill_matches_unsharded(tmp_path, world):
+    """Prefill rows (80, more than the fused kernel takes): NCCL all-reduce,
+    then the add and the RMSNorm as their own kernels."""
+    _run_tp(tmp_path, world, "prefill")

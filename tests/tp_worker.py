@@ -3,8 +3,13 @@ torchrun by tests/test_gpu_tp.py.
 
 Every rank builds the same full (unsharded) weights of a small GQA decoder
 from fixed seeds, keeps its own shard (column-parallel q/k/v/gate/up,
-row-parallel o/down), joins the plugin's NCCL group and runs one decode step
-through the plugin.  Rank 0 writes its logits and the oracle's logits of the
+row-parallel o/down), joins the plugin's NCCL group and runs one step through
+the plugin: a decode step of 4 rows (the residual all-reduces run fused with
+the add and RMSNorm that follow them, over NVLink) or, with ``prefill`` as the
+second argument, a prefill of 2 x 40 rows (more rows than the fused kernel
+takes: NCCL, then the add and the norm).  The step runs three times and every
+run must give the same logits (the exchange's flags and slots alternate
+between runs).  Rank 0 writes its logits and the oracle's logits of the
 unsharded step to the path given on the command line."""
 import datetime
 import os
@@ -27,21 +32,25 @@ from tests.helpers import seeded_graph_inputs, to_device_bytes  # noqa: E402
 
 # 16 query / 8 kv heads of 128, FFN 5632: every tensor splits evenly over 2, 4 or 8 ranks.
 SHAPE = DecoderShape(2048, 16, 8, 128, 5632, 512, 2)
-BATCH, MAX_LEN, FILL = 4, 136, 128
+MAX_LEN = 136
 
 
-def main(out_path):
+def main(out_path, mode):
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ["LOCAL_RANK"])
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     os.environ["STRATA_B200_DEVICE"] = str(local)
 
-    full_g, full_hd = decoder_graph(SHAPE, batch=BATCH, seq=1, max_len=MAX_LEN, fmt="w4g32", head="logits")
-    full = seeded_graph_inputs(full_g, cache_fill=FILL)
-    full[full_hd.tokens] = ora.uniform_i32(2, BATCH, 0, SHAPE.vocab)
-    full[full_hd.pos] = np.array([FILL - i for i in range(BATCH)], np.int32)
+    batch, seq, fill = (2, 40, 0) if mode == "prefill" else (4, 1, 128)
+    full_g, full_hd = decoder_graph(SHAPE, batch=batch, seq=seq, max_len=MAX_LEN, fmt="w4g32", head="logits")
+    full = seeded_graph_inputs(full_g, cache_fill=fill)
+    full[full_hd.tokens] = ora.uniform_i32(2, batch * seq, 0, SHAPE.vocab)
+    if seq == 1:
+        full[full_hd.pos] = np.array([fill - i for i in range(batch)], np.int32)
+    else:
+        full[full_hd.pos] = np.tile(np.arange(seq, dtype=np.int32), batch)
 
-    g, hd = decoder_graph(SHAPE, batch=BATCH, seq=1, max_len=MAX_LEN, fmt="w4g32", head="logits",
+    g, hd = decoder_graph(SHAPE, batch=batch, seq=seq, max_len=MAX_LEN, fmt="w4g32", head="logits",
                           tp_rank=rank, tp_world=world)
     host = {hd.tokens: full[full_hd.tokens], hd.pos: full[full_hd.pos],
             hd.embed_table: full[full_hd.embed_table], hd.final_norm: full[full_hd.final_norm],
@@ -64,8 +73,13 @@ def main(out_path):
             arena[i] = Device(b)
     exe = plugin.compile(g)
     assert exe is not None, "the plugin declined the shard graph"
-    exe.run(arena)
-    got = np.asarray(arena[hd.out])
+    runs = []
+    for _ in range(3):
+        exe.run(arena)
+        runs.append(np.array(arena[hd.out]))
+    for i, r in enumerate(runs[1:], 1):
+        assert np.array_equal(r, runs[0]), f"rank {rank}: run {i} differs from run 0"
+    got = runs[0]
     if g.values[hd.out].dtype == BF16:
         got = ora.from_bf16(got.view(np.uint16))
     exe.free()
@@ -81,4 +95,4 @@ def main(out_path):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1])
+    main(sys.argv[1], sys.argv[2] if len(sys.argv) > 2 else "decode")
