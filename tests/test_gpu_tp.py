@@ -27,10 +27,13 @@ def _run_tp(tmp_path, world, mode):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     out = tmp_path / "tp.npy"
-    cmd = ["timeout", "-k", "20", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
-           os.path.join(ROOT, "tests", "tp_worker.py"), str(out), mode]
-    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+    for _ in range(3):  # a port picked free can be taken before torchrun binds it
+        cmd = ["timeout", "-k", "20", "400", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               "--nproc-per-node", str(world), "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+               os.path.join(ROOT, "tests", "tp_worker.py"), str(out), mode]
+        r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+        if r.returncode == 0 or "EADDRINUSE" not in r.stderr:
+            break
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
     got, want = np.load(out)
     err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
