@@ -5,7 +5,10 @@
 // grid is persistent (at most one wave of resident blocks); block b computes
 // tiles b, b + grid, b + 2 grid, ...  Within a tile the 8 warps split K into 8
 // slices of whole 32-code groups and the 8 partial fragments are summed
-// through shared memory by finish_tile.
+// through shared memory by finish_tile.  (Splitting a tile's K over the CTAs
+// of a cluster, with the partial sums merged through distributed shared
+// memory, measured slower on most 7B shapes and at best 9 % faster on one:
+// the per-tile cluster barrier costs about what the shorter slices save.)
 //
 // Memory pipeline.  Each warp copies its slice of the 16 weight rows to its
 // own shared-memory ring with 16-byte cp.async (a row's slice is contiguous,
@@ -114,27 +117,12 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Sum the 8 K-slice partials of one tile through shared memory and run the
-// epilogue.  Every thread of the block calls this once per tile.
-template <int FMT, int NT, int MODE, bool kTrailingSync>
-__device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
-                                            float (&red)[kWarps][kTileRows][8 * NT],
-                                            const float (&acc)[NT][4], int warp, int g, int q, int tid) {
-#pragma unroll
-  for (int t = 0; t < NT; ++t) {
-    *reinterpret_cast<float2*>(&red[warp][g][t * 8 + 2 * q]) = make_float2(acc[t][0], acc[t][1]);
-    *reinterpret_cast<float2*>(&red[warp][g + 8][t * 8 + 2 * q]) = make_float2(acc[t][2], acc[t][3]);
-  }
-  __syncthreads();
-  const int items = 8 * p.m;
-  for (int it = tid; it < items; it += kWarps * 32) {
-    const int pp = it / p.m, m = it - pp * p.m;
-    float vlo = 0.0f, vhi = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      vlo += red[w][pp][m];
-      vhi += red[w][pp + 8][m];
-    }
+// The epilogue of output pair (tile row pp, pp + 8) for x row m: vlo / vhi are
+// the finished dot products.
+template <int FMT, int MODE>
+__device__ __forceinline__ void tile_epilogue(const Params& p, const TileRows& tr, int pp, int m, float vlo,
+                                              float vhi) {
+  {
     const int jl = tr.job_lo, nlo = tr.row_lo + pp, jh = tr.job_hi, nhi = tr.row_hi + pp;
     if (FMT == 1) {
       vlo *= reinterpret_cast<const float*>(p.s[jl])[nlo];
@@ -186,6 +174,31 @@ __device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
         }
       }
     }
+  }
+}
+
+// Sum the 8 K-slice partials of one tile through shared memory and run the
+// epilogue.  Every thread of the block calls this once per tile.
+template <int FMT, int NT, int MODE, bool kTrailingSync>
+__device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
+                                            float (&red)[kWarps][kTileRows][8 * NT],
+                                            const float (&acc)[NT][4], int warp, int g, int q, int tid) {
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    *reinterpret_cast<float2*>(&red[warp][g][t * 8 + 2 * q]) = make_float2(acc[t][0], acc[t][1]);
+    *reinterpret_cast<float2*>(&red[warp][g + 8][t * 8 + 2 * q]) = make_float2(acc[t][2], acc[t][3]);
+  }
+  __syncthreads();
+  const int items = 8 * p.m;
+  for (int it = tid; it < items; it += kWarps * 32) {
+    const int pp = it / p.m, m = it - pp * p.m;
+    float vlo = 0.0f, vhi = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      vlo += red[w][pp][m];
+      vhi += red[w][pp + 8][m];
+    }
+    tile_epilogue<FMT, MODE>(p, tr, pp, m, vlo, vhi);
   }
   // A single buffer is rewritten by the next tile; with two buffers the next
   // tile's barrier already orders this tile's reads before the reuse.
@@ -342,27 +355,21 @@ __global__ void __launch_bounds__(kWarps * 32, NT <= 2 ? 3 : 2) gemv_mma_kernel(
       const int nj = min(kChunk, ng - c * kChunk);
       if constexpr (FMT == 0) {
         if (NT == 1 && nj == kChunk) {
-          // Full chunk, in halves of four groups: every shared-memory and x
-          // load of the half first, then the math with no branches, so that
-          // the groups' chains interleave.
+          // Full chunk, two groups at a time: the pair's shared-memory and x
+          // loads first, then its math with no branches.
 #pragma unroll
-          for (int hb = 0; hb < kChunk; hb += 4) {
-            uint32_t f[2][4], sp[2][2];
-            uint4 xv[NT][4];
-#pragma unroll
-            for (int j2 = 0; j2 < 2; ++j2) {
-              ldsm_x4(f[j2], st + piece_off<0>((mi & 1) * 8 + rr, hb + 2 * j2 + (mi >> 1)));
-              sp[j2][0] = lds32(st + S::kW + g * (kChunk * 2) + (hb + 2 * j2) * 2);
-              sp[j2][1] = lds32(st + S::kW + (g + 8) * (kChunk * 2) + (hb + 2 * j2) * 2);
-            }
+          for (int hb = 0; hb < kChunk; hb += 2) {
+            uint32_t f[4];
+            uint4 xv[NT][2];
+            ldsm_x4(f, st + piece_off<0>((mi & 1) * 8 + rr, hb + (mi >> 1)));
+            const uint32_t slo = lds32(st + S::kW + g * (kChunk * 2) + hb * 2);
+            const uint32_t shi = lds32(st + S::kW + (g + 8) * (kChunk * 2) + hb * 2);
 #pragma unroll
             for (int t = 0; t < NT; ++t)
 #pragma unroll
-              for (int j = 0; j < 4; ++j) xv[t][j] = ldg16(xbase[t] + (c * kChunk + hb + j) * 32);
+              for (int j = 0; j < 2; ++j) xv[t][j] = ldg16(xbase[t] + (c * kChunk + hb + j) * 32);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              int4_group<NT>(acc, f[j >> 1][2 * (j & 1)], f[j >> 1][2 * (j & 1) + 1], sp[j >> 1][0],
-                             sp[j >> 1][1], j & 1, xv, j);
+            for (int j = 0; j < 2; ++j) int4_group<NT>(acc, f[2 * j], f[2 * j + 1], slo, shi, j, xv, j);
           }
         } else {
 #pragma unroll
@@ -416,8 +423,10 @@ __global__ void __launch_bounds__(kWarps * 32, NT <= 2 ? 3 : 2) gemv_mma_kernel(
   cp_async_wait<0>();
 }
 
+// Launch one x-row block: p holds everything but the K-slices and the grid.
+// scale16_ok: every job's int4 scale rows are 16-byte aligned.
 template <int FMT, int NT, int MODE>
-int launch_one(const Params& p, int blocks, bool pdl, cudaStream_t st) {
+int launch_one(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
   auto kern = gemv_mma_kernel<FMT, NT, MODE>;
   const size_t smem = kWarps * warp_smem_bytes(FMT);
   static int per_sm = 0;
@@ -428,10 +437,15 @@ int launch_one(const Params& p, int blocks, bool pdl, cudaStream_t st) {
         per_sm < 1)
       per_sm = 1;
   }
+  p.gpw = (p.groups + kWarps - 1) / kWarps;
+  p.gpw += p.gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
+  // Whole 8-group slices (K a multiple of 2048): each row's scales of a chunk
+  // are one aligned 16-byte copy.
+  p.scale16 = FMT == 0 && scale16_ok && p.groups % (8 * kWarps) == 0 ? 1 : 0;
   // Persistent: at most one full wave of blocks, each walking tiles.
-  const int grid = blocks < per_sm * kNumSMs ? blocks : per_sm * kNumSMs;
+  const int slots = per_sm * kNumSMs;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.gridDim = dim3(unsigned(p.tiles < slots ? p.tiles : slots), 1, 1);
   cfg.blockDim = dim3(kWarps * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -446,22 +460,22 @@ int launch_one(const Params& p, int blocks, bool pdl, cudaStream_t st) {
 }
 
 template <int FMT, int NT>
-int dispatch_mode(GemvMode mode, const Params& p, int blocks, bool pdl, cudaStream_t st) {
+int dispatch_mode(GemvMode mode, const Params& p, bool scale16_ok, bool pdl, cudaStream_t st) {
   switch (mode) {
-    case GemvMode::Plain: return launch_one<FMT, NT, 0>(p, blocks, pdl, st);
-    case GemvMode::SwiGLU: return launch_one<FMT, NT, 1>(p, blocks, pdl, st);
-    case GemvMode::QkvRope: return launch_one<FMT, NT, 2>(p, blocks, pdl, st);
+    case GemvMode::Plain: return launch_one<FMT, NT, 0>(p, scale16_ok, pdl, st);
+    case GemvMode::SwiGLU: return launch_one<FMT, NT, 1>(p, scale16_ok, pdl, st);
+    case GemvMode::QkvRope: return launch_one<FMT, NT, 2>(p, scale16_ok, pdl, st);
   }
   return SB_INVALID_ARGUMENT;
 }
 
 // x rows per launch: n-tiles of 8 (1, 2, 4 or 8 of them).
 template <int FMT>
-int dispatch_nt(const Params& p, GemvMode mode, int blocks, bool pdl, cudaStream_t st) {
-  if (p.m <= 8) return dispatch_mode<FMT, 1>(mode, p, blocks, pdl, st);
-  if (p.m <= 16) return dispatch_mode<FMT, 2>(mode, p, blocks, pdl, st);
-  if (p.m <= 32) return dispatch_mode<FMT, 4>(mode, p, blocks, pdl, st);
-  return dispatch_mode<FMT, 8>(mode, p, blocks, pdl, st);
+int dispatch_nt(const Params& p, GemvMode mode, bool scale16_ok, bool pdl, cudaStream_t st) {
+  if (p.m <= 8) return dispatch_mode<FMT, 1>(mode, p, scale16_ok, pdl, st);
+  if (p.m <= 16) return dispatch_mode<FMT, 2>(mode, p, scale16_ok, pdl, st);
+  if (p.m <= 32) return dispatch_mode<FMT, 4>(mode, p, scale16_ok, pdl, st);
+  return dispatch_mode<FMT, 8>(mode, p, scale16_ok, pdl, st);
 }
 
 }  // namespace
@@ -512,12 +526,9 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
   const LinearBatch& b = a.lb;
   const int fmt = b.fmt == WFormat::W4G32 ? 0 : 1;
   const int groups = b.k / 32;
-  int gpw = (groups + kWarps - 1) / kWarps;
-  gpw += gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
-  // Whole 8-group slices (K a multiple of 2048): each row's scales of a chunk
-  // are one aligned 16-byte copy.
-  bool scale16 = fmt == 0 && groups % (8 * kWarps) == 0;
-  for (int j = 0; j < b.njobs && scale16; ++j) scale16 = (reinterpret_cast<uintptr_t>(b.jobs[j].s) & 15) == 0;
+  bool scale16_ok = fmt == 0;
+  for (int j = 0; j < b.njobs && scale16_ok; ++j)
+    scale16_ok = (reinterpret_cast<uintptr_t>(b.jobs[j].s) & 15) == 0 && (int64_t(groups) * 2) % 16 == 0;
   int rows = 0;
   switch (a.mode) {
     case GemvMode::Plain:
@@ -534,7 +545,6 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
     p.x = b.x + int64_t(m0) * b.k;
     p.k = b.k;
     p.groups = groups;
-    p.gpw = gpw;
     p.njobs = b.njobs;
     for (int j = 0; j < b.njobs; ++j) {
       const LinearJob& J = b.jobs[j];
@@ -547,7 +557,6 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
     p.qkv = a.qkv;
     p.m_base = m0;
     p.tiles = blocks;
-    p.scale16 = scale16 ? 1 : 0;
     if (a.mode == GemvMode::QkvRope) {
       const QkvExtra& e = a.qkv;
       p.qkv.pos = e.pos + m0;
@@ -557,9 +566,9 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
     }
     int rc;
     if (fmt == 0)
-      rc = dispatch_nt<0>(p, a.mode, blocks, a.pdl, st);
+      rc = dispatch_nt<0>(p, a.mode, scale16_ok, a.pdl, st);
     else
-      rc = dispatch_nt<1>(p, a.mode, blocks, a.pdl, st);
+      rc = dispatch_nt<1>(p, a.mode, scale16_ok, a.pdl, st);
     if (rc) return rc;
   }
   return SB_OK;
