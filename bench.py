@@ -3,6 +3,10 @@
 One step = one decode token for every sequence of the batch through all 32
 layers plus the int4 lm_head and argmax, with a 2048-entry KV cache
 prefilled, run through the plugin ABI (libstrata_b200.so, strata_plugin_v1).
+``--model 70b`` runs the 70B-shape stack instead (80 layers, hidden 8192,
+64 query / 8 kv heads, FFN 28672, int4 g32) at batch 32 with a 4096-entry KV
+cache; its vocabulary is not specified, so that step has no embedding and no
+lm_head (hidden states in, hidden states out).
 
   value  device-timed tokens/s: CUDA events on the plugin's stream around K
          CUDA-graph replays, inputs resident in HBM (max over ranks).
@@ -33,26 +37,30 @@ for _p in (ROOT, PKG):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-from strata_host.blocks import LLAMA_7B, decoder_graph  # noqa: E402
+from strata_host.blocks import LLAMA_7B, LLAMA_70B, decoder_graph  # noqa: E402
 
 METRIC = "decode tokens/s, 7B-shape int4 g32 stack"
 KV_FILL = 2048            # prefilled cache entries; the new token sits at position 2048
-MAX_LEN = 2112            # cache capacity per sequence
+# --model: shape, default batch, prefilled KV entries, metric name
+MODELS = {
+    "7b": (LLAMA_7B, 8, KV_FILL, METRIC),
+    "70b": (LLAMA_70B, 32, 4096, "decode tokens/s, 70B-shape int4 g32 stack (no embedding / lm_head)"),
+}
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # DRAM bytes read + written by one gate/up GEMV launch (M = 1), from the ncu
 # capture summarised in profiles/gemv_w4g32_swiglu_m1.md.
 GATEUP_TRAFFIC_BYTES = 50_759_168 + 21_248
 
 
-def step_bytes(shape, batch, tp=1):
+def step_bytes(shape, batch, kv_fill=KV_FILL):
     """Algorithmic HBM bytes of one decode step (whole job): every int4
-    weight and bf16 scale once, the KV cache read over KV_FILL + 1 positions,
+    weight and bf16 scale once, the KV cache read over kv_fill + 1 positions,
     the new k/v rows written."""
     D, H, G, d, F, V, L = (shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn,
                            shape.vocab, shape.layers)
     mats = [(H * d, D), (G * d, D), (G * d, D), (D, H * d), (F, D), (F, D), (D, F)]
     w = sum(n * k // 2 + n * (k // 32) * 2 for n, k in mats) * L + V * D // 2 + V * (D // 32) * 2
-    kv = 2 * batch * G * (KV_FILL + 1) * d * 2 * L
+    kv = 2 * batch * G * (kv_fill + 1) * d * 2 * L
     return w + kv
 
 
@@ -125,15 +133,21 @@ class ClockSampler:
 # the B200 arm
 # ---------------------------------------------------------------------------
 class Model:
-    """A 7B-shape int4 stack resident on one GPU (one tensor-parallel shard)."""
+    """A decoder stack resident on one GPU (one tensor-parallel shard).  A
+    shape without a vocabulary has no embedding and no head: its step input
+    is the hidden state and its output the last layer's hidden state."""
 
-    def __init__(self, plugin, torch, batch, rank, world, layers, fmt="w4g32", seq=1, head="argmax"):
+    def __init__(self, plugin, torch, batch, rank, world, layers, fmt="w4g32", seq=1, head="argmax",
+                 shape=LLAMA_7B, kv_fill=KV_FILL):
         from strata_host import Device
         self.plugin, self.torch, self.batch, self.seq = plugin, torch, batch, seq
         prefill = seq > 1
-        max_len = seq if prefill else MAX_LEN
-        g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=seq, max_len=max_len, fmt=fmt, layers=layers,
-                              head=head, tp_rank=rank, tp_world=world, last_token=prefill)
+        max_len = seq if prefill else kv_fill + 64
+        self.embed = shape.vocab > 0
+        if not self.embed:
+            head = "none"
+        g, hd = decoder_graph(shape, batch=batch, seq=seq, max_len=max_len, fmt=fmt, layers=layers,
+                              embed=self.embed, head=head, tp_rank=rank, tp_world=world, last_token=prefill)
         self.graph, self.hd = g, hd
         lib = C.CDLL(plugin.path)
         q4 = lib.strata_b200_quant_w4g32
@@ -175,7 +189,7 @@ class Model:
             elif v.name.endswith("cache"):
                 c = torch.zeros(v.dims, dtype=torch.bfloat16, device=dev)
                 if not prefill:
-                    c[:, :, :KV_FILL].normal_(generator=gen)
+                    c[:, :, :kv_fill].normal_(generator=gen)
                 self.tensors[i] = c
             elif "norm" in v.name:
                 self.tensors[i] = (1 + 0.02 * torch.randn(v.dims, generator=gen, device=dev)).to(torch.bfloat16)
@@ -185,9 +199,10 @@ class Model:
         if prefill:  # each prompt from position 0
             self.tensors[hd.pos].copy_(torch.arange(seq, device=dev, dtype=torch.int32).repeat(batch))
         else:
-            self.tensors[hd.pos].fill_(KV_FILL)
-        ids = torch.randint(0, LLAMA_7B.vocab, (batch * seq,), generator=gen, device=dev, dtype=torch.int32)
-        self.tensors[hd.tokens].copy_(ids)
+            self.tensors[hd.pos].fill_(kv_fill)
+        if self.embed:
+            ids = torch.randint(0, shape.vocab, (batch * seq,), generator=gen, device=dev, dtype=torch.int32)
+            self.tensors[hd.tokens].copy_(ids)
         for i, t in self.tensors.items():
             b = plugin.wrap(t.data_ptr(), t.numel() * t.element_size())
             self.bufs.append(b)
@@ -208,20 +223,22 @@ class Model:
         self.tensors.clear()
 
 
-def dominant_kernel(plugin, torch, reps=32):
+def dominant_kernel(plugin, torch, shape=LLAMA_7B, m=1, tp=1, reps=32):
     """Time the gate/up + SwiGLU int4 GEMV launch (the largest weight stream of
-    the step) over 32 distinct weight sets, on the plugin's stream."""
+    the step) over `reps` distinct weight sets (more bytes than L2 holds), on
+    the plugin's stream: x [m, hidden], one tensor-parallel shard's rows."""
     from strata_host import BF16, W4G32, Device, GraphBuilder, Op
-    D, F = LLAMA_7B.hidden, LLAMA_7B.ffn
+    D, F = shape.hidden, shape.ffn // tp
+    reps = max(2, min(reps, int(2.5e9 // (F * D))))
     b = GraphBuilder("gateup")
-    x = b.input(BF16, (1, D), "x")
+    x = b.input(BF16, (m, D), "x")
     outs = []
     for i in range(reps):
         wg, sg = b.input(W4G32, (F, D // 2), f"wg{i}"), b.input(BF16, (F, D // 32), f"sg{i}")
         wu, su = b.input(W4G32, (F, D // 2), f"wu{i}"), b.input(BF16, (F, D // 32), f"su{i}")
-        g_ = b.node(Op.custom("fused::linear_w4g32"), [x, wg, sg], [(BF16, (1, F))], {}, f"g{i}")[0]
-        u_ = b.node(Op.custom("fused::linear_w4g32"), [x, wu, su], [(BF16, (1, F))], {}, f"u{i}")[0]
-        s_ = b.node(Op.custom("fused::swiglu"), [g_, u_], [(BF16, (1, F))], {}, f"s{i}")[0]
+        g_ = b.node(Op.custom("fused::linear_w4g32"), [x, wg, sg], [(BF16, (m, F))], {}, f"g{i}")[0]
+        u_ = b.node(Op.custom("fused::linear_w4g32"), [x, wu, su], [(BF16, (m, F))], {}, f"u{i}")[0]
+        s_ = b.node(Op.custom("fused::swiglu"), [g_, u_], [(BF16, (m, F))], {}, f"s{i}")[0]
         outs.append(s_)
     for o in outs:
         b.output(o)
@@ -250,7 +267,7 @@ def dominant_kernel(plugin, torch, reps=32):
     e1.record(stream)
     plugin.synchronize()
     per_launch_s = e0.elapsed_time(e1) / 1e3 / (iters * reps)
-    bytes_per_launch = 2 * (F * D // 2 + F * (D // 32) * 2) + D * 2 + F * 2
+    bytes_per_launch = 2 * (F * D // 2 + F * (D // 32) * 2) + m * (D * 2 + F * 2)
     bound.release()
     exe.free()
     for bb in bufs:
@@ -261,46 +278,49 @@ def dominant_kernel(plugin, torch, reps=32):
 _CPU_INPUTS: dict = {}
 
 
-def cpu_baseline_sample(batch, threads, fraction=1):
-    """One 7B decode layer on the CPU oracle (all host threads), scaled to the
-    32-layer step plus the lm_head; returns tokens/s and what was timed.
+def cpu_baseline_sample(batch, threads, fraction=1, shape=LLAMA_7B, kv_fill=KV_FILL):
+    """One decode layer on the CPU oracle (all host threads), scaled to the
+    whole step (and the lm_head, where the shape has one); returns tokens/s
+    and what was timed.
 
-    ``fraction`` > 1 times only the first 1/fraction of every weight matrix's
-    rows and of the kv heads (each row / head costs the same) and scales the
+    ``fraction`` > 1 times 1/fraction of every weight matrix's rows and of
+    the query and kv heads (each row / head costs the same) and scales the
     time back up, to bound one sample's CPU time."""
     import numpy as np
 
     from oracle import oracle as ora
-    from tests.helpers import seeded_graph_inputs
-    key = (batch, fraction)
-    if key not in _CPU_INPUTS:  # generated once; only the kernels below are timed
-        g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=1, max_len=KV_FILL + 1, fmt="w4g32", layers=1,
-                              embed=False, head="none")
-        _CPU_INPUTS[key] = (hd, seeded_graph_inputs(g, cache_fill=KV_FILL))
-    hd, host = _CPU_INPUTS[key]
-    pos = np.full(batch, KV_FILL, np.int32)
-    W = {name: host[vid] for name, vid in hd.layers[0].ids.items()}
     f = fraction
-    G = LLAMA_7B.kv_heads // f
-    kc = np.ascontiguousarray(W["k_cache"][:, :G])
-    vc = np.ascontiguousarray(W["v_cache"][:, :G])
-    xs = {k: ora.round_bf16(ora.normal(0, (batch, W["w" + k].shape[1] * 2))) for k in "qkvogud"}
-    q = ora.round_bf16(ora.normal(3, (batch, G * LLAMA_7B.head_dim)))
-    lw, ls = ora.quant_w4g32(ora.normal(99, (LLAMA_7B.vocab // f, LLAMA_7B.hidden), std=0.02))
+    D, H, G, d, F, V = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn, shape.vocab
+    Hf, Gf = H // f, G // f
+    mats = {"q": (H * d, D), "k": (G * d, D), "v": (G * d, D), "o": (D, H * d), "g": (F, D), "u": (F, D),
+            "d": (D, F)}
+    key = (D, batch, f, kv_fill)
+    if key not in _CPU_INPUTS:  # generated once; only the kernels below are timed
+        W = {k: ora.quant_w4g32(ora.normal(10 + i, (n // f, kk), std=0.02)) for i, (k, (n, kk)) in
+             enumerate(mats.items())}
+        kc = ora.round_bf16(ora.normal(20, (batch, Gf, kv_fill + 1, d)))
+        vc = ora.round_bf16(ora.normal(21, (batch, Gf, kv_fill + 1, d)))
+        xs = {k: ora.round_bf16(ora.normal(0, (batch, kk))) for k, (n, kk) in mats.items()}
+        q = ora.round_bf16(ora.normal(3, (batch, Hf * d)))
+        lm = ora.quant_w4g32(ora.normal(99, (V // f, D), std=0.02)) if V else None
+        _CPU_INPUTS[key] = (W, kc, vc, xs, q, lm)
+    W, kc, vc, xs, q, lm = _CPU_INPUTS[key]
+    pos = np.full(batch, kv_fill, np.int32)
     t0 = time.perf_counter()
-    for key in "qkvogud":
-        n = W["w" + key].shape[0] // f
-        ora.linear_w4g32(xs[key], W["w" + key][:n], W["s" + key][:n], threads=threads)
-    ora.attention(q, kc, vc, np.arange(batch), pos, G, G, LLAMA_7B.head_dim, threads=threads)
+    for k in mats:
+        ora.linear_w4g32(xs[k], W[k][0], W[k][1], threads=threads)
+    ora.attention(q, kc, vc, np.arange(batch), pos, Hf, Gf, d, threads=threads)
     layer_s = (time.perf_counter() - t0) * f
-    t1 = time.perf_counter()
-    ora.linear_w4g32(xs["q"], lw, ls, threads=threads)
-    head_s = (time.perf_counter() - t1) * f
-    step_s = layer_s * LLAMA_7B.layers + head_s
-    part = "" if f == 1 else f" (first 1/{f} of every matrix's rows and of the kv heads, time x{f})"
+    head_s = 0.0
+    if lm is not None:
+        t1 = time.perf_counter()
+        ora.linear_w4g32(xs["q"], lm[0], lm[1], threads=threads)
+        head_s = (time.perf_counter() - t1) * f
+    step_s = layer_s * shape.layers + head_s
+    part = "" if f == 1 else f" (1/{f} of every matrix's rows and of the heads, time x{f})"
     return batch / step_s, (f"one decode layer at batch {batch}: 7 int4 linears + attention over "
-                            f"{KV_FILL + 1} positions{part}, scaled x{LLAMA_7B.layers}, plus the lm_head; "
-                            f"threaded C oracle, k-order f32")
+                            f"{kv_fill + 1} positions{part}, scaled x{shape.layers}"
+                            f"{', plus the lm_head' if lm is not None else ''}; threaded C oracle, k-order f32")
 
 
 def run_reference(args):
@@ -310,19 +330,21 @@ def run_reference(args):
     import numpy as np  # noqa: F401
     from oracle import oracle as ora
     threads = ora.max_threads()
+    shape, _, kv_fill, metric = MODELS[args.model]
     values = []
     sample = ""
     for i in range(args.warmup + args.steps):
-        tps, sample = cpu_baseline_sample(args.batch, threads, fraction=16)
+        tps, sample = cpu_baseline_sample(args.batch, threads, fraction=16 if args.model == "7b" else 8,
+                                          shape=shape, kv_fill=kv_fill)
         if i >= args.warmup:
             values.append(tps)
     v = statistics.median(values)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+    line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.batch / v * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights, f32 compute",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV)",
-            "config": {"workload": f"7B-shape int4 g32 decode, batch {args.batch}, KV 2048",
-                       "batch": args.batch, "kv_len": KV_FILL, "parallelism": "cpu"},
+            "config": {"workload": f"{args.model.upper()}-shape int4 g32 decode, batch {args.batch}, KV {kv_fill}",
+                       "batch": args.batch, "kv_len": kv_fill, "parallelism": "cpu"},
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -428,8 +450,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=8)
-    ap.add_argument("--layers", type=int, default=LLAMA_7B.layers)
+    ap.add_argument("--model", default="7b", choices=sorted(MODELS),
+                    help="7b: 7B-shape stack (default batch 8, KV 2048); 70b: 70B-shape stack (batch 32, KV 4096)")
+    ap.add_argument("--batch", type=int, default=None, help="sequences per step (default: per --model)")
+    ap.add_argument("--layers", type=int, default=None, help="layers (default: all of --model's)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill", action="store_true",
@@ -437,6 +461,13 @@ def main():
     ap.add_argument("--seq", type=int, default=2048, help="tokens per prompt with --prefill")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    shape, batch0, kv_fill, metric = MODELS[args.model]
+    if args.batch is None:
+        args.batch = batch0
+    if args.layers is None:
+        args.layers = shape.layers
+    if args.prefill and args.model != "7b":
+        ap.error("--prefill runs the 7B-shape int8 configuration only")
     if args.impl == "reference":
         return run_reference(args)
     if args.prefill:
@@ -462,7 +493,7 @@ def main():
         dist.broadcast(uid, 0)
         plugin.tp_init(rank, world, bytes(uid.cpu().numpy().tobytes()))
 
-    model = Model(plugin, torch, args.batch, rank, world, args.layers)
+    model = Model(plugin, torch, args.batch, rank, world, args.layers, shape=shape, kv_fill=kv_fill)
     stream = torch.cuda.ExternalStream(plugin.stream())
 
     def barrier():
@@ -498,17 +529,26 @@ def main():
     value = tokens / dev_s
 
     # ---- end to end through the ABI with host buffers ------------------------
-    ids_h = torch.zeros(args.batch, dtype=torch.int32).pin_memory()
-    pos_h = torch.full((args.batch,), KV_FILL, dtype=torch.int32).pin_memory()
-    out_h = torch.zeros(args.batch, dtype=torch.int32).pin_memory()
+    # Token ids (or, without an embedding, the bf16 hidden states) and the
+    # positions in; the next ids (or the last hidden states) out.
+    pos_h = torch.full((args.batch,), kv_fill, dtype=torch.int32).pin_memory()
+    if model.embed:
+        ids_h = torch.zeros(args.batch, dtype=torch.int32).pin_memory()
+        out_h = torch.zeros(args.batch, dtype=torch.int32).pin_memory()
+    else:
+        ids_h = torch.randn((args.batch, shape.hidden)).to(torch.bfloat16).pin_memory()
+        out_h = torch.zeros((args.batch, shape.hidden), dtype=torch.bfloat16).pin_memory()
+    n_in = ids_h.numel() * ids_h.element_size()
+    n_out = out_h.numel() * out_h.element_size()
     nb = args.batch * 4
 
     def e2e_step():
-        model.ids_buf.write_ptr(ids_h.data_ptr(), nb)
+        model.ids_buf.write_ptr(ids_h.data_ptr(), n_in)
         model.pos_buf.write_ptr(pos_h.data_ptr(), nb)
         model.bound.run()
-        model.out_buf.read_into(out_h.data_ptr(), nb)
-        ids_h.copy_(out_h)  # feed the predicted ids back as the next tokens
+        model.out_buf.read_into(out_h.data_ptr(), n_out)
+        if model.embed:
+            ids_h.copy_(out_h)  # feed the predicted ids back as the next tokens
 
     for _ in range(args.warmup):
         e2e_step()
@@ -526,33 +566,39 @@ def main():
 
     # ---- roofline of the dominant kernel and of the whole step ----------------
     peak, peak_kind = load_peaks()
-    k_s, k_bytes = dominant_kernel(plugin, torch)
+    k_m = 1 if args.model == "7b" else args.batch
+    k_s, k_bytes = dominant_kernel(plugin, torch, shape=shape, m=k_m, tp=world)
     k_gbs = k_bytes / k_s / 1e9
-    sb = step_bytes(LLAMA_7B, args.batch) * args.layers // LLAMA_7B.layers
+    sb = step_bytes(shape, args.batch, kv_fill) * args.layers // shape.layers
     step_gbs = sb / (ms_step / 1e3) / 1e9 / world
     clock = clocks.summary()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as ora
-        tps, sample = cpu_baseline_sample(args.batch, ora.max_threads())
+        tps, sample = cpu_baseline_sample(args.batch, ora.max_threads(), fraction=1 if args.model == "7b" else 8,
+                                          shape=shape, kv_fill=kv_fill)
         cpu = {"value": tps, "unit": "tokens/s", "cores": ora.max_threads(), "kind": "port", "sample": sample}
 
     if rank == 0:
+        F = shape.ffn // world
+        head = "int4 lm_head + argmax" if model.embed else "no embedding / lm_head"
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights (g32, bf16 scales), bf16 activations, f32 accumulate",
             "data": "synthetic: device-generated N(0,0.02) weights quantised by the plugin, N(0,1) bf16 KV",
-            "config": {"workload": f"7B-shape int4 g32 decode stack ({args.layers} layers + int4 lm_head + argmax), "
-                                   f"batch {args.batch}, KV cache 2048 prefilled",
-                       "batch": args.batch, "kv_len": KV_FILL, "layers": args.layers,
+            "config": {"workload": f"{args.model.upper()}-shape int4 g32 decode stack ({args.layers} layers, "
+                                   f"{head}), batch {args.batch}, KV cache {kv_fill} prefilled",
+                       "model": args.model, "batch": args.batch, "kv_len": kv_fill, "layers": args.layers,
                        "parallelism": f"tp{world}",
                        "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB streamed per step"},
-            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * nb, "d2h_bytes_per_step": nb},
-            "roofline": {"bound": "hbm", "kernel": "w4g32 gate/up GEMV + SwiGLU epilogue, M=1, N=2x11008, K=4096",
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": n_in + nb, "d2h_bytes_per_step": n_out},
+            "roofline": {"bound": "hbm",
+                         "kernel": f"w4g32 gate/up GEMV + SwiGLU epilogue, M={k_m}, N=2x{F}, K={shape.hidden}",
                          "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
-                         "peak_kind": peak_kind, "traffic": GATEUP_TRAFFIC_BYTES,
+                         "peak_kind": peak_kind,
+                         "traffic": GATEUP_TRAFFIC_BYTES if (args.model, world) == ("7b", 1) else None,
                          "bytes_per_launch": k_bytes, "us_per_launch": k_s * 1e6},
             "step_roofline": {"bytes_per_step": sb, "achieved_gbs_per_gpu": step_gbs, "frac": step_gbs / peak,
                               "frac_of_8tbs": step_gbs / 8000.0},
