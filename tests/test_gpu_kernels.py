@@ -99,7 +99,7 @@ def _x_bf16(m, k, seed=0):
     return ora.to_bf16(ora.normal(seed, (m, k)))
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 128, 2048])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 32, 128, 2048])
 def test_linear_w4g32_matches_oracle(cuda, lib, m):
     """The quantized Linear sweep at K = N = 4096 (int4 group 32, bf16 scale)."""
     torch = cuda

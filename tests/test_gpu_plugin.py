@@ -214,9 +214,12 @@ def test_prefill_last_token_head_runs_on_each_sequence_last_row(cuda, plugin):
     assert np.array_equal(np.asarray(res[hd.out]), ora.argmax(logits))
 
 
-def test_llama70b_gqa_shard_decode(cuda, plugin):
-    """70B-shape GQA (64 q / 8 kv heads), one tensor-parallel shard of 8, KV 4096."""
-    g, hd, res, caches, ref = _decode_case(plugin, LLAMA_70B, 2, 1, 4160, 4096, tp_world=8, head="none")
+@pytest.mark.parametrize("batch", [2, 24])
+def test_llama70b_gqa_shard_decode(cuda, plugin, batch):
+    """70B-shape GQA (64 q / 8 kv heads), one tensor-parallel shard of 8, KV 4096.  Batch 24
+    takes the GEMV's two-tiles-per-item path (17-32 x rows) in the q/k/v + RoPE and the
+    gate/up + SwiGLU epilogues."""
+    g, hd, res, caches, ref = _decode_case(plugin, LLAMA_70B, batch, 1, 4160, 4096, tp_world=8, head="none")
     assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, "70B shard hidden")
 
 
