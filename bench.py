@@ -37,7 +37,7 @@ for _p in (ROOT, PKG):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-from strata_host.blocks import LLAMA_7B, LLAMA_70B, decoder_graph  # noqa: E402
+from strata_host.blocks import LLAMA_7B, LLAMA_70B, decoder_graph, ffn_shard  # noqa: E402
 
 METRIC = "decode tokens/s, 7B-shape int4 g32 stack"
 KV_FILL = 2048            # prefilled cache entries; the new token sits at position 2048
@@ -228,7 +228,7 @@ def dominant_kernel(plugin, torch, shape=LLAMA_7B, m=1, tp=1, reps=32):
     the step) over `reps` distinct weight sets (more bytes than L2 holds), on
     the plugin's stream: x [m, hidden], one tensor-parallel shard's rows."""
     from strata_host import BF16, W4G32, Device, GraphBuilder, Op
-    D, F = shape.hidden, shape.ffn // tp
+    D, F = shape.hidden, ffn_shard(shape.ffn, tp, 0)[1]
     reps = max(2, min(reps, int(2.5e9 // (F * D))))
     b = GraphBuilder("gateup")
     x = b.input(BF16, (m, D), "x")
@@ -581,7 +581,7 @@ def main():
         cpu = {"value": tps, "unit": "tokens/s", "cores": ora.max_threads(), "kind": "port", "sample": sample}
 
     if rank == 0:
-        F = shape.ffn // world
+        F = ffn_shard(shape.ffn, world, 0)[1]
         head = "int4 lm_head + argmax" if model.embed else "no embedding / lm_head"
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

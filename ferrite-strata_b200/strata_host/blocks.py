@@ -72,15 +72,34 @@ class DecoderHandles:
     hidden_out: int = -1
 
 
-def weight_shapes(shape: DecoderShape, fmt: str, tp_world: int = 1) -> dict:
+def ffn_shard(ffn: int, tp_world: int, tp_rank: int) -> tuple[int, int]:
+    """(first feature, features) of rank tp_rank's slice of the FFN.
+
+    Slices are whole units of 64 features (two int4 groups) where the FFN
+    allows it, so every rank's down_proj has an even number of 32-code
+    groups along K (the tensor-core GEMV's requirement); the first
+    (units % world) ranks take one unit more.  The 7B FFN of 11008 at 8
+    ranks splits as 4 x 1408 + 4 x 1344 instead of 8 x 1376 (43 groups).
+    Otherwise the FFN is split evenly."""
+    t, r = tp_world, tp_rank
+    if ffn % 64 == 0 and ffn // 64 >= t:
+        base, extra = divmod(ffn // 64, t)
+        return (r * base + min(r, extra)) * 64, (base + (1 if r < extra else 0)) * 64
+    if ffn % t:
+        raise ValueError("the ffn must divide by the tensor-parallel size")
+    return r * (ffn // t), ffn // t
+
+
+def weight_shapes(shape: DecoderShape, fmt: str, tp_world: int = 1, tp_rank: int = 0) -> dict:
     """Per-layer weight tensors (name -> (dtype, dims)) for one rank."""
-    D, H, G, d, F = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn
+    D, H, G, d = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim
     t = tp_world
-    if H % t or G % t or F % t:
-        raise ValueError("heads, kv heads and ffn must divide by the tensor-parallel size")
+    if H % t or G % t:
+        raise ValueError("heads and kv heads must divide by the tensor-parallel size")
+    Fr = ffn_shard(shape.ffn, t, tp_rank)[1]
     act = F32 if fmt == "f32" else BF16
     mats = {"q": (H // t * d, D), "k": (G // t * d, D), "v": (G // t * d, D), "o": (D, H // t * d),
-            "g": (F // t, D), "u": (F // t, D), "d": (D, F // t)}
+            "g": (Fr, D), "u": (Fr, D), "d": (D, Fr)}
     out = {"attn_norm": (act, (D,)), "ffn_norm": (act, (D,))}
     for key, (n, k) in mats.items():
         if fmt == "w4g32":
@@ -131,7 +150,7 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
     else:
         hd.tokens = b.input(act, (R, D), "x")
     hd.pos = b.input(I32, (R,), "pos")
-    wshapes = weight_shapes(shape, fmt, t)
+    wshapes = weight_shapes(shape, fmt, t, tp_rank)
     for li in range(layers):
         W = {k: b.input(dt, dims, f"l{li}.{k}") for k, (dt, dims) in wshapes.items()}
         W["k_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.k_cache")
@@ -153,7 +172,7 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
         h = b.node(Op.custom("fused::embed"), [hd.tokens, hd.embed_table], [(act, (R, D))], {}, "embed")[0]
     else:
         h = hd.tokens
-    Hl, Gl, Fl = H // t, G // t, shape.ffn // t
+    Hl, Gl, Fl = H // t, G // t, ffn_shard(shape.ffn, t, tp_rank)[1]
     for li, L in enumerate(hd.layers):
         W = L.ids
         p = f"l{li}."
@@ -217,10 +236,12 @@ def shard_layer(full: dict, shape: DecoderShape, fmt: str, rank: int, world: int
     scales [N], or plain [N, K] weights.  Column-parallel matrices keep rows
     [r*N/t, (r+1)*N/t); row-parallel ones keep columns [r*K/t, (r+1)*K/t) of
     the codes and the matching scale groups (per-channel int8 scales belong
-    to the unsharded output rows and are kept whole).  KV caches keep their
-    rank's kv heads.
+    to the unsharded output rows and are kept whole).  The FFN dimension
+    (gate/up rows, down_proj columns) follows ``ffn_shard`` instead.  KV
+    caches keep their rank's kv heads.
     """
     t, r = world, rank
+    f0, fn = ffn_shard(shape.ffn, t, r)
     out = {}
     for name, arr in full.items():
         if name in ("attn_norm", "ffn_norm"):
@@ -231,11 +252,17 @@ def shard_layer(full: dict, shape: DecoderShape, fmt: str, rank: int, world: int
         else:
             kind, key = name[0], name[1:]
             if key in _COLUMN_PARALLEL:
-                n = arr.shape[0] // t
-                out[name] = arr[r * n:(r + 1) * n].copy()
+                if key in ("g", "u"):
+                    out[name] = arr[f0:f0 + fn].copy()
+                else:
+                    n = arr.shape[0] // t
+                    out[name] = arr[r * n:(r + 1) * n].copy()
             elif key in _ROW_PARALLEL:
                 if kind == "s" and fmt == "w8pc":
                     out[name] = arr  # per output channel: unsharded rows
+                elif key == "d":
+                    per = arr.shape[1] / shape.ffn  # array columns per feature: 1/2 codes, 1/32 scales, 1
+                    out[name] = arr[:, int(f0 * per):int((f0 + fn) * per)].copy()
                 else:
                     c = arr.shape[1] // t
                     out[name] = arr[:, r * c:(r + 1) * c].copy()

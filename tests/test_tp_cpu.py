@@ -70,3 +70,27 @@ def test_two_rank_tensor_parallel_step_matches_unsharded(tmp_path):
     got, want = np.load(path)
     err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
     assert err <= 2e-2, f"tensor-parallel logits differ from unsharded by {err:.3e}"
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ffn_shards_cover_the_ffn_with_even_group_counts(world):
+    """The 7B FFN (11008) at 8 ranks splits 4 x 1408 + 4 x 1344 (even int4 group counts for every
+    down_proj shard), and the shards of gate/up rows and down_proj codes / scales concatenate
+    back to the full matrices."""
+    import numpy as np
+
+    from strata_host.blocks import LLAMA_7B, DecoderShape, ffn_shard, shard_layer, weight_shapes
+    shape = DecoderShape(256, 8, 8, 32, 11008, 0, 1)
+    full = {}
+    for name, (dt, dims) in weight_shapes(shape, "w4g32").items():
+        full[name] = np.arange(int(np.prod(dims)), dtype=np.int64).reshape(dims)
+    shards = [shard_layer(full, shape, "w4g32", r, world) for r in range(world)]
+    for r in range(world):
+        f0, fn = ffn_shard(shape.ffn, world, r)
+        assert fn % 64 == 0 and (fn // 32) % 2 == 0
+        ws = weight_shapes(shape, "w4g32", world, r)
+        for name in ("wg", "sg", "wu", "su", "wd", "sd"):
+            assert shards[r][name].shape == ws[name][1], (name, r)
+    for name, axis in (("wg", 0), ("sg", 0), ("wu", 0), ("su", 0), ("wd", 1), ("sd", 1)):
+        assert np.array_equal(np.concatenate([s[name] for s in shards], axis=axis), full[name]), name
+    assert [ffn_shard(LLAMA_7B.ffn, 8, r)[1] for r in range(8)] == [1408] * 4 + [1344] * 4
