@@ -30,8 +30,9 @@ from strata_host import BF16, Device, Plugin  # noqa: E402
 from strata_host.blocks import DecoderShape, decoder_graph, shard_layer  # noqa: E402
 from tests.helpers import seeded_graph_inputs, to_device_bytes  # noqa: E402
 
-# 16 query / 8 kv heads of 128, FFN 5632: every tensor splits evenly over 2, 4 or 8 ranks.
-SHAPE = DecoderShape(2048, 16, 8, 128, 5632, 512, 2)
+# 16 query / 8 kv heads of 128, FFN 11008 (the 7B FFN: at 8 ranks its shards are 1408 and 1344
+# features, so the uneven FFN split is exercised).
+SHAPE = DecoderShape(2048, 16, 8, 128, 11008, 512, 2)
 MAX_LEN = 136
 
 
