@@ -314,6 +314,23 @@ static uint32_t sb_supports(void* ctx, const StrataPatternQuery* q) {
 // Compile (raw.rs:642-657)
 // ---------------------------------------------------------------------------
 
+// Decode a graph section and lower it; null when the plugin declines.
+static std::unique_ptr<StrataExecutable> compile_graph_section(const uint8_t* sec, size_t sec_len) {
+  auto holder = std::make_unique<StrataExecutable>();
+  holder->exe.g = decode_graph(sec, sec_len);
+  holder->exe.label = "b200::" + holder->exe.g.name;
+  std::string reason;
+  if (!lower(holder->exe.g, holder->exe, &reason)) return nullptr;
+  return holder;
+}
+
+static void check_blob_header(const StrataWireBlob& b, const char* what) {
+  if (b.magic != kMagic) fail(STRATA_INVALID_ARGUMENT, std::string("the ") + what + " blob has the wrong magic");
+  if (b.format_major != kFormatMajor)
+    fail(STRATA_INVALID_ARGUMENT, "unsupported wire format major " + std::to_string(b.format_major));
+  if (!b.data && b.payload_len) fail(STRATA_INVALID_ARGUMENT, std::string("null ") + what + " payload");
+}
+
 static int32_t sb_compile(void* ctx, const StrataCompileArgs* a, StrataExecutable** out_exe,
                           StrataError** out_error) {
   if (out_exe) *out_exe = nullptr;
@@ -324,22 +341,163 @@ static int32_t sb_compile(void* ctx, const StrataCompileArgs* a, StrataExecutabl
     if (a->struct_size < sizeof(StrataCompileArgs))
       fail(STRATA_INVALID_ARGUMENT, "StrataCompileArgs is shorter than this plugin's ABI");
     const StrataWireBlob& b = a->subgraph;
-    if (b.magic != kMagic) fail(STRATA_INVALID_ARGUMENT, "the subgraph blob has the wrong magic");
-    if (b.format_major != kFormatMajor)
-      fail(STRATA_INVALID_ARGUMENT, "unsupported wire format major " + std::to_string(b.format_major));
-    if (!b.data && b.payload_len) fail(STRATA_INVALID_ARGUMENT, "null subgraph payload");
+    check_blob_header(b, "subgraph");
     const uint8_t* sec = nullptr;
     size_t sec_len = 0;
     if (!find_section(b.data, size_t(b.payload_len), kSectionGraph, &sec, &sec_len))
       fail(STRATA_INVALID_ARGUMENT, "the subgraph blob carries no graph section");
-    auto holder = std::make_unique<StrataExecutable>();
-    holder->exe.g = decode_graph(sec, sec_len);
-    holder->exe.label = "b200::" + holder->exe.g.name;
-    std::string reason;
-    if (!lower(holder->exe.g, holder->exe, &reason)) return STRATA_DECLINED;  // nothing allocated
+    auto holder = compile_graph_section(sec, sec_len);
+    if (!holder) return STRATA_DECLINED;  // nothing allocated
     *out_exe = holder.release();
     return STRATA_OK;
   });
+}
+
+// ---------------------------------------------------------------------------
+// Ahead-of-time executables (raw.rs:760-788; the reference host does not call
+// these yet).  A serialised executable is a framed blob with two sections:
+//   kSectionB200Exe  u32 format version, u32 SM architecture (100),
+//                    u32 ABI major, u32 ABI minor, u64 plan fingerprint,
+//                    u32 steps, u64 workspace bytes, str label
+//   kSectionGraph    the executable's graph, in the reference's encoding.
+// Loading decodes and lowers the graph again and accepts the result only if
+// its plan has the recorded fingerprint, so a blob from a build that lowers
+// differently is refused rather than run.  Weights and caches stay run-time
+// buffers; CUDA graphs are captured on the loaded executable's first run.
+// abi_compatible answers OK or INVALID_ARGUMENT and touches no device.
+// ---------------------------------------------------------------------------
+
+constexpr uint32_t kExeFormat = 1, kExeArch = 100;
+
+// FNV-1a over everything the lowering decided.
+static uint64_t plan_fingerprint(const Exe& e) {
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&](uint64_t x) {
+    for (int k = 0; k < 8; ++k) {
+      h ^= (x >> (8 * k)) & 0xff;
+      h *= 1099511628211ull;
+    }
+  };
+  mix(e.steps.size());
+  mix(e.ws_bytes);
+  for (const Step& st : e.steps) {
+    mix(uint64_t(st.kind));
+    mix(st.bf16);
+    mix(st.v.size());
+    for (uint32_t v : st.v) mix(v);
+    for (int64_t i : st.i) mix(uint64_t(i));
+    uint64_t dbits;
+    std::memcpy(&dbits, &st.d, sizeof dbits);
+    mix(dbits);
+    mix(uint64_t(st.fmt));
+    mix(uint64_t(st.epi));
+    mix(uint64_t(st.njobs));
+    mix(st.scratch_bytes);
+    for (uint32_t v : st.reads) mix(v);
+    for (uint32_t v : st.writes) mix(v);
+  }
+  return h;
+}
+
+struct ExeHeader {
+  uint32_t format = 0, arch = 0, abi_major = 0, abi_minor = 0;
+  uint64_t fingerprint = 0;
+  uint32_t steps = 0;
+  uint64_t ws_bytes = 0;
+  std::string label;
+};
+
+static ExeHeader read_exe_header(const StrataWireBlob& b) {
+  check_blob_header(b, "executable");
+  const uint8_t* sec = nullptr;
+  size_t n = 0;
+  if (!find_section(b.data, size_t(b.payload_len), kSectionB200Exe, &sec, &n))
+    fail(STRATA_INVALID_ARGUMENT, "the blob is not a serialised B200 executable");
+  Reader r(sec, n);
+  ExeHeader h;
+  h.format = r.u32();
+  h.arch = r.u32();
+  h.abi_major = r.u32();
+  h.abi_minor = r.u32();
+  h.fingerprint = r.u64();
+  h.steps = r.u32();
+  h.ws_bytes = r.u64();
+  h.label = r.str();
+  if (h.format != kExeFormat) fail(STRATA_INVALID_ARGUMENT, "unknown serialised-executable format");
+  if (h.arch != kExeArch) fail(STRATA_INVALID_ARGUMENT, "the executable was built for another architecture");
+  if (h.abi_major != STRATA_ABI_MAJOR || h.abi_minor > STRATA_ABI_MINOR)
+    fail(STRATA_INVALID_ARGUMENT, "the executable was serialised under an incompatible ABI");
+  return h;
+}
+
+static int32_t sb_serialize(void* ctx, const StrataExecutable* e, StrataWireBlob* out) {
+  if (!ctx || !e || !out) return STRATA_INVALID_ARGUMENT;
+  try {
+    Writer hw;
+    hw.u32(kExeFormat);
+    hw.u32(kExeArch);
+    hw.u32(STRATA_ABI_MAJOR);
+    hw.u32(STRATA_ABI_MINOR);
+    hw.u64(plan_fingerprint(e->exe));
+    hw.u32(uint32_t(e->exe.steps.size()));
+    hw.u64(e->exe.ws_bytes);
+    hw.str(e->exe.label);
+    const std::vector<uint8_t> framed =
+        frame_sections({{kSectionB200Exe, std::move(hw.data())}, {kSectionGraph, encode_graph(e->exe.g)}});
+    uint8_t* data = new uint8_t[framed.size() + 1];
+    std::memcpy(data, framed.data(), framed.size());
+    data[framed.size()] = 0;
+    out->magic = kMagic;
+    out->format_major = kFormatMajor;
+    out->format_minor = kFormatMinor;
+    out->payload_len = framed.size();
+    out->data = data;
+    out->nul = 0;
+    return STRATA_OK;
+  } catch (const Failure& f) {
+    return f.code;
+  } catch (...) {
+    return STRATA_INTERNAL;
+  }
+}
+
+static int32_t sb_abi_compatible(void* ctx, const StrataWireBlob* blob) {
+  if (!ctx || !blob) return STRATA_INVALID_ARGUMENT;
+  try {
+    read_exe_header(*blob);
+    const uint8_t* sec = nullptr;
+    size_t n = 0;
+    if (!find_section(blob->data, size_t(blob->payload_len), kSectionGraph, &sec, &n))
+      return STRATA_INVALID_ARGUMENT;
+    return STRATA_OK;
+  } catch (const Failure& f) {
+    return f.code;
+  } catch (...) {
+    return STRATA_INVALID_ARGUMENT;
+  }
+}
+
+static int32_t sb_deserialize_load(void* ctx, const StrataWireBlob* blob, StrataExecutable** out_exe) {
+  if (out_exe) *out_exe = nullptr;
+  if (!ctx || !blob || !out_exe) return STRATA_INVALID_ARGUMENT;
+  try {
+    const ExeHeader h = read_exe_header(*blob);
+    const uint8_t* sec = nullptr;
+    size_t n = 0;
+    if (!find_section(blob->data, size_t(blob->payload_len), kSectionGraph, &sec, &n))
+      return STRATA_INVALID_ARGUMENT;
+    auto holder = compile_graph_section(sec, n);
+    if (!holder || plan_fingerprint(holder->exe) != h.fingerprint || holder->exe.steps.size() != h.steps)
+      return STRATA_INVALID_ARGUMENT;  // this build lowers the graph differently
+    *out_exe = holder.release();
+    return STRATA_OK;
+  } catch (const Failure& f) {
+    return f.code;
+  } catch (const WireError&) {
+    return STRATA_INVALID_ARGUMENT;
+  } catch (...) {
+    return STRATA_INTERNAL;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -806,8 +964,8 @@ __attribute__((visibility("default"))) StrataPluginV1 strata_plugin_v1 = {
     sb_free_blob,
     sb_plugin_init,
     sb_plugin_free,
-    nullptr,  // serialize
-    nullptr,  // deserialize_load
-    nullptr,  // abi_compatible
+    sb_serialize,
+    sb_deserialize_load,
+    sb_abi_compatible,
 };
 }  // extern "C"

@@ -366,4 +366,18 @@ std::vector<uint8_t> frame_payload(uint32_t kind, const std::vector<uint8_t>& se
   return std::move(w.data());
 }
 
+std::vector<uint8_t> frame_sections(const std::vector<std::pair<uint32_t, std::vector<uint8_t>>>& sections) {
+  Writer w;
+  w.u32(uint32_t(sections.size()));
+  uint64_t off = 4 + 20 * uint64_t(sections.size());  // relative to the start of the payload
+  for (const auto& s : sections) {
+    w.u32(s.first);
+    w.u64(off);
+    w.u64(s.second.size());
+    off += s.second.size();
+  }
+  for (const auto& s : sections) w.bytes(s.second.data(), s.second.size());
+  return std::move(w.data());
+}
+
 }  // namespace sbp

@@ -24,6 +24,9 @@ constexpr uint64_t kMagic = 0x3147415441525453ull;  // "STRATAG1" little-endian
 constexpr uint32_t kFormatMajor = 0, kFormatMinor = 1;
 constexpr uint32_t kGraphSchema = 1, kCapsSchema = 1;
 constexpr uint32_t kSectionGraph = 1, kSectionCaps = 2;
+// Ahead-of-time executables: a section of this plugin's own (outside the
+// reference's section kinds) that records the build and the lowered plan.
+constexpr uint32_t kSectionB200Exe = 0x45583242;  // "B2XE"
 constexpr int kMaxRank = 8;
 
 class Reader {
@@ -133,5 +136,7 @@ std::vector<uint8_t> encode_graph(const Graph& g);
 
 // A framed payload (count + table + sections) for one section.
 std::vector<uint8_t> frame_payload(uint32_t kind, const std::vector<uint8_t>& section);
+// The same for several sections, in order.
+std::vector<uint8_t> frame_sections(const std::vector<std::pair<uint32_t, std::vector<uint8_t>>>& sections);
 
 }  // namespace sbp

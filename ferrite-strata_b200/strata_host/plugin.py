@@ -247,6 +247,51 @@ class Plugin:
             return None
         raise self.take_error(out_err.value, rc)
 
+    # -- ahead-of-time executables (raw.rs:760-788) -------------------------
+    def _take_blob(self, blob) -> bytes:
+        payload = C.string_at(blob.data, blob.payload_len)
+        copy = abi.StrataWireBlob()  # freed through a copy of the header, as the host does
+        C.memmove(C.addressof(copy), C.addressof(blob), C.sizeof(blob))
+        self.vt.free_blob(self.ctx, C.byref(copy))
+        return payload
+
+    @staticmethod
+    def _as_blob(payload: bytes):
+        buf = (C.c_uint8 * (len(payload) + 1)).from_buffer_copy(payload + b"\0")
+        b = abi.StrataWireBlob()
+        b.magic = abi.MAGIC
+        b.format_major = abi.FORMAT_MAJOR
+        b.format_minor = abi.FORMAT_MINOR
+        b.payload_len = len(payload)
+        b.data = C.cast(buf, C.POINTER(C.c_uint8))
+        return b, buf
+
+    def serialize(self, exe: "Executable") -> bytes:
+        """serialize: the payload (framed sections) of an opaque executable blob."""
+        blob = abi.StrataWireBlob()
+        rc = self.vt.serialize(self.ctx, exe.handle, C.byref(blob))
+        if rc != abi.OK:
+            raise StrataError(rc, f"serialize returned {abi.STATUS_NAMES.get(rc, rc)}")
+        return self._take_blob(blob)
+
+    def abi_compatible(self, payload: bytes) -> bool:
+        """abi_compatible: whether this plugin can load the blob (no device work)."""
+        b, keep = self._as_blob(payload)
+        return self.vt.abi_compatible(self.ctx, C.byref(b)) == abi.OK
+
+    def deserialize(self, payload: bytes, graph: Graph) -> "Executable":
+        """deserialize_load: the executable a blob from ``serialize`` describes.
+        ``graph`` is the host's copy of the executable's graph (value metadata
+        for ``run``)."""
+        b, keep = self._as_blob(payload)
+        out = C.c_void_p()
+        rc = self.vt.deserialize_load(self.ctx, C.byref(b), C.byref(out))
+        if rc != abi.OK:
+            raise StrataError(rc, f"deserialize_load returned {abi.STATUS_NAMES.get(rc, rc)}")
+        exe = Executable(self, out.value, graph)
+        self._executables.add(exe)
+        return exe
+
     # -- buffers ----------------------------------------------------------
     def alloc(self, dtype: DType, dims) -> Buffer:
         dims = [int(d) for d in dims]

@@ -108,6 +108,63 @@ def test_hot_path_graphs_compile_without_decline(plugin, graph_fn):
     assert plugin.compile(graph_fn(), probe=True) is not None
 
 
+def _exe_header_offset(payload: bytes) -> int:
+    """Offset of the serialised executable's header section in a framed payload."""
+    count = struct.unpack_from("<I", payload, 0)[0]
+    for i in range(count):
+        kind, off, _ = struct.unpack_from("<IQQ", payload, 4 + 20 * i)
+        if kind == 0x45583242:
+            return off
+    raise AssertionError("no executable header section")
+
+
+@pytest.mark.parametrize("graph_fn", [
+    lambda: decoder_graph(LLAMA_7B, batch=2, seq=1, max_len=256, fmt="w4g32", layers=2)[0],
+    lambda: decoder_graph(LLAMA_70B, batch=32, seq=1, max_len=4160, fmt="w4g32", layers=1,
+                          tp_rank=1, tp_world=8, head="none")[0],
+], ids=["7b_decode", "70b_tp8"])
+def test_executable_serialises_and_loads_back(plugin, graph_fn):
+    """The ahead-of-time entries (raw.rs:760-788): serialize, abi_compatible and
+    deserialize_load round-trip an executable with no device work, and the loaded
+    executable serialises to the same bytes (same graph, same lowered plan)."""
+    g = graph_fn()
+    exe = plugin.compile(g)
+    blob = plugin.serialize(exe)
+    assert plugin.abi_compatible(blob)
+    exe2 = plugin.deserialize(blob, g)
+    assert exe2.handle and exe2.handle != exe.handle
+    assert plugin.serialize(exe2) == blob
+    exe.free()
+    exe2.free()
+
+
+def test_foreign_or_tampered_executable_blobs_are_refused(plugin):
+    g = decoder_graph(LLAMA_7B, batch=1, seq=1, max_len=128, fmt="w4g32", layers=1)[0]
+    exe = plugin.compile(g)
+    blob = plugin.serialize(exe)
+    exe.free()
+    # a subgraph blob is not an executable
+    subgraph = frame([(SECTION_GRAPH, encode_graph(g))])[abi.WIRE_HEADER_LEN:]
+    assert not plugin.abi_compatible(subgraph)
+    with pytest.raises(StrataError) as e:
+        plugin.deserialize(subgraph, g)
+    assert e.value.code == abi.INVALID_ARGUMENT
+    off = _exe_header_offset(blob)
+    # another architecture
+    other = bytearray(blob)
+    struct.pack_into("<I", other, off + 4, 90)
+    assert not plugin.abi_compatible(bytes(other))
+    # a plan this build does not produce (fingerprint changed): loadable header, refused load
+    stale = bytearray(blob)
+    struct.pack_into("<Q", stale, off + 16, struct.unpack_from("<Q", blob, off + 16)[0] ^ 1)
+    assert plugin.abi_compatible(bytes(stale))
+    with pytest.raises(StrataError) as e:
+        plugin.deserialize(bytes(stale), g)
+    assert e.value.code == abi.INVALID_ARGUMENT
+    # truncated
+    assert not plugin.abi_compatible(blob[: off + 8])
+
+
 def _one_node(op, in_dt=F32, out_dt=F32, dims=(1, 4)):
     b = GraphBuilder("g")
     x = b.input(in_dt, dims, "x")
