@@ -41,7 +41,7 @@ namespace sb {
 
 namespace {
 
-constexpr int kWarps = 8;      // K-slices per block
+constexpr int kWarps = 8;      // K-slices per block (12 for one-wave launches, below)
 constexpr int kTileRows = 16;  // output rows per block
 constexpr int kChunk = 8;      // groups per pipeline stage
 constexpr int kMaxRows = 64;  // x rows per launch
@@ -179,9 +179,9 @@ __device__ __forceinline__ void tile_epilogue(const Params& p, const TileRows& t
 
 // Sum the 8 K-slice partials of one tile through shared memory and run the
 // epilogue.  Every thread of the block calls this once per tile.
-template <int FMT, int NT, int MODE, bool kTrailingSync>
+template <int FMT, int NT, int MODE, bool kTrailingSync, int W>
 __device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
-                                            float (&red)[kWarps][kTileRows][8 * NT],
+                                            float (&red)[W][kTileRows][8 * NT],
                                             const float (&acc)[NT][4], int warp, int g, int q, int tid) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
@@ -190,11 +190,11 @@ __device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
   }
   __syncthreads();
   const int items = 8 * p.m;
-  for (int it = tid; it < items; it += kWarps * 32) {
+  for (int it = tid; it < items; it += W * 32) {
     const int pp = it / p.m, m = it - pp * p.m;
     float vlo = 0.0f, vhi = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < W; ++w) {
       vlo += red[w][pp][m];
       vhi += red[w][pp + 8][m];
     }
@@ -254,11 +254,14 @@ __device__ __forceinline__ void int4_group(float (&acc)[NT][4], uint32_t ul, uin
   }
 }
 
-template <int FMT, int NT, int MODE>
-__global__ void __launch_bounds__(kWarps * 32, NT <= 2 ? 3 : 2) gemv_mma_kernel(const __grid_constant__ Params p) {
+// W warps per block: 8, or 12 for launches whose tiles fit one wave of
+// 12-warp blocks (two per SM), where every tile's K is split 12 ways.
+template <int FMT, int NT, int MODE, int W>
+__global__ void __launch_bounds__(W * 32, W == 12 ? 2 : NT <= 2 ? 3 : 2)
+    gemv_mma_kernel(const __grid_constant__ Params p) {
   using S = Stage<FMT>;
   constexpr int kRedBufs = NT <= 2 ? 2 : 1;  // partial-sum buffers (alternate tiles)
-  __shared__ __align__(16) float red[kRedBufs][kWarps][kTileRows][8 * NT];
+  __shared__ __align__(16) float red[kRedBufs][W][kTileRows][8 * NT];
   extern __shared__ __align__(128) uint8_t dsm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, q = lane & 3;
@@ -417,36 +420,36 @@ __global__ void __launch_bounds__(kWarps * 32, NT <= 2 ? 3 : 2) gemv_mma_kernel(
       issue();  // refills the stage just read
       slot = slot + 1 == S::kDepth ? 0 : slot + 1;
     }
-    finish_tile<FMT, NT, MODE, kRedBufs == 1>(p, tile_rows<MODE>(p, y), red[buf], acc, warp, g, q, tid);
+    finish_tile<FMT, NT, MODE, kRedBufs == 1, W>(p, tile_rows<MODE>(p, y), red[buf], acc, warp, g, q, tid);
     buf = kRedBufs == 1 ? 0 : buf ^ 1;
   }
   cp_async_wait<0>();
 }
 
-// Launch one x-row block: p holds everything but the K-slices and the grid.
-// scale16_ok: every job's int4 scale rows are 16-byte aligned.
-template <int FMT, int NT, int MODE>
-int launch_one(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
-  auto kern = gemv_mma_kernel<FMT, NT, MODE>;
-  const size_t smem = kWarps * warp_smem_bytes(FMT);
+// Launch one x-row block with W warps per block: p holds everything but the
+// K-slices and the grid.  scale16_ok: every job's int4 scale rows are 16-byte
+// aligned.
+template <int FMT, int NT, int MODE, int W>
+int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
+  auto kern = gemv_mma_kernel<FMT, NT, MODE, W>;
+  const size_t smem = W * warp_smem_bytes(FMT);
   static int per_sm = 0;
   if (per_sm == 0) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
       return SB_INTERNAL;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWarps * 32, smem) != cudaSuccess ||
-        per_sm < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, W * 32, smem) != cudaSuccess || per_sm < 1)
       per_sm = 1;
   }
-  p.gpw = (p.groups + kWarps - 1) / kWarps;
+  p.gpw = (p.groups + W - 1) / W;
   p.gpw += p.gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
-  // Whole 8-group slices (K a multiple of 2048): each row's scales of a chunk
-  // are one aligned 16-byte copy.
-  p.scale16 = FMT == 0 && scale16_ok && p.groups % (8 * kWarps) == 0 ? 1 : 0;
+  // Whole 8-group slices: each row's scales of a chunk are one aligned
+  // 16-byte copy.
+  p.scale16 = FMT == 0 && scale16_ok && p.groups % (8 * W) == 0 ? 1 : 0;
   // Persistent: at most one full wave of blocks, each walking tiles.
   const int slots = per_sm * kNumSMs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(p.tiles < slots ? p.tiles : slots), 1, 1);
-  cfg.blockDim = dim3(kWarps * 32, 1, 1);
+  cfg.blockDim = dim3(W * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr;
@@ -457,6 +460,22 @@ int launch_one(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
   if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return SB_INTERNAL;
   count_launch();
   return SB_OK;
+}
+
+// A launch with few tiles (o_proj and down_proj of a 7B layer: 256) leaves
+// each warp a long K-slice and the SMs unevenly loaded; when the tiles fit one
+// wave of 12-warp blocks (two per SM) every tile's K is split 12 ways instead
+// of 8.  STRATA_B200_GEMV_WARPS=8 keeps 8 (A/B runs).
+template <int FMT, int NT, int MODE>
+int launch_one(const Params& p, bool scale16_ok, bool pdl, cudaStream_t st) {
+  static const bool wide_ok = [] {
+    const char* v = std::getenv("STRATA_B200_GEMV_WARPS");
+    return !(v && std::string(v) == "8");
+  }();
+  if constexpr (FMT == 0 && NT == 1)
+    if (wide_ok && p.tiles <= 2 * kNumSMs && p.groups >= 4 * 12)
+      return launch_w<FMT, NT, MODE, 12>(p, scale16_ok, pdl, st);
+  return launch_w<FMT, NT, MODE, kWarps>(p, scale16_ok, pdl, st);
 }
 
 template <int FMT, int NT>
