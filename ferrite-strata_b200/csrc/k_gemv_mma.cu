@@ -254,10 +254,11 @@ __device__ __forceinline__ void int4_group(float (&acc)[NT][4], uint32_t ul, uin
   }
 }
 
-// W warps per block: 8, or 12 for launches whose tiles fit one wave of
-// 12-warp blocks (two per SM), where every tile's K is split 12 ways.
+// W warps per block: 8, or 12 / 16 for launches whose tiles fit one wave of
+// 12-warp blocks (two per SM) / 16-warp blocks (one per SM), where every
+// tile's K is split W ways.
 template <int FMT, int NT, int MODE, int W>
-__global__ void __launch_bounds__(W * 32, W == 12 ? 2 : NT <= 2 ? 3 : 2)
+__global__ void __launch_bounds__(W * 32, W == 16 ? 1 : W == 12 ? 2 : NT <= 2 ? 3 : 2)
     gemv_mma_kernel(const __grid_constant__ Params p) {
   using S = Stage<FMT>;
   constexpr int kRedBufs = NT <= 2 ? 2 : 1;  // partial-sum buffers (alternate tiles)
@@ -462,19 +463,24 @@ int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
   return SB_OK;
 }
 
-// A launch with few tiles (o_proj and down_proj of a 7B layer: 256) leaves
-// each warp a long K-slice and the SMs unevenly loaded; when the tiles fit one
-// wave of 12-warp blocks (two per SM) every tile's K is split 12 ways instead
-// of 8.  STRATA_B200_GEMV_WARPS=8 keeps 8 (A/B runs).
+// A launch with few tiles (o_proj and down_proj of a 7B layer: 256; most
+// tensor-parallel shards) leaves each warp a long K-slice and the SMs unevenly
+// loaded.  When the tiles fit one wave of 16-warp blocks (one per SM) or of
+// 12-warp blocks (two per SM), and every warp still gets at least two groups,
+// each tile's K is split 16 or 12 ways instead of 8.
+// STRATA_B200_GEMV_WARPS=8 keeps 8 (A/B runs).
 template <int FMT, int NT, int MODE>
 int launch_one(const Params& p, bool scale16_ok, bool pdl, cudaStream_t st) {
   static const bool wide_ok = [] {
     const char* v = std::getenv("STRATA_B200_GEMV_WARPS");
     return !(v && std::string(v) == "8");
   }();
-  if constexpr (FMT == 0 && NT == 1)
-    if (wide_ok && p.tiles <= 2 * kNumSMs && p.groups >= 4 * 12)
+  if constexpr (FMT == 0 && NT == 1) {
+    if (wide_ok && p.tiles <= kNumSMs && p.groups >= 2 * 16)
+      return launch_w<FMT, NT, MODE, 16>(p, scale16_ok, pdl, st);
+    if (wide_ok && p.tiles <= 2 * kNumSMs && p.groups >= 2 * 12)
       return launch_w<FMT, NT, MODE, 12>(p, scale16_ok, pdl, st);
+  }
   return launch_w<FMT, NT, MODE, kWarps>(p, scale16_ok, pdl, st);
 }
 
