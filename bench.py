@@ -445,6 +445,84 @@ def run_prefill(args):
     return 0
 
 
+SWEEP_METRIC = "quantized Linear sweep, K = N = 4096 (us per launch, % of roofline)"
+
+
+def run_sweep(args):
+    """Config 2: one quantized Linear node per case, int4 g32 and int8 per-channel weights,
+    K = N = 4096, M in {1, 16, 128, 2048}, through the C-ABI entry points
+    (strata_b200_linear_w4g32 / _w8pc: the tensor-core GEMV up to 64 rows, the tcgen05 GEMM
+    above).  Weight copies rotate so every launch streams its weights from HBM."""
+    import torch
+    torch.cuda.set_device(0)
+    lib = C.CDLL(os.path.join(PKG, "libstrata_b200.so"))
+    P, I64 = C.c_void_p, C.c_int64
+    for f in (lib.strata_b200_linear_w4g32, lib.strata_b200_linear_w8pc):
+        f.argtypes = [P, I64, I64, P, P, I64, P, P, P]
+        f.restype = C.c_int32
+    bw, bw_kind = load_peaks()
+    try:
+        with open(PEAKS_PATH) as fh:
+            tf_peak, tf_kind = float(json.load(fh)["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        tf_peak, tf_kind = 1590.0, "fallback (burst)"
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    K = N = 4096
+    stream = torch.cuda.current_stream()
+    cases = []
+    for fmt in ("w4g32", "w8pc"):
+        wbytes = N * K // 2 + N * (K // 32) * 2 if fmt == "w4g32" else N * K + N * 4
+        copies = max(2, (2 * l2) // wbytes + 1)
+        if fmt == "w4g32":
+            ws = [torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda") for _ in range(copies)]
+            ss = [(torch.rand((N, K // 32), device="cuda") * 0.01).to(torch.bfloat16) for _ in range(copies)]
+            fn = lib.strata_b200_linear_w4g32
+        else:
+            ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda") for _ in range(copies)]
+            ss = [torch.rand((N,), device="cuda") * 0.01 for _ in range(copies)]
+            fn = lib.strata_b200_linear_w8pc
+        for m in (1, 16, 128, 2048):
+            x = torch.randn((m, K), device="cuda").to(torch.bfloat16)
+            y = torch.empty((m, N), dtype=torch.bfloat16, device="cuda")
+
+            def launch(i):
+                rc = fn(x.data_ptr(), m, K, ws[i % copies].data_ptr(), ss[i % copies].data_ptr(), N, None,
+                        y.data_ptr(), stream.cuda_stream)
+                assert rc == 0, rc
+
+            for i in range(max(args.warmup, 3) * copies):
+                launch(i)
+            torch.cuda.synchronize()
+            reps = max(args.steps, 1) * copies
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for i in range(reps):
+                launch(i)
+            e1.record(stream)
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) / 1e3 / reps
+            nbytes = wbytes + m * K * 2 + m * N * 2
+            flops = 2 * m * N * K
+            t_roof = max(nbytes / (bw * 1e9), flops / (tf_peak * 1e12))
+            bound = "hbm" if nbytes / (bw * 1e9) >= flops / (tf_peak * 1e12) else "tensor"
+            cases.append({"fmt": fmt, "m": m, "us": t * 1e6, "bytes": nbytes, "flops": flops,
+                          "gbs": nbytes / t / 1e9, "tflops": flops / t / 1e12, "bound": bound,
+                          "frac": t_roof / t})
+        del ws, ss
+        torch.cuda.empty_cache()
+    line = {"metric": SWEEP_METRIC, "value": cases[0]["frac"], "unit": "fraction of roofline (int4, M=1)",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 g32 / int8 per-channel weights, bf16 activations, f32 accumulate",
+            "data": "synthetic: random codes and scales on the device, N(0,1) bf16 x",
+            "config": {"workload": "one quantized Linear node, K = N = 4096, M in {1, 16, 128, 2048}",
+                       "l2": f"{copies}+ weight copies rotated (more than twice the {l2 >> 20} MB L2)"},
+            "roofline": {"hbm_gbs": bw, "hbm_kind": bw_kind, "bf16_tflops": tf_peak, "tensor_kind": tf_kind},
+            "cases": cases}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -459,6 +537,8 @@ def main():
     ap.add_argument("--prefill", action="store_true",
                     help="time the int8 prefill configuration instead of decode")
     ap.add_argument("--seq", type=int, default=2048, help="tokens per prompt with --prefill")
+    ap.add_argument("--sweep", action="store_true",
+                    help="time the quantized Linear sweep (K = N = 4096, M in {1, 16, 128, 2048}, int4 and int8)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     shape, batch0, kv_fill, metric = MODELS[args.model]
@@ -472,6 +552,8 @@ def main():
         return run_reference(args)
     if args.prefill:
         return run_prefill(args)
+    if args.sweep:
+        return run_sweep(args)
 
     import torch
     import torch.distributed as dist
