@@ -3,9 +3,9 @@
 //
 // Work decomposition.  The output is cut into 16-row mma.m16n8k16 tiles.  The
 // grid is persistent (at most one wave of resident blocks); block b computes
-// tiles b, b + grid, b + 2 grid, ...  Within a tile the 8 warps split K into 8
-// slices of whole 32-code groups and the 8 partial fragments are summed
-// through shared memory by finish_tile.  (Splitting a tile's K over the CTAs
+// tiles b, b + grid, b + 2 grid, ...  Within a tile the W warps (8, 12 or 16:
+// choose_warps) split K into W slices of whole 32-code groups and the W
+// partial fragments are summed through shared memory by finish_tile.  (Splitting a tile's K over the CTAs
 // of a cluster, with the partial sums merged through distributed shared
 // memory, measured slower on most 7B shapes and at best 9 % faster on one:
 // the per-tile cluster barrier costs about what the shorter slices save.)
@@ -41,7 +41,7 @@ namespace sb {
 
 namespace {
 
-constexpr int kWarps = 8;      // K-slices per block (12 for one-wave launches, below)
+constexpr int kWarps = 8;      // K-slices per block (12 or 16 where choose_warps picks them)
 constexpr int kTileRows = 16;  // output rows per block
 constexpr int kChunk = 8;      // groups per pipeline stage
 constexpr int kMaxRows = 64;  // x rows per launch
@@ -463,23 +463,45 @@ int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
   return SB_OK;
 }
 
-// A launch with few tiles (o_proj and down_proj of a 7B layer: 256; most
-// tensor-parallel shards) leaves each warp a long K-slice and the SMs unevenly
-// loaded.  When the tiles fit one wave of 16-warp blocks (one per SM) or of
-// 12-warp blocks (two per SM), and every warp still gets at least two groups,
-// each tile's K is split 16 or 12 ways instead of 8.
-// STRATA_B200_GEMV_WARPS=8 keeps 8 (A/B runs).
-template <int FMT, int NT, int MODE>
-int launch_one(const Params& p, bool scale16_ok, bool pdl, cudaStream_t st) {
+// Warps per block for an int4 launch of one n-tile.  Each warp walks its
+// K-slice of one tile after another, so a launch takes about
+// (tiles per block, rounded up) x (groups per slice) group steps: 8-warp
+// blocks fit three per SM, 12-warp blocks two and 16-warp blocks one.  Few
+// tiles with long K (o_proj and down_proj of a 7B layer: 256 tiles; most
+// tensor-parallel shards) favour the wider blocks, and so does a tile count
+// that divides unevenly over three blocks per SM (7B gate/up: 1376 tiles).
+// Every warp keeps at least two groups.  Ties keep the narrower block.
+int choose_warps(int tiles, int groups) {
   static const bool wide_ok = [] {
-    const char* v = std::getenv("STRATA_B200_GEMV_WARPS");
+    const char* v = std::getenv("STRATA_B200_GEMV_WARPS");  // "8": always 8 (A/B runs)
     return !(v && std::string(v) == "8");
   }();
+  if (!wide_ok) return kWarps;
+  int best = kWarps;
+  long best_cost = -1;
+  for (int w : {8, 12, 16}) {
+    if (w > kWarps && groups < 2 * w) continue;
+    const int blocks_per_sm = w == 8 ? 3 : w == 12 ? 2 : 1;
+    const long slots = long(blocks_per_sm) * kNumSMs;
+    int gpw = (groups + w - 1) / w;
+    gpw += gpw & 1;
+    const long cost = (tiles + slots - 1) / slots * gpw;
+    if (best_cost < 0 || cost < best_cost) {
+      best = w;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+template <int FMT, int NT, int MODE>
+int launch_one(const Params& p, bool scale16_ok, bool pdl, cudaStream_t st) {
   if constexpr (FMT == 0 && NT == 1) {
-    if (wide_ok && p.tiles <= kNumSMs && p.groups >= 2 * 16)
-      return launch_w<FMT, NT, MODE, 16>(p, scale16_ok, pdl, st);
-    if (wide_ok && p.tiles <= 2 * kNumSMs && p.groups >= 2 * 12)
-      return launch_w<FMT, NT, MODE, 12>(p, scale16_ok, pdl, st);
+    switch (choose_warps(p.tiles, p.groups)) {
+      case 16: return launch_w<FMT, NT, MODE, 16>(p, scale16_ok, pdl, st);
+      case 12: return launch_w<FMT, NT, MODE, 12>(p, scale16_ok, pdl, st);
+      default: break;
+    }
   }
   return launch_w<FMT, NT, MODE, kWarps>(p, scale16_ok, pdl, st);
 }
