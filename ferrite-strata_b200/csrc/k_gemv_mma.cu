@@ -465,12 +465,13 @@ int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
 
 // Warps per block for an int4 launch of one n-tile.  Each warp walks its
 // K-slice of one tile after another, so a launch takes about
-// (tiles per block, rounded up) x (groups per slice) group steps: 8-warp
-// blocks fit three per SM, 12-warp blocks two and 16-warp blocks one.  Few
-// tiles with long K (o_proj and down_proj of a 7B layer: 256 tiles; most
-// tensor-parallel shards) favour the wider blocks, and so does a tile count
-// that divides unevenly over three blocks per SM (7B gate/up: 1376 tiles).
-// Every warp keeps at least two groups.  Ties keep the narrower block.
+// (tiles per block, rounded up) x (groups per slice + about four groups'
+// worth of per-tile reduction and barrier) group steps: 8-warp blocks fit
+// three per SM, 12-warp blocks two and 16-warp blocks one.  Few tiles with
+// long K (o_proj and down_proj of a 7B layer: 256 tiles; most tensor-parallel
+// shards) favour the wider blocks; the 7B gate/up (1376 tiles) measured
+// slower with 12 warps (28.8 against 23.9 us cold) and keeps 8.  Every warp
+// keeps at least two groups.  Ties keep the narrower block.
 int choose_warps(int tiles, int groups) {
   static const bool wide_ok = [] {
     const char* v = std::getenv("STRATA_B200_GEMV_WARPS");  // "8": always 8 (A/B runs)
@@ -485,7 +486,7 @@ int choose_warps(int tiles, int groups) {
     const long slots = long(blocks_per_sm) * kNumSMs;
     int gpw = (groups + w - 1) / w;
     gpw += gpw & 1;
-    const long cost = (tiles + slots - 1) / slots * gpw;
+    const long cost = (tiles + slots - 1) / slots * (gpw + 4);
     if (best_cost < 0 || cost < best_cost) {
       best = w;
       best_cost = cost;
