@@ -302,3 +302,29 @@ def test_bare_integer_dtype_is_rejected_by_the_host_builder():
     with pytest.raises(ValueError):
         DType.plain("i32")
     assert W4G32.quant_kind == 1 and w8pc(4096).block_size == 4096
+
+
+def _plan_steps(plugin, g) -> int:
+    """Steps of the lowered plan, read from the serialised executable's header
+    (u32 format, u32 arch, u32 abi major, u32 abi minor, u64 fingerprint, u32 steps)."""
+    exe = plugin.compile(g)
+    assert exe is not None
+    blob = plugin.serialize(exe)
+    exe.free()
+    return struct.unpack_from("<I", blob, _exe_header_offset(blob) + 24)[0]
+
+
+def test_tensor_parallel_layer_lowers_to_fused_steps(plugin):
+    """A tensor-parallel decode layer lowers to 10 steps: embed, RMSNorm, q/k/v GEMV with RoPE
+    and cache append, attention, o_proj, all-reduce + residual add + RMSNorm, gate/up GEMV with
+    SwiGLU, down_proj, all-reduce + residual add + final RMSNorm, lm_head.  Without the fused
+    all-reduce step it would be 14."""
+    shape = LLAMA_7B
+    for rank in (0, 7):  # 7B FFN shards at 8 ranks: 1408 and 1344 features
+        g = decoder_graph(shape, batch=4, seq=1, max_len=256, fmt="w4g32", layers=1, head="logits",
+                          tp_rank=rank, tp_world=8)[0]
+        assert _plan_steps(plugin, g) == 10
+    # the same layer unsharded (10 as well): the residual adds ride on the o_proj and down_proj
+    # GEMV epilogues, and the two RMSNorms after them are steps of their own
+    g1 = decoder_graph(shape, batch=4, seq=1, max_len=256, fmt="w4g32", layers=1, head="logits")[0]
+    assert _plan_steps(plugin, g1) == 10
