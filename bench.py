@@ -661,6 +661,11 @@ def main():
         tps, sample = cpu_baseline_sample(args.batch, ora.max_threads(), fraction=1 if args.model == "7b" else 8,
                                           shape=shape, kv_fill=kv_fill)
         cpu = {"value": tps, "unit": "tokens/s", "cores": ora.max_threads(), "kind": "port", "sample": sample}
+        # The reference's own CPU backend is single-threaded: the same sample on one core
+        # (1/16 of the rows and heads, scaled), for the like-for-like figure.
+        tps1, sample1 = cpu_baseline_sample(args.batch, 1, fraction=16 if args.model == "7b" else 8,
+                                            shape=shape, kv_fill=kv_fill)
+        cpu["single_thread"] = {"value": tps1, "unit": "tokens/s", "cores": 1, "sample": sample1}
 
     if rank == 0:
         F = ffn_shard(shape.ffn, world, 0)[1]
