@@ -328,3 +328,16 @@ def test_tensor_parallel_layer_lowers_to_fused_steps(plugin):
     # GEMV epilogues, and the two RMSNorms after them are steps of their own
     g1 = decoder_graph(shape, batch=4, seq=1, max_len=256, fmt="w4g32", layers=1, head="logits")[0]
     assert _plan_steps(plugin, g1) == 10
+
+
+def test_decode_and_prefill_layers_lower_to_their_fused_plans(plugin):
+    """Per-layer plan sizes (one more layer adds exactly these steps): a 7B decode layer is 7
+    steps (RMSNorm, q/k/v GEMV with RoPE and cache append, attention, o_proj with residual,
+    RMSNorm, gate/up GEMV with SwiGLU, down_proj with residual); an int8 prefill layer is 10
+    (q/k/v as one grouped GEMM step, separate RoPE and cache-append steps)."""
+    def per_layer(**kw):
+        one = _plan_steps(plugin, decoder_graph(LLAMA_7B, layers=1, **kw)[0])
+        two = _plan_steps(plugin, decoder_graph(LLAMA_7B, layers=2, **kw)[0])
+        return two - one, one
+    assert per_layer(batch=2, seq=1, max_len=256, fmt="w4g32", head="argmax") == (7, 11)
+    assert per_layer(batch=2, seq=96, max_len=96, fmt="w8pc", head="logits", last_token=True) == (10, 14)
