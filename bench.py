@@ -47,9 +47,31 @@ MODELS = {
     "70b": (LLAMA_70B, 32, 4096, "decode tokens/s, 70B-shape int4 g32 stack (no embedding / lm_head)"),
 }
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
-# DRAM bytes read + written by one gate/up GEMV launch (M = 1), from the ncu
-# capture summarised in profiles/gemv_w4g32_swiglu_m1.md.
-GATEUP_TRAFFIC_BYTES = 50_759_168 + 21_248
+# The decode GEMV's sources: a DRAM-traffic figure below is used only while
+# these files are unchanged since it was measured.
+GEMV_SOURCES = ("ferrite-strata_b200/csrc/k_gemv_mma.cu", "ferrite-strata_b200/csrc/k_int4.cuh")
+# DRAM bytes read + written by one launch of the gate/up GEMV with the SwiGLU
+# epilogue (ncu: dram__bytes_read.sum + dram__bytes_write.sum of one launch
+# among weight sets larger than L2), keyed by (source digest, M, N, K).
+GEMV_TRAFFIC = {}
+
+
+def gemv_source_digest():
+    import hashlib
+    h = hashlib.sha256()
+    for rel in GEMV_SOURCES:
+        with open(os.path.join(ROOT, rel), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()[:16]
+
+
+def measured_traffic(m, n, k):
+    """The measured DRAM traffic of the current GEMV source at this shape, or
+    None when it has not been measured."""
+    try:
+        return GEMV_TRAFFIC.get((gemv_source_digest(), m, n, k))
+    except OSError:
+        return None
 
 
 def step_bytes(shape, batch, kv_fill=KV_FILL):
@@ -78,7 +100,7 @@ def load_peaks():
 # ---------------------------------------------------------------------------
 class ClockSampler:
     """Samples SM clock, its maximum and the clock-event reasons through NVML
-    every 20 ms in a background thread while the timed region runs (reading
+    every 5 ms in a background thread while the timed region runs (reading
     only; no setting is changed)."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
@@ -109,7 +131,7 @@ class ClockSampler:
                     self.samples.append((mhz, reasons))
                 except Exception:
                     pass
-                self._stop.wait(0.02)
+                self._stop.wait(0.005)
 
         self._thread = threading.Thread(target=run, daemon=True)
         self._thread.start()
@@ -278,73 +300,130 @@ def dominant_kernel(plugin, torch, shape=LLAMA_7B, m=1, tp=1, reps=32):
 _CPU_INPUTS: dict = {}
 
 
-def cpu_baseline_sample(batch, threads, fraction=1, shape=LLAMA_7B, kv_fill=KV_FILL):
-    """One decode layer on the CPU oracle (all host threads), scaled to the
-    whole step (and the lm_head, where the shape has one); returns tokens/s
-    and what was timed.
-
-    ``fraction`` > 1 times 1/fraction of every weight matrix's rows and of
-    the query and kv heads (each row / head costs the same) and scales the
-    time back up, to bound one sample's CPU time."""
+def _cpu_inputs(shape, batch, kv_fill):
+    """Host inputs for the CPU oracle's decode step, generated once: one
+    layer's int4 weights (every layer runs on them: the oracle's time does
+    not depend on the values, and 32 distinct layers would need 26 GB of f32
+    to generate), norm gains, one KV cache pair prefilled over kv_fill
+    positions, the embedding table and the int4 lm_head."""
     import numpy as np
 
     from oracle import oracle as ora
-    f = fraction
+    key = (shape, batch, kv_fill)
+    if key in _CPU_INPUTS:
+        return _CPU_INPUTS[key]
     D, H, G, d, F, V = shape.hidden, shape.heads, shape.kv_heads, shape.head_dim, shape.ffn, shape.vocab
-    Hf, Gf = H // f, G // f
     mats = {"q": (H * d, D), "k": (G * d, D), "v": (G * d, D), "o": (D, H * d), "g": (F, D), "u": (F, D),
             "d": (D, F)}
-    key = (D, batch, f, kv_fill)
-    if key not in _CPU_INPUTS:  # generated once; only the kernels below are timed
-        W = {k: ora.quant_w4g32(ora.normal(10 + i, (n // f, kk), std=0.02)) for i, (k, (n, kk)) in
-             enumerate(mats.items())}
-        kc = ora.round_bf16(ora.normal(20, (batch, Gf, kv_fill + 1, d)))
-        vc = ora.round_bf16(ora.normal(21, (batch, Gf, kv_fill + 1, d)))
-        xs = {k: ora.round_bf16(ora.normal(0, (batch, kk))) for k, (n, kk) in mats.items()}
-        q = ora.round_bf16(ora.normal(3, (batch, Hf * d)))
-        lm = ora.quant_w4g32(ora.normal(99, (V // f, D), std=0.02)) if V else None
-        _CPU_INPUTS[key] = (W, kc, vc, xs, q, lm)
-    W, kc, vc, xs, q, lm = _CPU_INPUTS[key]
+    W = {k: ora.quant_w4g32(ora.normal(10 + i, (n, kk), std=0.02)) for i, (k, (n, kk)) in enumerate(mats.items())}
+    kc = ora.round_bf16(ora.normal(20, (batch, G, kv_fill + 1, d)))
+    vc = ora.round_bf16(ora.normal(21, (batch, G, kv_fill + 1, d)))
+    norms = [ora.round_bf16(1.0 + ora.normal(30 + i, (D,), std=0.02)) for i in range(3)]
+    table = ora.round_bf16(ora.normal(40, (V, D))) if V else None
+    lm = ora.quant_w4g32(ora.normal(99, (V, D), std=0.02)) if V else None
+    ids = ora.uniform_i32(2, batch, 0, V) if V else None
+    h0 = ora.round_bf16(ora.normal(0, (batch, D)))
+    _CPU_INPUTS[key] = (W, kc, vc, norms, table, lm, ids, h0)
+    return _CPU_INPUTS[key]
+
+
+def cpu_decode_layers(shape, batch, kv_fill, threads, layers, head=True):
+    """One decode step on the CPU oracle: `layers` decoder layers (RMSNorm,
+    q/k/v int4 linears, RoPE, KV append, attention over kv_fill + 1
+    positions, o_proj + residual, RMSNorm, gate/up, SwiGLU, down_proj +
+    residual) and, with `head`, the final norm, the int4 lm_head and argmax.
+    Every value is rounded to bf16 where the graph produces it, as the
+    graph-level oracle does.  Returns the seconds it took."""
+    import numpy as np
+
+    from oracle import oracle as ora
+    W, kc, vc, norms, table, lm, ids, h0 = _cpu_inputs(shape, batch, kv_fill)
+    H, G, d = shape.heads, shape.kv_heads, shape.head_dim
+    r = ora.round_bf16
     pos = np.full(batch, kv_fill, np.int32)
+    seq = np.arange(batch, dtype=np.int32)
+
+    def lin(x, k):
+        return r(ora.linear_w4g32(x, W[k][0], W[k][1], threads=threads))
+
     t0 = time.perf_counter()
-    for k in mats:
-        ora.linear_w4g32(xs[k], W[k][0], W[k][1], threads=threads)
-    ora.attention(q, kc, vc, np.arange(batch), pos, Hf, Gf, d, threads=threads)
-    layer_s = (time.perf_counter() - t0) * f
-    head_s = 0.0
-    if lm is not None:
-        t1 = time.perf_counter()
-        ora.linear_w4g32(xs["q"], lm[0], lm[1], threads=threads)
-        head_s = (time.perf_counter() - t1) * f
-    step_s = layer_s * shape.layers + head_s
-    part = "" if f == 1 else f" (1/{f} of every matrix's rows and of the heads, time x{f})"
-    return batch / step_s, (f"one decode layer at batch {batch}: 7 int4 linears + attention over "
-                            f"{kv_fill + 1} positions{part}, scaled x{shape.layers}"
-                            f"{', plus the lm_head' if lm is not None else ''}; threaded C oracle, k-order f32")
+    h = r(ora.embed(ids, table)[0]) if table is not None else h0
+    for _ in range(layers):
+        n = r(ora.rms_norm(h, norms[0], shape.eps))
+        q = r(ora.rope(lin(n, "q"), pos, d, shape.theta))
+        k = r(ora.rope(lin(n, "k"), pos, d, shape.theta))
+        v = lin(n, "v")
+        kc[:, :, kv_fill] = k.reshape(batch, G, d)
+        vc[:, :, kv_fill] = v.reshape(batch, G, d)
+        a = r(ora.attention(q, kc, vc, seq, pos, H, G, d, threads=threads))
+        h = r(h + lin(a, "o"))
+        n = r(ora.rms_norm(h, norms[1], shape.eps))
+        gu = r(ora.swiglu(lin(n, "g"), lin(n, "u")))
+        h = r(h + lin(gu, "d"))
+    if head and lm is not None:
+        n = r(ora.rms_norm(h, norms[2], shape.eps))
+        ora.argmax(r(ora.linear_w4g32(n, lm[0], lm[1], threads=threads)))
+    return time.perf_counter() - t0
+
+
+def cpu_step_sample(shape, batch, kv_fill, threads, whole_step=True):
+    """The CPU baseline beside the B200 arm: one whole decode step on all host
+    threads (or, for a stack too large to run whole in a few minutes, one
+    layer scaled to the stack), and one layer on one thread scaled to the
+    stack (the reference's own CPU backend is single-threaded)."""
+    head = "the int4 lm_head and argmax" if shape.vocab else "no lm_head"
+    if whole_step:
+        step_s = cpu_decode_layers(shape, batch, kv_fill, threads, shape.layers)
+        what = f"one whole decode step at batch {batch} ({shape.layers} layers over {kv_fill + 1} positions, {head})"
+    else:
+        step_s = cpu_decode_layers(shape, batch, kv_fill, threads, 1, head=False) * shape.layers
+        what = (f"one decode layer at batch {batch} over {kv_fill + 1} positions, scaled x{shape.layers} "
+                f"(an extrapolation; {head})")
+    one = cpu_decode_layers(shape, batch, kv_fill, 1, 1, head=False)
+    return {"value": batch / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{what} on the threaded C oracle; every layer reuses one layer's weights",
+            "single_thread": {"value": batch / (one * shape.layers), "unit": "tokens/s", "cores": 1,
+                              "sample": f"one layer on one thread, scaled x{shape.layers} (lm_head excluded)"}}
+
+
+def decode_config(args, shape, kv_fill, world, sb):
+    """The `config` object both arms print for the decode workload."""
+    head = "int4 lm_head + argmax" if shape.vocab else "no embedding / lm_head"
+    return {"workload": f"{args.model.upper()}-shape int4 g32 decode stack ({args.layers} layers, "
+                        f"{head}), batch {args.batch}, KV cache {kv_fill} prefilled",
+            "model": args.model, "batch": args.batch, "kv_len": kv_fill, "layers": args.layers,
+            "parallelism": f"tp{world}",
+            "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB streamed per step"}
 
 
 def run_reference(args):
+    """The reference arm: the CPU oracle (the port of the reference's CPU
+    backend plus the decoder ops it lacks) running whole decode steps of the
+    same workload on all host threads.  Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import numpy as np  # noqa: F401
     from oracle import oracle as ora
     threads = ora.max_threads()
     shape, _, kv_fill, metric = MODELS[args.model]
-    values = []
-    sample = ""
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    steps = []
     for i in range(args.warmup + args.steps):
-        tps, sample = cpu_baseline_sample(args.batch, threads, fraction=16 if args.model == "7b" else 8,
-                                          shape=shape, kv_fill=kv_fill)
+        t = cpu_decode_layers(shape, args.batch, kv_fill, threads, args.layers)
         if i >= args.warmup:
-            values.append(tps)
-    v = statistics.median(values)
+            steps.append(t)
+    step_s = sum(steps) / len(steps)
+    v = args.batch / step_s
+    sb = step_bytes(shape, args.batch, kv_fill) * args.layers // shape.layers
+    sample = (f"whole decode steps at batch {args.batch} ({args.layers} layers over {kv_fill + 1} positions"
+              f"{', the int4 lm_head and argmax' if shape.vocab else ''}) on the threaded C oracle; every layer "
+              f"reuses one layer's weights")
     line = {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.batch / v * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights, f32 compute",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights (g32, bf16 scales), bf16-rounded values, f32 compute",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) KV)",
-            "config": {"workload": f"{args.model.upper()}-shape int4 g32 decode, batch {args.batch}, KV {kv_fill}",
-                       "batch": args.batch, "kv_len": kv_fill, "parallelism": "cpu"},
+            "config": decode_config(args, shape, kv_fill, world, sb),
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -526,7 +605,7 @@ def run_sweep(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--model", default="7b", choices=sorted(MODELS),
                     help="7b: 7B-shape stack (default batch 8, KV 2048); 70b: 70B-shape stack (batch 32, KV 4096)")
@@ -647,10 +726,13 @@ def main():
     e2e = tokens / e2e_s
 
     # ---- roofline of the dominant kernel and of the whole step ----------------
+    # The dominant kernel is timed at the step's own M (the batch) and, as a
+    # side figure, at M = 1.
     peak, peak_kind = load_peaks()
-    k_m = 1 if args.model == "7b" else args.batch
+    k_m = args.batch
     k_s, k_bytes = dominant_kernel(plugin, torch, shape=shape, m=k_m, tp=world)
     k_gbs = k_bytes / k_s / 1e9
+    k1_s, k1_bytes = dominant_kernel(plugin, torch, shape=shape, m=1, tp=world) if k_m != 1 else (k_s, k_bytes)
     sb = step_bytes(shape, args.batch, kv_fill) * args.layers // shape.layers
     step_gbs = sb / (ms_step / 1e3) / 1e9 / world
     clock = clocks.summary()
@@ -658,35 +740,26 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as ora
-        tps, sample = cpu_baseline_sample(args.batch, ora.max_threads(), fraction=1 if args.model == "7b" else 8,
-                                          shape=shape, kv_fill=kv_fill)
-        cpu = {"value": tps, "unit": "tokens/s", "cores": ora.max_threads(), "kind": "port", "sample": sample}
-        # The reference's own CPU backend is single-threaded: the same sample on one core
-        # (1/16 of the rows and heads, scaled), for the like-for-like figure.
-        tps1, sample1 = cpu_baseline_sample(args.batch, 1, fraction=16 if args.model == "7b" else 8,
-                                            shape=shape, kv_fill=kv_fill)
-        cpu["single_thread"] = {"value": tps1, "unit": "tokens/s", "cores": 1, "sample": sample1}
+        cpu = cpu_step_sample(shape, args.batch, kv_fill, ora.max_threads(), whole_step=args.model == "7b")
 
     if rank == 0:
         F = ffn_shard(shape.ffn, world, 0)[1]
-        head = "int4 lm_head + argmax" if model.embed else "no embedding / lm_head"
         line = {
             "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights (g32, bf16 scales), bf16 activations, f32 accumulate",
             "data": "synthetic: device-generated N(0,0.02) weights quantised by the plugin, N(0,1) bf16 KV",
-            "config": {"workload": f"{args.model.upper()}-shape int4 g32 decode stack ({args.layers} layers, "
-                                   f"{head}), batch {args.batch}, KV cache {kv_fill} prefilled",
-                       "model": args.model, "batch": args.batch, "kv_len": kv_fill, "layers": args.layers,
-                       "parallelism": f"tp{world}",
-                       "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB streamed per step"},
+            "config": decode_config(args, shape, kv_fill, world, sb),
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": n_in + nb, "d2h_bytes_per_step": n_out},
             "roofline": {"bound": "hbm",
                          "kernel": f"w4g32 gate/up GEMV + SwiGLU epilogue, M={k_m}, N=2x{F}, K={shape.hidden}",
                          "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
                          "peak_kind": peak_kind,
-                         "traffic": GATEUP_TRAFFIC_BYTES if (args.model, world) == ("7b", 1) else None,
-                         "bytes_per_launch": k_bytes, "us_per_launch": k_s * 1e6},
+                         "traffic": measured_traffic(k_m, 2 * F, shape.hidden),
+                         "bytes_per_launch": k_bytes, "us_per_launch": k_s * 1e6,
+                         "m1": {"achieved": k1_bytes / k1_s / 1e9, "frac": k1_bytes / k1_s / 1e9 / peak,
+                                "bytes_per_launch": k1_bytes, "us_per_launch": k1_s * 1e6,
+                                "traffic": measured_traffic(1, 2 * F, shape.hidden)}},
             "step_roofline": {"bytes_per_step": sb, "achieved_gbs_per_gpu": step_gbs, "frac": step_gbs / peak,
                               "frac_of_8tbs": step_gbs / 8000.0},
             "gpu_launches": launches,

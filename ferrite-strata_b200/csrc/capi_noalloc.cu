@@ -14,7 +14,12 @@
 // reserved until the process exits.  Host code cannot use the array's name as
 // a device address (on the host it names a stand-in object), so the address
 // is looked up with cudaGetSymbolAddress once per device, with that device
-// current, the first time this entry point runs on it.
+// current, the first time this entry point runs on it.  The lookup is kept
+// together with the CUDA context it was made in: after cudaDeviceReset the
+// device gets a new context, the module is loaded again (possibly at another
+// address), and the next call looks the address up again.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "../../include/strata_b200.h"
@@ -29,24 +34,51 @@ constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kMaxDevices] = {};
+struct ScratchAddr {
+  CUcontext ctx = nullptr;  // the context the address belongs to
+  void* ptr = nullptr;
+};
 
-// The device address of the scratch array on the current device, looked up
-// once per device.  Returns null if the lookup fails.
+std::mutex g_noalloc_mutex;
+ScratchAddr g_noalloc_addr[kMaxDevices];
+
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+
+CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return CtxGetCurrent(nullptr);
+    return reinterpret_cast<CtxGetCurrent>(p);
+  }();
+  return fn;
+}
+
+// The device address of the scratch array on the current device.  Returns
+// null if it cannot be determined.  Allocates nothing: the lookup only reads
+// the address of memory the module already holds.
 void* noalloc_scratch() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  CtxGetCurrent get = ctx_get_current();
+  if (!get) return nullptr;
+  CUcontext ctx = nullptr;  // null until the runtime has started on this thread's device
+  if (get(&ctx) != CUDA_SUCCESS) return nullptr;
   std::lock_guard<std::mutex> lk(g_noalloc_mutex);
-  if (!g_noalloc_ptr[dev]) {
+  ScratchAddr& a = g_noalloc_addr[dev];
+  if (!ctx || a.ctx != ctx || !a.ptr) {
     void* ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess) {
       cudaGetLastError();
       return nullptr;
     }
-    g_noalloc_ptr[dev] = ptr;
+    if (get(&ctx) != CUDA_SUCCESS || !ctx) return nullptr;  // the lookup made the context current
+    a.ctx = ctx;
+    a.ptr = ptr;
   }
-  return g_noalloc_ptr[dev];
+  return a.ptr;
 }
 
 }  // namespace
@@ -67,8 +99,12 @@ int32_t strata_b200_attention_decode_bf16_noalloc(const uint16_t* q, const uint1
                                                   void* stream) {
   if (batch < 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || max_len <= 0)
     return SB_INVALID_ARGUMENT;
-  // The partials this call needs; every slot the merge reads is written first
-  // by the same call, so nothing has to be cleared between calls.
+  // The partials this call needs: zero when the shape runs on the tensor-core
+  // kernel (its splits merge on chip), the split-KV partials of the CUDA-core
+  // kernel otherwise (more than 8 query heads per kv head).  Every slot the
+  // merge reads is written first by the same call, so nothing has to be
+  // cleared between calls.
+  if (batch > 65535) return SB_INVALID_ARGUMENT;
   const uint64_t need = attention_v2_scratch_bytes(batch, heads, kv_heads, head_dim, max_len);
   if (need > kNoAllocScratchBytes) return SB_RESOURCE_EXHAUSTED;
   void* scratch = noalloc_scratch();

@@ -19,6 +19,23 @@ constexpr int kNumSMs = 148;  // B200: 2 dies x 74 SMs
 
 inline int ceil_div(int64_t a, int64_t b) { return int((a + b - 1) / b); }
 
+// Runs a set-up step (such as raising a kernel's dynamic shared-memory limit,
+// which the runtime keeps per device) once on each device that needs it.
+// Devices past the 64th run it on every call.
+struct PerDeviceOnce {
+  std::atomic<uint64_t> done{0};
+  template <typename F>
+  bool run(F&& setup) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return setup();
+    const uint64_t bit = uint64_t(1) << dev;
+    if (done.load(std::memory_order_acquire) & bit) return true;
+    if (!setup()) return false;
+    done.fetch_or(bit, std::memory_order_acq_rel);
+    return true;
+  }
+};
+
 #if !defined(__CUDACC__)
 bool pdl_enabled();
 #endif

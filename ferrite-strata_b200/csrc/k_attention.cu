@@ -309,7 +309,9 @@ __global__ void attn_merge_kernel(const float* __restrict__ partial, int heads, 
 // position itself (just appended by that kernel) and q are read after the
 // wait.  The block computes the G query heads' scores for its chunk from the
 // staged k rows, a local softmax, and the unnormalised PV sum, and writes
-// (max, sum, acc) partials for attn_merge_kernel.
+// (max, sum, acc) partials for attn_merge_kernel.  A kv head shared by more
+// than kMaxGroup query heads (wide GQA, MQA) is covered by several blocks,
+// each taking kMaxGroup of its query heads: grid.y = kv head x head chunk.
 // ---------------------------------------------------------------------------
 template <int D, int CH>
 struct AttnV2Smem {
@@ -332,8 +334,12 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int kPairs = D / 2;
   constexpr int kPhases = kThreads / kPairs;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
-  const int G = heads / kv_heads;
+  const int split = blockIdx.x, row = blockIdx.z;
+  const int G_all = heads / kv_heads;                    // query heads per kv head
+  const int nchunk = (G_all + kMaxGroup - 1) / kMaxGroup;
+  const int kvh = blockIdx.y / nchunk;
+  const int h0 = kvh * G_all + (blockIdx.y - kvh * nchunk) * kMaxGroup;  // first query head of this block
+  const int G = min(kMaxGroup, kvh * G_all + G_all - h0);                // query heads of this block
   const int tid = threadIdx.x;
   uint8_t* sK = smem;
   uint8_t* sV = sK + CH * L::kRowK;
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(kThreads)
   if (n_t > pre) stage(pre, n_t);
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
-    sQ[i] = bf2f(q[int64_t(row) * heads * D + int64_t(kvh * G + g) * D + d]);
+    sQ[i] = bf2f(q[int64_t(row) * heads * D + int64_t(h0 + g) * D + d]);
   }
   cp_async_commit_wait_all();
   __syncthreads();
@@ -460,7 +466,7 @@ __global__ void __launch_bounds__(kThreads)
     float acc = 0.0f;
 #pragma unroll
     for (int ph = 0; ph < kPhases; ++ph) acc += sA[(ph * G + g) * D + d];
-    const int h = kvh * G + g;
+    const int h = h0 + g;
     const float mx = n_t > 0 ? sM[g] : -INFINITY, l = n_t > 0 ? sM[G + g] : 0.0f;
     if (splits == 1) {
       out[int64_t(row) * heads * D + int64_t(h) * D + d] = f2bf(l > 0.0f ? acc / l : 0.0f);
@@ -489,10 +495,11 @@ int attention_v2_splits(int64_t rows, int64_t kv_heads, int64_t max_len) {
 
 uint64_t attention_v2_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
                                     int64_t max_len) {
-  // Room for whichever kernel runs (the CUDA-core or the tensor-core one).
-  const int64_t span = attention_tc_span(rows, kv_heads, max_len);
-  const int64_t s_tc = (max_len + span - 1) / span;
-  const int64_t s = std::max<int64_t>(attention_v2_splits(rows, kv_heads, max_len), s_tc);
+  // Only the CUDA-core kernel writes split partials; the tensor-core decode
+  // kernel merges its splits on chip and the prefill kernel has none.  This
+  // mirrors launch_attention_v2's choice of kernel.
+  if (attention_tc_supported(heads, kv_heads, head_dim)) return 0;
+  const int64_t s = attention_v2_splits(rows, kv_heads, max_len);
   if (s == 1) return 0;
   return uint64_t(rows) * heads * s * (head_dim + 2) * sizeof(float);
 }
@@ -503,16 +510,16 @@ static int launch_v2(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, 
                      int splits, bool pos_external, float* scratch, uint16_t* out, int* err,
                      cudaStream_t st) {
   const int G = int(heads / kv_heads);
-  const size_t smem = AttnV2Smem<D, CH>::bytes(G);
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(attn_v2_kernel<D, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             int(AttnV2Smem<D, CH>::bytes(kMaxGroup))) != cudaSuccess)
-      return SB_INTERNAL;
-    configured = true;
-  }
+  const int nchunk = (G + kMaxGroup - 1) / kMaxGroup;
+  const size_t smem = AttnV2Smem<D, CH>::bytes(G < kMaxGroup ? G : kMaxGroup);
+  static PerDeviceOnce configured;
+  if (!configured.run([] {
+        return cudaFuncSetAttribute(attn_v2_kernel<D, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    int(AttnV2Smem<D, CH>::bytes(kMaxGroup))) == cudaSuccess;
+      }))
+    return SB_INTERNAL;
   const float scale = 1.0f / sqrtf(float(D));
-  const dim3 grid(splits, unsigned(kv_heads), unsigned(rows));
+  const dim3 grid(splits, unsigned(kv_heads * nchunk), unsigned(rows));
   if (launch_pdl(attn_v2_kernel<D, CH>, grid, dim3(kThreads), smem, st, q, kc, vc, pos, int(tps), int(heads),
                  int(kv_heads), int(max_len), splits, scale, pos_external ? 1 : 0, scratch, out, err) !=
       cudaSuccess)
@@ -545,27 +552,23 @@ int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t head
   return SB_OK;
 }
 
-// STRATA_B200_ATTN=v2 keeps bf16 decode attention on the CUDA-core kernel (for A/B measurements).
-static bool tensor_core_attention_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("STRATA_B200_ATTN");
-    return !(v && std::string(v) == "v2");
-  }();
-  return on;
-}
-
+// bf16 attention: the tensor-core prefill kernel for 16 or more tokens per
+// sequence, the tensor-core decode kernel (k_attn_tc.cu) for up to 8 query
+// heads per kv head, and the CUDA-core kernel above for wider groups (MQA,
+// 16:1 GQA), which is the only one of the three that uses `scratch`.
 int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                         const int32_t* pos, int64_t rows, int64_t tokens_per_seq, int64_t heads,
                         int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
                         float* scratch, uint16_t* out, int* err, cudaStream_t st) {
   if (rows == 0) return SB_OK;
-  if (tensor_core_attention_enabled() && attention_prefill_supported(rows, tokens_per_seq, heads, kv_heads, head_dim))
+  if (attention_prefill_supported(rows, tokens_per_seq, heads, kv_heads, head_dim))
     return launch_attention_prefill(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim,
                                     max_len, out, err, st);
-  if (tensor_core_attention_enabled() && attention_tc_supported(heads, kv_heads, head_dim))
+  if (attention_tc_supported(heads, kv_heads, head_dim))
     return launch_attention_tc(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim, max_len,
                                pos_external, scratch, out, err, st);
-  if (kv_heads <= 0 || heads % kv_heads || heads / kv_heads > kMaxGroup) return SB_INVALID_ARGUMENT;
+  if (kv_heads <= 0 || heads % kv_heads || rows > 65535) return SB_INVALID_ARGUMENT;
+  if (kv_heads * ((heads / kv_heads + kMaxGroup - 1) / kMaxGroup) > 65535) return SB_INVALID_ARGUMENT;
   const int splits = attention_v2_splits(rows, kv_heads, max_len);
   if (splits > 1 && scratch == nullptr) return SB_INVALID_ARGUMENT;
   const int ch = attention_chunk(rows, kv_heads);

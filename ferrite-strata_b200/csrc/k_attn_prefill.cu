@@ -254,13 +254,12 @@ int launch_pf(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
               int64_t tps, int64_t heads, int64_t kv_heads, int64_t max_len, uint16_t* out, int* err,
               cudaStream_t st) {
   using Lay = PfLayout<D>;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(attn_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) !=
-        cudaSuccess)
-      return SB_INTERNAL;
-    configured = true;
-  }
+  static PerDeviceOnce configured;
+  if (!configured.run([] {
+        return cudaFuncSetAttribute(attn_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) ==
+               cudaSuccess;
+      }))
+    return SB_INTERNAL;
   const dim3 grid{unsigned((tps + kPfRows - 1) / kPfRows), unsigned(heads), unsigned(batch)};
   if (launch_pdl(attn_prefill_kernel<D>, grid, dim3(kPfWarps * 32), size_t(Lay::kBytes), st, q, kc, vc, pos,
                  int(tps), int(heads), int(kv_heads), int(max_len), out, err) != cudaSuccess)

@@ -312,13 +312,12 @@ int launch_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
               int64_t tps, int64_t heads, int64_t kv_heads, int64_t max_len, bool pos_external, float* scratch,
               uint16_t* out, int* err, cudaStream_t st) {
   using Lay = TcLayout<D>;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) !=
-        cudaSuccess)
-      return SB_INTERNAL;
-    configured = true;
-  }
+  static PerDeviceOnce configured;
+  if (!configured.run([] {
+        return cudaFuncSetAttribute(attn_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::kBytes) ==
+               cudaSuccess;
+      }))
+    return SB_INTERNAL;
   const int span = attention_tc_span(rows, kv_heads, max_len);
   const int splits = int((max_len + span - 1) / span);
   // Splits merge inside their cluster; no partials reach memory.

@@ -439,13 +439,12 @@ namespace {
 template <int EPI>
 int launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mw2, const GemmArgs& a, int tiles_n,
                 cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) !=
-        cudaSuccess)
-      return SB_INTERNAL;
-    configured = true;
-  }
+  static PerDeviceOnce configured;
+  if (!configured.run([] {
+        return cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) ==
+               cudaSuccess;
+      }))
+    return SB_INTERNAL;
   const int tiles = tiles_n * ((a.m + kBM - 1) / kBM);
   const dim3 grid{unsigned(tiles < kNumSMs ? tiles : kNumSMs), 1u, 1u};  // persistent: one CTA per SM
   if (launch_pdl(gemm_tc_kernel<EPI>, grid, dim3(kGThreads), size_t(kGSmem), st, mx, mw, mw2, a) != cudaSuccess)

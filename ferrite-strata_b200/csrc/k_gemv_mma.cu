@@ -473,11 +473,6 @@ int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
 // slower with 12 warps (28.8 against 23.9 us cold) and keeps 8.  Every warp
 // keeps at least two groups.  Ties keep the narrower block.
 int choose_warps(int tiles, int groups) {
-  static const bool wide_ok = [] {
-    const char* v = std::getenv("STRATA_B200_GEMV_WARPS");  // "8": always 8 (A/B runs)
-    return !(v && std::string(v) == "8");
-  }();
-  if (!wide_ok) return kWarps;
   int best = kWarps;
   long best_cost = -1;
   for (int w : {8, 12, 16}) {
@@ -528,17 +523,7 @@ int dispatch_nt(const Params& p, GemvMode mode, bool scale16_ok, bool pdl, cudaS
 
 }  // namespace
 
-// STRATA_B200_GEMV=cudacore routes every batch to the CUDA-core GEMV (for A/B measurements).
-static bool tensor_core_gemv_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("STRATA_B200_GEMV");
-    return !(v && std::string(v) == "cudacore");
-  }();
-  return on;
-}
-
 bool gemv_mma_supported(const GemvMmaArgs& a) {
-  if (!tensor_core_gemv_enabled() && a.mode != GemvMode::QkvRope) return false;
   const LinearBatch& b = a.lb;
   if (b.fmt != WFormat::W4G32 && b.fmt != WFormat::W8PC) return false;
   if (b.k % 32 || b.m <= 0) return false;

@@ -36,6 +36,13 @@ def _norm_in(v, arr):
     return np.asarray(arr)
 
 
+def _threads() -> int:
+    # The threaded oracle kernels give every output element to one thread,
+    # which accumulates it in the same k order as the single-threaded ones,
+    # so the results are identical; threads only shorten large parity cases.
+    return ora.max_threads()
+
+
 def evaluate(graph, inputs: dict, all_reduce=None) -> dict:
     """Run `graph` on the oracle.  `inputs` maps value id -> array; KV caches
     are updated in place in the returned dict.  `all_reduce(name, x)` sums
@@ -81,10 +88,10 @@ def evaluate(graph, inputs: dict, all_reduce=None) -> dict:
             continue
         elif pid == "fused::linear_w4g32":
             x = ins[0].reshape(-1, ins[0].shape[-1])
-            res = ora.linear_w4g32(x, ins[1], ora.to_bf16(ins[2]))
+            res = ora.linear_w4g32(x, ins[1], ora.to_bf16(ins[2]), threads=_threads())
         elif pid == "fused::linear_w8pc":
             x = ins[0].reshape(-1, ins[0].shape[-1])
-            res = ora.linear_w8pc(x, ins[1], ins[2])
+            res = ora.linear_w8pc(x, ins[1], ins[2], threads=_threads())
         elif pid == "fused::rms_norm":
             res = ora.rms_norm(ins[0], ins[1], float(n.attrs.get("eps", 1e-5)))
         elif pid == "fused::rope":
@@ -105,7 +112,7 @@ def evaluate(graph, inputs: dict, all_reduce=None) -> dict:
                 if 0 <= p < kc.shape[2]:
                     kc[seq[r], :, p, :] = knr[r]
                     vc[seq[r], :, p, :] = vnr[r]
-            res = ora.attention(q, kc, vc, seq, pos, H, G, d)
+            res = ora.attention(q, kc, vc, seq, pos, H, G, d, threads=_threads())
         elif pid == "fused::embed":
             res, _rc = ora.embed(ins[0], ins[1])
         elif pid == "fused::argmax":

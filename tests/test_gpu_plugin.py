@@ -150,9 +150,12 @@ def _decode_case(plugin, shape, batch, layers, max_len, fill, tp_world=1, head="
     return g, hd, res, caches, ref
 
 
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 8, 64])
 def test_llama7b_shape_decode_two_layers(cuda, plugin, batch):
-    """7B-shape decode (int4 g32, KV 2048 prefilled) at reduced depth: 2 layers."""
+    """7B-shape decode (int4 g32, KV 2048 prefilled) at reduced depth: 2 layers,
+    at each batch of the decode configuration.  Batch 64 runs the GEMV's widest
+    x-row blocks (33-64 rows) in the q/k/v + RoPE and gate/up + SwiGLU
+    epilogues."""
     g, hd, res, caches, ref = _decode_case(plugin, LLAMA_7B, batch, 2, 2112, 2048)
     assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, "7B logits")
     for i, raw in caches.items():  # the appended k/v rows match the oracle's
@@ -193,6 +196,62 @@ def test_prefill_runs_tensor_core_gemms_and_matches_oracle(cuda, plugin, fmt, kv
     for i, raw in caches.items():
         got = ora.from_bf16(np.frombuffer(raw, np.uint16).reshape(g.values[i].dims))
         assert_close(got, ref[i], TOL_BF16, g.values[i].name)
+
+
+def test_llama7b_shape_int8_prefill_layer(cuda, plugin):
+    """One 7B-shape int8 prefill layer at full width (hidden 4096, 32 x 128
+    heads, FFN 11008, vocab 32000): 2 sequences x 128 tokens from position 0,
+    so every linear is a tcgen05 GEMM (K = 11008 on down_proj, the SwiGLU
+    epilogue at 11008 features) and the head runs on each sequence's last
+    row."""
+    batch, seq = 2, 128
+    g, hd = decoder_graph(LLAMA_7B, batch=batch, seq=seq, max_len=seq, fmt="w8pc", layers=1, head="logits",
+                          last_token=True)
+    host = seeded_graph_inputs(g, cache_fill=0)
+    host[hd.tokens] = ora.uniform_i32(2, batch * seq, 0, LLAMA_7B.vocab)
+    host[hd.pos] = np.tile(np.arange(seq, dtype=np.int32), batch)
+    res, caches = run_graph(plugin, g, host)
+    ref = graph_eval.evaluate(g, {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in host.items()})
+    assert g.values[hd.out].dims == (batch, LLAMA_7B.vocab)
+    assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, "7B int8 prefill logits")
+    for i, raw in caches.items():
+        got = ora.from_bf16(np.frombuffer(raw, np.uint16).reshape(g.values[i].dims))
+        assert_close(got, ref[i], TOL_BF16, g.values[i].name)
+
+
+def test_loaded_executable_runs_on_the_device(cuda, plugin):
+    """serialize -> deserialize_load -> run (raw.rs:760-788): an executable
+    loaded from its blob runs a 7B-shape decode layer on the device and
+    matches both the oracle and the executable it was saved from, bit for
+    bit."""
+    g, hd = decoder_graph(LLAMA_7B, batch=4, seq=1, max_len=2112, fmt="w4g32", layers=1, head="logits")
+    host = seeded_graph_inputs(g, cache_fill=2048)
+    host[hd.tokens] = ora.uniform_i32(2, 4, 0, LLAMA_7B.vocab)
+    host[hd.pos] = np.array([2048, 2047, 1000, 3], np.int32)
+    exe = plugin.compile(g)
+    assert exe is not None
+    blob = plugin.serialize(exe)
+    exe.free()
+    assert plugin.abi_compatible(blob)
+    outs = []
+    for loaded in (False, True):
+        arena, bufs = {}, []
+        for i, v in enumerate(g.values):
+            if v.producer is None:
+                b = plugin.upload(v.dtype, v.dims, to_device_bytes(v, host[i]))
+                bufs.append(b)
+                arena[i] = Device(b)
+        e = plugin.deserialize(blob, g) if loaded else plugin.compile(g)
+        try:
+            e.run(arena, every_value=False)
+            outs.append(arena[hd.out])
+        finally:
+            for b in bufs:
+                b.release()
+            e.free()
+    assert np.array_equal(np.asarray(outs[0]), np.asarray(outs[1]))
+    ref = graph_eval.evaluate(g, host)
+    assert_close(as_f32(g.values[hd.out], outs[1]), ref[hd.out], TOL_BF16, "loaded executable logits")
 
 
 def test_prefill_last_token_head_runs_on_each_sequence_last_row(cuda, plugin):
