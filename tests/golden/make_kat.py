@@ -2,12 +2,12 @@
 for the hot path, transcribed with the file:line each value comes from.
 
 The reference is Rust and cannot be built in this image, so its golden values
-are taken from its test sources as text.  When the reference checkout is
-present (REFERENCE_ROOT, default /root/reference) this script also re-reads
+are taken from its test sources as text.  When the environment variable
+REFERENCE_ROOT names a checkout of the reference, this script also re-reads
 every cited line and fails if the literal it quotes is not there, so the
 fixture cannot drift from its source.
 
-Usage: python tests/golden/make_kat.py
+Usage: REFERENCE_ROOT=<reference checkout> python tests/golden/make_kat.py
 """
 from __future__ import annotations
 
@@ -16,7 +16,7 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT", "")
 KERNELS = "crates/ferrite-strata-cpu/tests/kernels.rs"
 E2E = "crates/ferrite-strata-runtime/tests/end_to_end.rs"
 
@@ -59,8 +59,8 @@ CASES = [
 
 
 def verify() -> None:
-    if not os.path.isdir(REF):
-        print(f"{REF} not present; transcription not re-checked", file=sys.stderr)
+    if not REF or not os.path.isdir(REF):
+        print("REFERENCE_ROOT not set to a reference checkout; transcription not re-checked", file=sys.stderr)
         return
     for cid, src, line, literal, _ in CASES:
         with open(os.path.join(REF, src)) as f:
