@@ -461,6 +461,15 @@ def run_prefill(args):
     for _ in range(args.warmup):
         model.bound.run_async()
     sync()
+    if args.profile_step:
+        torch.cuda.profiler.start()
+        for _ in range(args.steps):
+            model.bound.run_async()
+        sync()
+        torch.cuda.profiler.stop()
+        model.close()
+        plugin.close()
+        return 0
     launches0 = plugin.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clocks:
@@ -618,6 +627,9 @@ def main():
     ap.add_argument("--seq", type=int, default=2048, help="tokens per prompt with --prefill")
     ap.add_argument("--sweep", action="store_true",
                     help="time the quantized Linear sweep (K = N = 4096, M in {1, 16, 128, 2048}, int4 and int8)")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after the warm-up, run --steps steps between cudaProfilerStart/Stop and exit "
+                         "(for ncu --profile-from-start off)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     shape, batch0, kv_fill, metric = MODELS[args.model]
@@ -674,6 +686,19 @@ def main():
     for _ in range(args.warmup):
         model.bound.run_async()
     barrier()
+    if args.profile_step:
+        # --steps steps between cudaProfilerStart and cudaProfilerStop, for a
+        # profiler started with --profile-from-start off; nothing else runs.
+        torch.cuda.profiler.start()
+        for _ in range(args.steps):
+            model.bound.run_async()
+        barrier()
+        torch.cuda.profiler.stop()
+        model.close()
+        plugin.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
     launches0 = plugin.launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
