@@ -79,23 +79,6 @@ static int32_t linear_common(WFormat fmt, const uint16_t* x, int64_t m, int64_t 
   ga.lb = b;
   ga.mode = GemvMode::Plain;
   ga.pdl = pdl_enabled();
-  if (gemv_tma_supported(ga)) {
-    // The stream-K GEMV's workspace (block counters, zeroed, and partial
-    // sums) as a stream-ordered temporary.
-    const cudaStream_t st = S(stream);
-    const int nn = int(n);
-    const int counters = gemv_tma_counters(GemvMode::Plain, &nn, 1);
-    const uint64_t pbytes = gemv_tma_partial_bytes(int(m));
-    const size_t cbytes = (size_t(counters) * sizeof(int) + 255) / 256 * 256;
-    void* tmp = nullptr;
-    if (cudaMallocAsync(&tmp, cbytes + pbytes, st) != cudaSuccess) return SB_RESOURCE_EXHAUSTED;
-    int rc = cudaMemsetAsync(tmp, 0, cbytes, st) == cudaSuccess ? SB_OK : SB_INTERNAL;
-    if (rc == SB_OK)
-      rc = launch_gemv_tma(ga, static_cast<int*>(tmp), counters,
-                           reinterpret_cast<float*>(static_cast<char*>(tmp) + cbytes), pbytes, nullptr, st);
-    cudaFreeAsync(tmp, st);
-    return rc;
-  }
   if (gemv_mma_supported(ga)) return launch_gemv_mma(ga, S(stream));
   return launch_linear(b, S(stream));
 }

@@ -34,17 +34,5 @@ struct GemvMmaArgs {
 bool gemv_mma_supported(const GemvMmaArgs& a);
 int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st);
 
-// The TMA-fed stream-K GEMV (k_gemv_tma.cu).  It needs a workspace: one
-// counter per 128-row block (gemv_tma_counters; zero before the first launch,
-// and left zero by every launch) and gemv_tma_partial_bytes of partial sums.
-// Launches that overlap on the GPU must not share a workspace.
-bool gemv_tma_supported(const GemvMmaArgs& a);
-// Counters for a launch over jobs of n[0..njobs) rows in `mode`.
-int gemv_tma_counters(GemvMode mode, const int* n, int njobs);
-// Partial-sum bytes for a launch over m rows of x.
-uint64_t gemv_tma_partial_bytes(int m);
-int launch_gemv_tma(const GemvMmaArgs& a, int* counters, int counter_capacity, float* partials,
-                    uint64_t partial_bytes, int* err, cudaStream_t st);
-
 
 }  // namespace sb

@@ -212,33 +212,7 @@ struct Lowerer {
     }
     fuse_qkv_rope();
     plan_gemm_scratch();
-    plan_gemv_workspace();
     return true;
-  }
-
-  // Decode-sized quantised linears (and the fused q/k/v projection) run on
-  // the stream-K GEMV, which keeps per-block counters and partial sums in a
-  // workspace of the executable; size it for the largest of them.
-  void plan_gemv_workspace() {
-    for (const Step& st : exe.steps) {
-      int n[3] = {0, 0, 0}, njobs = 0;
-      sb::GemvMode mode = sb::GemvMode::Plain;
-      if (st.kind == SK::Linear && !st.scratch_bytes &&
-          (st.fmt == sb::WFormat::W4G32 || st.fmt == sb::WFormat::W8PC)) {
-        njobs = st.njobs;
-        for (int j = 0; j < njobs; ++j) n[j] = int(g.values[st.v[1 + 4 * j]].dims[0]);
-        if (st.epi == sb::Epilogue::SwiGLU) mode = sb::GemvMode::SwiGLU;
-      } else if (st.kind == SK::QkvRope) {
-        njobs = 3;
-        n[0] = int(st.i[2] * st.i[4]);
-        n[1] = n[2] = int(st.i[3] * st.i[4]);
-        mode = sb::GemvMode::QkvRope;
-      } else {
-        continue;
-      }
-      exe.gemv_counter_cap = std::max(exe.gemv_counter_cap, sb::gemv_tma_counters(mode, n, njobs));
-      exe.gemv_partial_bytes = std::max(exe.gemv_partial_bytes, sb::gemv_tma_partial_bytes(int(st.i[0])));
-    }
   }
 
   // Linear steps over more than kGemvMaxRows rows run as tcgen05 GEMMs over
@@ -945,8 +919,6 @@ Exe::~Exe() {
   for (auto& c : graphs)
     if (c.exec) cudaGraphExecDestroy(c.exec);
   if (ws) cudaFree(ws);
-  if (gemv_counters) cudaFree(gemv_counters);
-  if (gemv_partials) cudaFree(gemv_partials);
 }
 
 namespace {
@@ -1098,11 +1070,7 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
         ga.lb = b;
         ga.mode = st.epi == sb::Epilogue::SwiGLU ? sb::GemvMode::SwiGLU : sb::GemvMode::Plain;
         ga.pdl = sb::pdl_enabled();
-        if (exe.gemv_counters && sb::gemv_tma_supported(ga))
-          rc = sb::launch_gemv_tma(ga, exe.gemv_counters, exe.gemv_counter_cap, exe.gemv_partials,
-                                   exe.gemv_partial_bytes, ctx.d_err, s);
-        else
-          rc = sb::gemv_mma_supported(ga) ? sb::launch_gemv_mma(ga, s) : sb::launch_linear(b, s);
+        rc = sb::gemv_mma_supported(ga) ? sb::launch_gemv_mma(ga, s) : sb::launch_linear(b, s);
         break;
       }
       case SK::QkvRope: {
@@ -1132,11 +1100,6 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
         e.tokens_per_seq = int(st.i[6]);
         e.theta = st.d;
         e.err = ctx.d_err;
-        if (exe.gemv_counters && sb::gemv_tma_supported(ga)) {
-          rc = sb::launch_gemv_tma(ga, exe.gemv_counters, exe.gemv_counter_cap, exe.gemv_partials,
-                                   exe.gemv_partial_bytes, ctx.d_err, s);
-          break;
-        }
         if (!sb::gemv_mma_supported(ga))
           fail(STRATA_INTERNAL, "fused q/k/v projection `" + st.label + "` has an unsupported layout");
         rc = sb::launch_gemv_mma(ga, s);

@@ -656,13 +656,6 @@ void enqueue_run(Ctx& c, const StrataRunArgs* a) {
       fail(STRATA_INVALID_ARGUMENT, "no buffer for input `" + e.g.values[v].name + "` of `" + e.label + "`");
   c.ensure_device();
   if (!e.ws && e.ws_bytes) cuda_check(cudaMalloc(&e.ws, e.ws_bytes), "workspace cudaMalloc");
-  if (!e.gemv_counters && e.gemv_counter_cap) {
-    cuda_check(cudaMalloc(reinterpret_cast<void**>(&e.gemv_partials), e.gemv_partial_bytes), "GEMV workspace");
-    cuda_check(cudaMalloc(reinterpret_cast<void**>(&e.gemv_counters), size_t(e.gemv_counter_cap) * sizeof(int)),
-               "GEMV counters");
-    cuda_check(cudaMemsetAsync(e.gemv_counters, 0, size_t(e.gemv_counter_cap) * sizeof(int), c.stream),
-               "GEMV counters");
-  }
 
   if (!graphs_enabled()) {
     enqueue(c, e, ext);

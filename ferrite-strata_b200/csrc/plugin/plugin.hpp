@@ -104,12 +104,6 @@ struct Exe {
   std::vector<int64_t> ws_off;      // value -> workspace offset, -1 if none
   uint64_t ws_bytes = 0;
   void* ws = nullptr;
-  // Decode GEMV workspace (kept across runs): per-block counters, zero
-  // between launches, and partial sums.
-  int gemv_counter_cap = 0;
-  uint64_t gemv_partial_bytes = 0;
-  int* gemv_counters = nullptr;
-  float* gemv_partials = nullptr;
   std::vector<bool> is_output;
   std::vector<bool> needed_input;   // graph inputs some step reads
   // CUDA graph cache, keyed by the external pointers of a run.
