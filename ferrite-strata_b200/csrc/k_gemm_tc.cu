@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "k_elem.cuh"
+#include "k_tc.cuh"
 
 namespace sb {
 
@@ -40,13 +41,8 @@ constexpr int kBBytes = kBN * kBK * 2;            // 32 KB
 constexpr int kGStageBytes = kABytes + kBBytes;   // 48 KB
 constexpr int kGSmem = kGStages * kGStageBytes + 1024 + 256;  // ring + alignment + barriers
 constexpr uint32_t kTmemCols = 2 * kBN;        // two accumulators of 256 f32 columns
-constexpr uint32_t kWaitLimit = 1u << 22;         // bounded mbarrier polls
 
-// Instruction descriptor, kind::f16: f32 accumulate (bits 4-5 = 1), bf16 A
-// and B (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
-// bit 17, M >> 4 at bit 24.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
-                            (uint32_t(kBM >> 4) << 24);
+constexpr uint32_t kIdesc = tc::idesc_bf16(kBM, kBN);
 
 struct GemmArgs {
   int m, n, k;               // n: output features (for SwiGLU: of the gate and of the up matrix)
@@ -59,81 +55,7 @@ struct GemmArgs {
   int* err;
 };
 
-__device__ __forceinline__ uint32_t su32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
-}
-
-// Wait for the phase with parity `parity` to complete; false when the poll
-// limit runs out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const uint32_t a = su32(bar);
-  for (uint32_t i = 0; i < kWaitLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
-      : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile whose
-// rows are 128 bytes (64 bf16): 8-row core groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
-  const uint32_t a = su32(tile);
-  uint64_t d = uint64_t((a & 0x3FFFF) >> 4);  // start address
-  d |= uint64_t(1) << 16;                      // leading byte offset (unused when swizzled)
-  d |= uint64_t(1024 >> 4) << 32;              // stride byte offset
-  d |= uint64_t(1) << 46;                      // descriptor version
-  d |= uint64_t(2) << 61;                      // SWIZZLE_128B
-  return d;
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
-          tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
-      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
-}
+using namespace tc;
 
 // Epilogue of one tile for one token row: TMEM columns [col0, col0 + 256) of
 // this warp's lane quarter.  EPI 0: y = scale * acc (+ residual); EPI 1: the
@@ -323,7 +245,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
           const uint64_t da = sw128_desc(sa), db = sw128_desc(sa + kABytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)  // +32 bytes along K per step
-            umma_bf16(acc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), (kb | kk) != 0);
+            umma_bf16(acc, da + uint64_t(2 * kk), db + uint64_t(2 * kk), kIdesc, (kb | kk) != 0);
           umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[b]);

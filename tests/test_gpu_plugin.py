@@ -254,6 +254,40 @@ def test_loaded_executable_runs_on_the_device(cuda, plugin):
     assert_close(as_f32(g.values[hd.out], outs[1]), ref[hd.out], TOL_BF16, "loaded executable logits")
 
 
+@pytest.mark.parametrize("batch,seq,heads,kv_heads,d,offset", [
+    (2, 300, 8, 2, 128, 0),     # 3 query tiles x 3 position tiles, 4:1 GQA
+    (1, 520, 4, 4, 128, 0),     # 5 x 5 tiles, MHA, a 8-row last query tile
+    (2, 200, 8, 8, 64, 0),      # head_dim 64
+    (2, 150, 8, 4, 128, 333),   # continuing prompts: positions 333.. after a prefilled cache
+])
+def test_prefill_attention_kernel_across_tiles(cuda, plugin, batch, seq, heads, kv_heads, d, offset):
+    """One fused::attention node over several tokens per sequence: the
+    tcgen05 prefill kernel (128-row query tiles, 128-position K/V tiles,
+    online softmax across tiles, causal mask from the positions) against the
+    oracle, including a cache prefilled before the prompt's own positions."""
+    b = GraphBuilder("prefill_attention")
+    R, L = batch * seq, offset + seq + 37
+    q = b.input(BF16, (R, heads * d), "q")
+    k = b.input(BF16, (R, kv_heads * d), "k")
+    v = b.input(BF16, (R, kv_heads * d), "v")
+    kc = b.input(BF16, (batch, kv_heads, L, d), "k_cache")
+    vc = b.input(BF16, (batch, kv_heads, L, d), "v_cache")
+    pos = b.input(I32, (R,), "pos")
+    out = b.node(Op.custom("fused::attention"), [q, k, v, kc, vc, pos], [(BF16, (R, heads * d))],
+                 {"num_heads": heads, "num_kv_heads": kv_heads, "head_dim": d}, "attention")[0]
+    b.output(out)
+    g = b.build()
+    cache = lambda seed: np.concatenate(
+        [ora.round_bf16(ora.normal(seed, (batch, kv_heads, offset, d))),
+         np.zeros((batch, kv_heads, L - offset, d), np.float32)], axis=2)
+    host = {q: ora.round_bf16(ora.normal(51, (R, heads * d))), k: ora.round_bf16(ora.normal(52, (R, kv_heads * d))),
+            v: ora.round_bf16(ora.normal(53, (R, kv_heads * d))), kc: cache(54), vc: cache(55),
+            pos: np.tile(np.arange(offset, offset + seq, dtype=np.int32), batch)}
+    res, caches = run_graph(plugin, g, host)
+    ref = graph_eval.evaluate(g, {kk: (vv.copy() if isinstance(vv, np.ndarray) else vv) for kk, vv in host.items()})
+    assert_close(as_f32(g.values[out], res[out]), ref[out], TOL_BF16, "prefill attention")
+
+
 def test_prefill_last_token_head_runs_on_each_sequence_last_row(cuda, plugin):
     """fused::last_token: the prefill head (final norm, lm_head, argmax) runs on
     each sequence's last row only, giving the next token of every prompt."""
