@@ -6,33 +6,42 @@
 // sequence, after the step's KV append has written every row's k and v.
 // With pos = 0..S-1 this is causal self-attention over the prompt.
 //
-// One CTA per (128-row query tile, query head, sequence), heaviest tiles
-// first; 128-position K/V tiles up to the largest position of its rows.
-// Per KV tile j, FlashAttention-style with both products on tcgen05.mma
-// (kind::f16, M = 128, f32 accumulators in TMEM):
-//   S = Q K^T        A = Q (loaded once), B = K tile, S in TMEM;
+// One CTA per (pair of 128-row query tiles, query head, sequence), heaviest
+// pairs first; the two query tiles share every 128-position K/V tile, which
+// is loaded once by TMA (double-buffered).  Per query tile t and KV tile j,
+// FlashAttention-style, with both products on tcgen05.mma (kind::f16,
+// M = 128, f32 accumulators in TMEM):
+//   S_t = Q_t K^T    A = Q_t (shared memory, loaded once), B = the K tile;
+//                    S_t in TMEM columns [128 t, 128 t + 128);
 //   softmax          one thread per query row reads its S row from TMEM,
 //                    masks positions past pos[r], and keeps a running row
-//                    maximum in base 2; the probabilities P are written as
-//                    bf16 into shared memory in the K-major 128-byte-swizzled
-//                    layout the MMA reads.  O is rescaled (read, scaled,
-//                    written back in TMEM) only when a row's maximum grows
-//                    by more than 8 (a factor of 256), so P stays below 2^8;
-//                    the row sum uses the same reference maximum, so the
-//                    final O / l is exact;
-//   O += P V         A = P, B = V^T: the V tile as loaded is [position][d],
-//                    and a transposing warpgroup rewrites it [d][position]
-//                    (ldmatrix.trans + stmatrix), zeroing positions at or past
-//                    the tile's last needed position;
-// and at the end O / l as bf16.
+//                    maximum in base 2.  O_t is rescaled in TMEM only when a
+//                    row's maximum grows by more than 8 (a factor of 256), so
+//                    the probabilities stay below 2^8; the row sum uses the
+//                    same reference maximum, so the final O / l is exact.
+//                    P goes back into the first 64 columns of S_t as bf16
+//                    pairs;
+//   O_t += P_t V     A = P_t from TMEM, B = the V tile exactly as loaded
+//                    ([position][d] rows, read as an MN-major operand);
+// and at the end O_t / l as bf16.
 //
-// Warps: 0 TMA (Q once, K and V double-buffered), 1 TMEM allocation and the
-// MMA issuer (S two tiles ahead of P V, in two TMEM buffers, so the tensor
-// cores compute the next scores while the softmax works), 2-5 softmax and
-// output (TMEM lane quarter = warp % 4), 6-9 the V transpose.  Every
-// mbarrier wait is bounded; one that runs out records error word 4 and the
-// CTA winds down (the TMA thread lets its loads land, the TMEM owner frees its
-// columns).  No TMA multicast.
+// The MMAs of one thread run in issue order, and each S_t is issued after
+// the previous P_t V, so the commit that publishes S_t also says that O_t is
+// settled and P_t's columns are free: the softmax never waits for the P V.
+// While one softmax warpgroup works on its S, the tensor cores compute the
+// other query tile's products.
+//
+// Positions at or past the last one any row needs hold whatever the cache
+// holds there; P is zero for them, and the MMA warp zeroes the V rows of the
+// last tile's 16-position group that contains the end (so 0 * NaN never
+// reaches O) and stops the last P V at that group.
+//
+// Warps: 0 TMA, 1 TMEM allocation and the MMA issuer, 2-5 softmax and output
+// for query tile 0, 6-9 for query tile 1 (TMEM lane quarter = warp % 4).
+// Every mbarrier wait is bounded; one that runs out records error word 4 and
+// the CTA winds down (the TMA thread lets its loads land, the MMA warp waits
+// for its MMAs to finish, the TMEM owner frees its columns).  No TMA
+// multicast.
 #include "common.cuh"
 #include "k_elem.cuh"
 #include "k_tc.cuh"
@@ -43,49 +52,33 @@ namespace {
 
 using namespace tc;
 
-constexpr int kQ = 128;    // query rows per CTA (TMEM lanes)
+constexpr int kQ = 128;    // query rows per tile (TMEM lanes); two tiles per CTA
 constexpr int kKV = 128;   // positions per KV tile
 constexpr int kPfThreads = 320;
-constexpr uint32_t kTmemColsPf = 512;  // two S buffers (128 columns each) and O (up to 128)
+constexpr uint32_t kTmemColsPf = 512;  // S_0, S_1 (128 columns each), O_0, O_1 (head_dim each)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescale = 8.0f;  // log2 of the largest P before O is rescaled
 
 template <int D>
 struct PfLay {
-  static constexpr int kKB = D / 64;                // 64-wide blocks of head_dim
-  static constexpr int kQBytes = kQ * D * 2;        // Q: kKB blocks of [128 rows][128 B]
-  static constexpr int kKBytes = kKV * D * 2;       // one K tile, same layout
-  static constexpr int kVBytes = kKV * D * 2;       // the V tile as loaded
-  static constexpr int kVtBytes = D * kKV * 2;      // V^T: 2 blocks (64 positions) of [D rows][128 B]
-  static constexpr int kPBytes = kQ * kKV * 2;      // P: 2 blocks of [128 rows][128 B]
-  static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQBytes;     // 2 stages
-  static constexpr int kVOff = kKOff + 2 * kKBytes;
-  static constexpr int kVtOff = kVOff + 2 * kVBytes; // V: 2 stages
-  static constexpr int kPOff = kVtOff + kVtBytes;
-  static constexpr int kPosOff = kPOff + kPBytes;   // int [128] positions
-  static constexpr int kBarOff = kPosOff + kQ * 4;  // mbarriers
-  static constexpr int kBytes = kBarOff + 16 * 8 + 16 + 1024;
+  static constexpr int kKB = D / 64;                 // 64-wide blocks of head_dim
+  static constexpr int kTile = 128 * D * 2;          // a Q, K or V tile: kKB blocks of [128 rows][128 B]
+  static constexpr int kQOff = 0;                    // two query tiles
+  static constexpr int kKOff = kQOff + 2 * kTile;    // two K stages
+  static constexpr int kVOff = kKOff + 2 * kTile;    // two V stages
+  static constexpr int kPosOff = kVOff + 2 * kTile;  // int [256] positions
+  static constexpr int kBarOff = kPosOff + 2 * kQ * 4;
+  static constexpr int kBars = 16;
+  static constexpr int kBytes = kBarOff + kBars * 8 + 16 + 1024;
+  static constexpr uint32_t kOCol = 256;             // O_t at column 256 + t * D
 };
 
 struct PfArgs {
-  int tps, heads, kv_heads, max_len, qtiles;
+  int tps, heads, kv_heads, max_len, pairs;
   const int32_t* pos;
   uint16_t* out;
   int* err;
 };
-
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-
-__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
-  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
-               "r"(r[2]), "r"(r[3])
-               : "memory");
-}
 
 // 2^x by the hardware approximation (relative error about 2^-22).
 __device__ __forceinline__ float ex2(float x) {
@@ -94,8 +87,15 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+// mbar_wait by every lane of a warp, with one answer for the whole warp (a
+// lane that ran out of polls fails it for all, so the warp never splits
+// around the .sync.aligned tcgen05 instructions that follow).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
+__device__ __forceinline__ void sts128_zero(uint32_t addr) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};" ::"r"(addr), "r"(0u) : "memory");
 }
 
 template <int D>
@@ -108,24 +108,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   int* s_pos = reinterpret_cast<int*>(smem + L::kPosOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]: S buffer b holds tile 2i + b
-  uint64_t* s_used = bars + 11;  // [2]: the softmax has read S buffer b
-  uint64_t* p_full = bars + 13;
-  uint64_t* vt_full = bars + 14;
-  uint64_t* pv_done = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);  // after 16 barriers
-  __shared__ int s_len, s_fail;
+  uint64_t* k_full = bars + 1;    // [2] per stage
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per query tile: S_t of the next KV tile is in TMEM
+  uint64_t* p_full = bars + 11;   // [2] per query tile: P_t is in TMEM (4 warps arrive)
+  uint64_t* o_done = bars + 13;   // [2] per query tile: the last P_t V has completed
+  uint64_t* mma_done = bars + 15; // every MMA of the CTA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kBars);
+  __shared__ int s_len[2], s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = a.qtiles - 1 - int(blockIdx.x);  // heaviest (latest) tiles first
+  const int pair = a.pairs - 1 - int(blockIdx.x);  // heaviest (latest) pairs first
   const int h = blockIdx.y, seq = blockIdx.z;
   const int kvh = h / (a.heads / a.kv_heads);
-  const int t0 = qt * kQ;
-  const int n_rows = min(kQ, a.tps - t0);
+  const int t0 = pair * 2 * kQ;
+  const int n_rows = min(2 * kQ, a.tps - t0);
   const int64_t row0 = int64_t(seq) * a.tps + t0;
   const int kv_row0 = (seq * a.kv_heads + kvh) * a.max_len;
 
@@ -135,14 +134,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 4);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_used[s], 4);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&o_done[s], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(vt_full, 4);
-    mbar_init(pv_done, 1);
-    s_len = 0;
+    mbar_init(mma_done, 1);
+    s_len[0] = s_len[1] = 0;
     s_fail = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -155,7 +153,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   pdl_trigger();
   pdl_wait();  // q and the appended cache rows come from the previous kernels
   __syncthreads();
-  if (threadIdx.x < kQ) {
+  if (threadIdx.x < 2 * kQ) {
     int p = -1;
     if (int(threadIdx.x) < n_rows) {
       p = a.pos[row0 + threadIdx.x];
@@ -165,23 +163,27 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
     }
     s_pos[threadIdx.x] = p;
-    if (p >= 0) atomicMax(&s_len, p + 1);
+    if (p >= 0) atomicMax(&s_len[threadIdx.x >> 7], p + 1);
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int len = s_len;                       // positions any row needs
-  const int nt = (len + kKV - 1) / kKV;        // KV tiles
+  const int len = max(s_len[0], s_len[1]);     // positions any row needs
+  const int nt0 = (s_len[0] + kKV - 1) / kKV;  // KV tiles of query tile 0
+  const int nt1 = (s_len[1] + kKV - 1) / kKV;
+  const int nt = max(nt0, nt1);                // KV tiles loaded
   auto fail = [&]() { atomicExch(&s_fail, 1); };
 
   if (warp == 0) {
     // ---- TMA ------------------------------------------------------------------
     if (lane == 0 && nt > 0) {
       bool ok = true;
-      mbar_expect_tx(q_full, L::kQBytes);
-      for (int kb = 0; kb < L::kKB; ++kb)
-        tma_load_2d(smem + L::kQOff + kb * 16384, &qmap, q_full, h * D + kb * 64, int(row0));
+      mbar_expect_tx(q_full, 2 * L::kTile);
+      for (int t = 0; t < 2; ++t)
+        for (int kb = 0; kb < L::kKB; ++kb)
+          tma_load_2d(smem + L::kQOff + t * L::kTile + kb * 16384, &qmap, q_full, h * D + kb * 64,
+                      int(row0) + t * kQ);
       int k_issued = 0, v_issued = 0;
       for (int j = 0; j < nt && ok; ++j) {
         const int s = j & 1;
@@ -189,17 +191,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           ok = false;
           break;
         }
-        mbar_expect_tx(&k_full[s], L::kKBytes);
+        mbar_expect_tx(&k_full[s], L::kTile);
         for (int kb = 0; kb < L::kKB; ++kb)
-          tma_load_2d(smem + L::kKOff + s * L::kKBytes + kb * 16384, &kmap, &k_full[s], kb * 64, kv_row0 + j * kKV);
+          tma_load_2d(smem + L::kKOff + s * L::kTile + kb * 16384, &kmap, &k_full[s], kb * 64, kv_row0 + j * kKV);
         k_issued = j + 1;
         if (j >= 2 && !mbar_wait(&v_empty[s], ((j - 2) >> 1) & 1)) {
           ok = false;
           break;
         }
-        mbar_expect_tx(&v_full[s], L::kVBytes);
+        mbar_expect_tx(&v_full[s], L::kTile);
         for (int kb = 0; kb < L::kKB; ++kb)
-          tma_load_2d(smem + L::kVOff + s * L::kVBytes + kb * 16384, &vmap, &v_full[s], kb * 64, kv_row0 + j * kKV);
+          tma_load_2d(smem + L::kVOff + s * L::kTile + kb * 16384, &vmap, &v_full[s], kb * 64, kv_row0 + j * kKV);
         v_issued = j + 1;
       }
       if (!ok) fail();
@@ -209,71 +211,94 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_wait(&v_full[j & 1], (j >> 1) & 1);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer -------------------------------------------------------------
-    if (lane == 0 && nt > 0) {
-      constexpr uint32_t kIdS = idesc_bf16(kQ, kKV), kIdO = idesc_bf16(kQ, D);
-      const uint32_t tO = tmem + 256;
-      bool ok = mbar_wait(q_full, 0);
-      // S of tile j into TMEM buffer j % 2, once its K has landed and the
-      // softmax has read that buffer's previous tile (j - 2).
-      auto issue_s = [&](int j) {
-        const int s = j & 1;
-        if (!mbar_wait(&k_full[s], (j >> 1) & 1) || (j >= 2 && !mbar_wait(&s_used[s], ((j - 2) >> 1) & 1)))
-          return false;
+    // ---- MMA issuer (lane 0 issues; the warp waits and zeroes V) ----------------
+    if (nt > 0) {
+      constexpr uint32_t kIdS = idesc_bf16(kQ, kKV), kIdO = idesc_bf16(kQ, D, true);
+      const int ntt[2] = {nt0, nt1};
+      // S_t of KV tile j into TMEM columns [128 t, 128 t + 128).
+      auto issue_s = [&](int t, int j) {
         tc_fence_after();
+        if (lane == 0) {
+          const uint8_t* qs = smem + L::kQOff + t * L::kTile;
+          const uint8_t* ks = smem + L::kKOff + (j & 1) * L::kTile;
 #pragma unroll
-        for (int kb = 0; kb < L::kKB; ++kb) {
-          const uint64_t da = sw128_desc(smem + L::kQOff + kb * 16384);
-          const uint64_t db = sw128_desc(smem + L::kKOff + s * L::kKBytes + kb * 16384);
+          for (int kb = 0; kb < L::kKB; ++kb) {
+            const uint64_t da = sw128_desc(qs + kb * 16384), db = sw128_desc(ks + kb * 16384);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + uint32_t(s * 128), da + uint64_t(2 * kk), db + uint64_t(2 * kk), kIdS, (kb | kk) != 0);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(tmem + uint32_t(t * 128), da + uint64_t(2 * kk), db + uint64_t(2 * kk), kIdS,
+                        (kb | kk) != 0);
+          }
+          umma_commit(&s_full[t]);
         }
-        umma_commit(&s_full[s]);
-        umma_commit(&k_empty[s]);
-        return true;
+        __syncwarp();
       };
-      auto issue_pv = [&](int j) {
-        if (!mbar_wait(p_full, j & 1) || !mbar_wait(vt_full, j & 1)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {  // 64 positions per block
-          const uint64_t da = sw128_desc(smem + L::kPOff + kb * 16384);
-          const uint64_t db = sw128_desc(smem + L::kVtOff + kb * (D * 128));
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tO, da + uint64_t(2 * kk), db + uint64_t(2 * kk), kIdO, (j | kb | kk) != 0);
-        }
-        umma_commit(pv_done);
-        return true;
-      };
-      // S runs two tiles ahead of P V, so the scores of the next tile are
-      // ready when the softmax finishes the current one.
-      if (ok) ok = issue_s(0);
-      if (ok && nt > 1) ok = issue_s(1);
+      bool ok = warp_wait(q_full, 0) && warp_wait(&k_full[0], 0);
+      if (ok) {
+        for (int t = 0; t < 2; ++t)
+          if (ntt[t] > 0) issue_s(t, 0);
+        if (lane == 0) umma_commit(&k_empty[0]);
+        __syncwarp();
+      }
       for (int j = 0; j < nt && ok; ++j) {
-        ok = issue_pv(j);
-        if (ok && j + 2 < nt) ok = issue_s(j + 2);
+        const int s = j & 1;
+        uint8_t* vs = smem + L::kVOff + s * L::kTile;
+        if (!(ok = warp_wait(&v_full[s], (j >> 1) & 1))) break;
+        int ksl = kKV / 16;  // 16-position K steps of the P V product
+        if (j == nt - 1) {
+          const int nv = len - j * kKV, nv16 = (nv + 15) & ~15, nz = nv16 - nv;
+          for (int i = lane; i < nz * L::kKB * 8; i += 32) {
+            const int piece = i & 7, rr = (i >> 3) % nz, kb = (i >> 3) / nz;
+            sts128_zero(su32(vs + kb * 16384 + (nv + rr) * 128 + piece * 16));
+          }
+          fence_proxy_async();
+          __syncwarp();
+          ksl = nv16 / 16;
+        }
+        if (j + 1 < nt && !(ok = warp_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1))) break;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= ntt[t]) continue;
+          if (!(ok = warp_wait(&p_full[t], j & 1))) break;
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t tP = tmem + uint32_t(t * 128), tO = tmem + L::kOCol + uint32_t(t * D);
+            const uint64_t vd = sw128_desc_mn(vs, 16384);
+            for (int kk = 0; kk < ksl; ++kk)
+              umma_bf16_ts(tO, tP + uint32_t(kk * 8), vd + uint64_t(kk * (2048 >> 4)), kIdO, (j | kk) != 0);
+            if (j + 1 >= ntt[t]) umma_commit(&o_done[t]);
+          }
+          __syncwarp();
+          if (j + 1 < ntt[t]) issue_s(t, j + 1);
+        }
+        if (!ok) break;
+        if (lane == 0) {
+          umma_commit(&v_empty[s]);
+          if (j + 1 < nt) umma_commit(&k_empty[(j + 1) & 1]);
+        }
+        __syncwarp();
       }
       if (!ok) fail();
+      if (lane == 0) umma_commit(mma_done);
+      __syncwarp();
+      warp_wait(mma_done, 0);
     }
-  } else if (warp < 6) {
-    // ---- softmax and output: thread = query row --------------------------------
+  } else {
+    // ---- softmax and output: thread = query row of tile t ------------------------
+    const int t = (warp - 2) >> 2;
     const int quarter = warp & 3, row = quarter * 32 + lane;
     const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
-    const uint32_t tO = tmem + lane_addr + 256;
-    const int prow = s_pos[row];
+    const uint32_t tS = tmem + lane_addr + uint32_t(t * 128);
+    const uint32_t tO = tmem + lane_addr + L::kOCol + uint32_t(t * D);
+    const int prow = s_pos[t * kQ + row];
+    const int my_nt = t ? nt1 : nt0;
     const float sl = kLog2e / sqrtf(float(D));
     float m_ref = -INFINITY, l = 0.0f;
-    const uint32_t pbase = su32(smem + L::kPOff) + uint32_t(row) * 128;
     bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (ok && !mbar_wait(&s_full[j & 1], (j >> 1) & 1)) {
-        fail();
-        ok = false;
-      }
+    // The loop stays converged: a lane whose wait ran out stops waiting and
+    // records the failure; no output is written then.
+    for (int j = 0; j < my_nt; ++j) {
+      if (ok && !mbar_wait(&s_full[t], j & 1)) ok = false;
       tc_fence_after();
-      const uint32_t tS = tmem + lane_addr + uint32_t((j & 1) * 128);
       const int p0 = j * kKV;
       // The whole S row (128 columns) in two loads and one wait.
       uint32_t r[kKV];
@@ -299,28 +324,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         l *= corr;
         m_ref = mt;
       }
-      // P = 2^(s - m_ref) as bf16 pairs; masked positions are 0.
-      uint32_t pk[kKV / 2];
+      // P = 2^(s - m_ref) as bf16 pairs (masked positions 0), packed in place.
       float ps = 0.0f;
 #pragma unroll
       for (int e = 0; e < kKV; e += 2) {
         const float x0 = e < nv ? ex2(__uint_as_float(r[e]) - m_ref) : 0.0f;
         const float x1 = e + 1 < nv ? ex2(__uint_as_float(r[e + 1]) - m_ref) : 0.0f;
         ps += x0 + x1;
-        pk[e / 2] = pack_bf2(x0, x1);
+        r[e / 2] = pack_bf2(x0, x1);
       }
       l += ps;
-      // S has been read: the MMA may compute the next tile's scores.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_used[j & 1]);
-      // The previous tile's P V must be done before P and O are touched.
-      if (j >= 1 && ok && !mbar_wait(pv_done, (j - 1) & 1)) {
-        fail();
-        ok = false;
-      }
-      tc_fence_after();
-      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+      // O_t is settled (its last P V completed before this S was published).
+      if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o32[32];
@@ -330,38 +345,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           tmem_st32(tO + uint32_t(c * 32), o32);
         }
       }
-      // P row into the two 64-position blocks (16-byte pieces swizzled by row & 7).
-#pragma unroll
-      for (int kb = 0; kb < 2; ++kb)
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          const int w0 = kb * 32 + c8 * 4;
-          sts128(pbase + uint32_t(kb * 16384) + (uint32_t(c8 ^ (row & 7)) << 4), pk[w0], pk[w0 + 1], pk[w0 + 2],
-                 pk[w0 + 3]);
-        }
-      fence_proxy_async();
+      tmem_st64(tS, r);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[t]);
     }
     // ---- output: O / l ---------------------------------------------------------
-    if (nt > 0 && ok && !mbar_wait(pv_done, (nt - 1) & 1)) {
-      fail();
-      ok = false;
-    }
+    if (my_nt > 0 && ok && !mbar_wait(&o_done[t], 0)) ok = false;
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) fail();
     tc_fence_after();
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-    uint16_t* orow = a.out + (row0 + row) * int64_t(a.heads) * D + int64_t(h) * D;
+    const int qrow = t * kQ + row;
+    uint16_t* orow = a.out + (row0 + qrow) * int64_t(a.heads) * D + int64_t(h) * D;
 #pragma unroll
     for (int c = 0; c < D / 32; ++c) {
       uint32_t r[32];
-      if (nt > 0) {
+      if (my_nt > 0) {
         tmem_ld32(tO + uint32_t(c * 32), r);
       } else {
 #pragma unroll
         for (int e = 0; e < 32; ++e) r[e] = 0u;
       }
-      if (row < n_rows && ok) {
+      if (qrow < n_rows && ok) {
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           uint32_t w[4];
@@ -370,47 +376,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             w[e] = pack_bf2(__uint_as_float(r[8 * v + 2 * e]) * inv, __uint_as_float(r[8 * v + 2 * e + 1]) * inv);
           *reinterpret_cast<uint4*>(orow + c * 32 + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-      }
-    }
-  } else {
-    // ---- V transpose: [position][d] -> [d][position], 8x8 blocks --------------
-    const int tw = warp - 6;
-    const int i = lane >> 3, jr = lane & 7;
-    const uint32_t vdst = su32(smem + L::kVtOff);
-    constexpr int kQuads = (D / 8) * 4;  // (d block, group of four position blocks)
-    bool ok = true;
-    for (int j = 0; j < nt; ++j) {
-      if (ok && (!mbar_wait(&v_full[j & 1], (j >> 1) & 1) || (j >= 1 && !mbar_wait(pv_done, (j - 1) & 1)))) {
-        fail();
-        ok = false;
-      }
-      const uint32_t vsrc = su32(smem + L::kVOff + (j & 1) * L::kVBytes);
-      const int p0 = j * kKV;
-      for (int qi = tw; qi < kQuads; qi += 4) {
-        const int db = qi >> 2, kq = qi & 3;
-        const int kbk = 4 * kq + i;          // this lane's 8-position block
-        const int r = 8 * kbk + jr;          // source row (position within the tile)
-        const uint32_t src = vsrc + uint32_t((db >> 3) * 16384 + r * 128) + (uint32_t((db & 7) ^ (r & 7)) << 4);
-        const int d = 8 * db + jr;           // destination row
-        const uint32_t dst =
-            vdst + uint32_t((kbk >> 3) * (D * 128) + d * 128) + (uint32_t((kbk & 7) ^ (d & 7)) << 4);
-        uint32_t v[4];
-        ldsm_x4_trans(v, src);
-        // Thread (g, q) holds positions 8 (4 kq + b) + 2q and + 1 of block b.
-        const int qq = lane & 3;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int pp = p0 + 8 * (4 * kq + b) + 2 * qq;
-          if (pp >= len) v[b] &= 0u;
-          else if (pp + 1 >= len) v[b] &= 0x0000FFFFu;
-        }
-        stsm_x4(dst, v);
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(vt_full);
-        mbar_arrive(&v_empty[j & 1]);
       }
     }
   }
@@ -468,8 +433,8 @@ int launch_pf(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
   if (!make_map(&qm, q, uint64_t(batch * tps), uint64_t(heads * D)) || !make_map(&km, kc, kv_rows, D) ||
       !make_map(&vm, vc, kv_rows, D))
     return SB_INTERNAL;
-  PfArgs args{int(tps), int(heads), int(kv_heads), int(max_len), int((tps + kQ - 1) / kQ), pos, out, err};
-  const dim3 grid{unsigned(args.qtiles), unsigned(heads), unsigned(batch)};
+  PfArgs args{int(tps), int(heads), int(kv_heads), int(max_len), int((tps + 2 * kQ - 1) / (2 * kQ)), pos, out, err};
+  const dim3 grid{unsigned(args.pairs), unsigned(heads), unsigned(batch)};
   if (launch_pdl(attn_prefill_tc_kernel<D>, grid, dim3(kPfThreads), size_t(L::kBytes), st, qm, km, vm, args) !=
       cudaSuccess)
     return SB_INTERNAL;
@@ -492,7 +457,8 @@ int launch_attention_prefill(const uint16_t* q, const uint16_t* k_cache, const u
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!a16(q) || !a16(k_cache) || !a16(v_cache)) return SB_INVALID_ARGUMENT;
   const int64_t batch = rows / tokens_per_seq;
-  if (batch * kv_heads * max_len > int64_t(INT32_MAX)) return SB_INVALID_ARGUMENT;
+  if (batch * kv_heads * max_len > int64_t(INT32_MAX) || rows + 2 * kQ > int64_t(INT32_MAX))
+    return SB_INVALID_ARGUMENT;
   if (head_dim == 128)
     return launch_pf<128>(q, k_cache, v_cache, pos, batch, tokens_per_seq, heads, kv_heads, max_len, out, err, st);
   return launch_pf<64>(q, k_cache, v_cache, pos, batch, tokens_per_seq, heads, kv_heads, max_len, out, err, st);

@@ -65,11 +65,26 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
   return d;
 }
 
+// Shared-memory matrix descriptor of an MN-major, 128-byte-swizzled tile: 128-byte
+// rows of 64 consecutive M (or N) elements, one row per K index, 8-row groups
+// 1024 bytes apart (stride byte offset), and the next 64 M (or N) elements
+// `mn_block_bytes` further on (leading byte offset).
+__device__ __forceinline__ uint64_t sw128_desc_mn(const void* tile, uint32_t mn_block_bytes) {
+  const uint32_t a = su32(tile);
+  uint64_t d = uint64_t((a & 0x3FFFF) >> 4);
+  d |= uint64_t((mn_block_bytes >> 4) & 0x3FFF) << 16;
+  d |= uint64_t(1024 >> 4) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
 // Instruction descriptor, kind::f16: f32 accumulate (bits 4-5 = 1), bf16 A
-// and B (bits 7-9 = 1, 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
-// bit 17, M >> 4 at bit 24.
-constexpr uint32_t idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+// and B (bits 7-9 = 1, 10-12 = 1), A K-major (bit 15 = 0), B K-major or, with
+// b_mn, MN-major (bit 16), N >> 3 at bit 17, M >> 4 at bit 24.
+constexpr uint32_t idesc_bf16(int m, int n, bool b_mn = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(b_mn) << 16) | (uint32_t(n >> 3) << 17) |
+         (uint32_t(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -78,6 +93,16 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint6
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(
           tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Same, with A read from TMEM (M lanes, two bf16 per 32-bit column, the K
+// index increasing with the column) instead of shared memory.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -125,6 +150,23 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 64 consecutive 32-bit columns of this thread's TMEM lane, then wait.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,"
+      "%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,"
+      "%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]),
+      "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]),
+      "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]),
+      "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
