@@ -147,13 +147,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// mbar_wait by every lane of a warp, with one answer for the whole warp (a
-// lane that ran out of polls fails it for all, so the warp never splits
-// around the .sync.aligned tcgen05 instructions that follow).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
-}
-
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float m;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
@@ -336,7 +329,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int ntt[2] = {(len0 + kKV - 1) / kKV, (len1 + kKV - 1) / kKV};
       const int nt = max(ntt[0], ntt[1]);
       if (nt == 0) continue;
-      if (!(ok = warp_wait(q_full, nq & 1) && warp_wait(&k_full[nk & 1], (nk >> 1) & 1))) break;
+      if (!(ok = mbar_wait_warp(q_full, nq & 1) && mbar_wait_warp(&k_full[nk & 1], (nk >> 1) & 1))) break;
       for (int t = 0; t < 2; ++t)
         if (ntt[t] > 0) issue_s(t, nk & 1);
       if (lane == 0) umma_commit(&k_empty[nk & 1]);
@@ -345,7 +338,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int j = 0; j < nt && ok; ++j) {
         const int g = nk + j, s = g & 1;
         uint8_t* vs = smem + L::kVOff + s * L::kTile;
-        if (!(ok = warp_wait(&v_full[s], (g >> 1) & 1))) break;
+        if (!(ok = mbar_wait_warp(&v_full[s], (g >> 1) & 1))) break;
         int ksl = kKV / 16;  // 16-position K steps of the P V product
         if (j == nt - 1) {
           const int nv = len - j * kKV, nv16 = (nv + 15) & ~15, nz = nv16 - nv;
@@ -357,10 +350,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
           __syncwarp();
           ksl = nv16 / 16;
         }
-        if (j + 1 < nt && !(ok = warp_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1))) break;
+        if (j + 1 < nt && !(ok = mbar_wait_warp(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1))) break;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= ntt[t]) continue;
-          if (!(ok = warp_wait(&p_full[t], ns[t] & 1))) break;
+          if (!(ok = mbar_wait_warp(&p_full[t], ns[t] & 1))) break;
           ++ns[t];
           tc_fence_after();
           if (lane == 0) {
@@ -388,7 +381,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (!ok) fail();
     if (lane == 0) umma_commit(mma_done);
     __syncwarp();
-    warp_wait(mma_done, 0);
+    mbar_wait_warp(mma_done, 0);
   } else {
     // ---- softmax and output: thread = query row of tile t ------------------------
     const int t = (warp - 2) >> 2;
@@ -431,13 +424,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       for (int j = 0; j < my_nt; ++j) {
         if (ok && !mbar_wait(&s_full[t], nsp & 1)) ok = false;
         ++nsp;
+        __syncwarp();  // the poll may have split the warp; tcgen05.ld needs it whole
         tc_fence_after();
         const int p0 = j * kKV;
-        // The whole S row (128 columns) in two loads and one wait.
+        // The whole S row (128 columns).
         uint32_t r[kKV];
-        tmem_ld64_nowait(tS, r);
-        tmem_ld64_nowait(tS + 64, r + 64);
-        tmem_ld_wait();
+        tmem_ld64(tS, r);
+        tmem_ld64(tS + 64, r + 64);
         // Positions past pos[r] become -inf (whatever the cache holds there), on
         // the diagonal tiles only: the others have no masked position in the warp.
         const int nv = min(kKV, prow - p0 + 1);  // valid positions of this row in the tile (<= 0: none)
@@ -551,33 +544,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiled encode_fn() {
-  static EncodeTiled fn = [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess)
-      return EncodeTiled(nullptr);
-    return reinterpret_cast<EncodeTiled>(p);
-  }();
-  return fn;
-}
-
 // bf16 [rows, cols] row-major as 64 x 128 tiles, 128-byte swizzled.
 bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
-  EncodeTiled enc = encode_fn();
-  if (!enc) return false;
-  const cuuint64_t dims[2] = {cols, rows};
-  const cuuint64_t strides[1] = {cols * 2};
-  const cuuint32_t box[2] = {64, 128};
-  const cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, 64, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <int D>
@@ -613,7 +583,7 @@ int launch_pf(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
 bool attention_prefill_supported(int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads,
                                  int64_t head_dim) {
   return tokens_per_seq >= 16 && rows % tokens_per_seq == 0 && attention_tc_supported(heads, kv_heads, head_dim) &&
-         heads <= 65535 && rows / tokens_per_seq <= 65535 && encode_fn() != nullptr;
+         heads <= 65535 && rows / tokens_per_seq <= 65535 && encode_tiled_fn() != nullptr;
 }
 
 int launch_attention_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,

@@ -257,7 +257,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
     int i = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++i) {
       const int b = i & 1;
-      if (!mbar_wait(&acc_full[b], (i >> 1) & 1)) {
+      if (!mbar_wait_warp(&acc_full[b], (i >> 1) & 1)) {
         atomicExch(&s_fail, 1);
         break;
       }
