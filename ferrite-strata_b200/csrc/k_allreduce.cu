@@ -221,11 +221,182 @@ __global__ void __launch_bounds__(kArnThreads)
   if (tid == 0) counters[fb] = gen;
 }
 
+// Distributed argmax over a vocabulary whose rows (the lm_head's output
+// features) are split between the tensor-parallel ranks.  Each row's best
+// logit becomes a 64-bit key that orders like (value, then lowest id): the
+// value's bits, flipped so that unsigned order is float order (-0 counted as
+// +0), over the complement of the vocabulary id; a row with no number (all
+// NaN) has key 0.  The largest key over the ranks is the global argmax with
+// the replicated argmax's rules (NaN skipped, lowest id on ties, 0 for a row
+// of NaNs).  The exchange is the one above with flags and counters at block
+// index kAmFlag0 + b and the key slots after the all-reduce's four slots; the
+// grid is always kAmBlocks blocks and block b owns rows b, b + kAmBlocks, ...
+// in every call, so the per-block double-buffer argument holds.
+constexpr int kAmBlocks = 32;
+constexpr int kAmThreads = 512;
+constexpr int kAmFlag0 = kArBlocks + kArMaxRows;
+constexpr size_t kAmSlotBytes = size_t(kAmMaxRows) * sizeof(uint64_t);
+static_assert((kAmFlag0 + kAmBlocks) * 8 * 4 <= kArFlagBytes, "flag area too small");
+
+__device__ __forceinline__ uint64_t am_key(float v, uint32_t id) {
+  uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (uint64_t(u) << 32) | uint64_t(0xFFFFFFFFu - id);
+}
+
+__device__ __forceinline__ int32_t am_id(uint64_t key) {
+  return key ? int32_t(0xFFFFFFFFu - uint32_t(key)) : 0;
+}
+
+template <typename T>
+__device__ __forceinline__ float am_ld(const T* p, int64_t i) {
+  if constexpr (sizeof(T) == 2)
+    return bf2f(p[i]);
+  else
+    return p[i];
+}
+
+__device__ __forceinline__ uint64_t am_max(uint64_t a, uint64_t b) { return a > b ? a : b; }
+
+// The block's largest key of row xr (every thread gets it).
+template <typename T>
+__device__ uint64_t am_row_key(const T* __restrict__ xr, int64_t cols, int64_t offset, uint64_t* red) {
+  uint64_t k = 0;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float v = am_ld(xr, c);
+    if (v == v) k = am_max(k, am_key(v, uint32_t(offset + c)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) k = am_max(k, __shfl_xor_sync(0xffffffffu, k, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();  // red is reused from the previous row
+  if (lane == 0) red[warp] = k;
+  __syncthreads();
+  k = 0;
+  for (int w = 0; w < int(blockDim.x >> 5); ++w) k = am_max(k, red[w]);
+  return k;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kAmThreads)
+    vocab_argmax_kernel(const T* __restrict__ x, int64_t rows, int64_t cols, int64_t offset, int rank, int world,
+                        ArPeers peers, uint32_t* __restrict__ counters, uint64_t* __restrict__ keys_out,
+                        int32_t* __restrict__ out, int* err) {
+  __shared__ uint64_t red[kAmThreads / 32];
+  __shared__ uint64_t s_key[kAmMaxRows / kAmBlocks];
+  __shared__ uint32_t s_gen;
+  __shared__ int s_ok;
+  pdl_trigger();
+  pdl_wait();  // the logits come from the preceding kernel
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const int nmine = rows > b ? int((rows - b + kAmBlocks - 1) / kAmBlocks) : 0;
+  for (int j = 0; j < nmine; ++j) {
+    const int64_t row = b + int64_t(j) * kAmBlocks;
+    const uint64_t k = am_row_key(x + row * cols, cols, offset, red);
+    if (tid == 0) s_key[j] = k;
+  }
+  __syncthreads();
+  if (world <= 1 || keys_out) {
+    for (int j = tid; j < nmine; j += blockDim.x) {
+      const int64_t row = b + int64_t(j) * kAmBlocks;
+      if (keys_out)
+        keys_out[row] = s_key[j];
+      else
+        out[row] = am_id(s_key[j]);
+    }
+    return;
+  }
+  const int fb = kAmFlag0 + b;
+  if (tid == 0) {
+    s_gen = counters[fb] + 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const uint32_t gen = s_gen;
+  const size_t slot = kArFlagBytes + 4 * kArSlotBytes + size_t(gen & 1) * kAmSlotBytes;
+  uint64_t* mine = reinterpret_cast<uint64_t*>(static_cast<char*>(peers.base[rank]) + slot);
+  for (int j = tid; j < nmine; j += blockDim.x) mine[b + j * kAmBlocks] = s_key[j];
+  __syncthreads();
+  if (tid < world && tid != rank) {
+    __threadfence_system();
+    st_release_sys(static_cast<uint32_t*>(peers.base[tid]) + fb * 8 + rank, gen);
+  }
+  if (tid < world && tid != rank) {
+    const uint32_t* f = static_cast<const uint32_t*>(peers.base[rank]) + fb * 8 + tid;
+    uint32_t spins = 0;
+    while (ld_acquire_sys(f) < gen) {
+      if (++spins == kArSpinLimit) {
+        atomicExch(&s_ok, 0);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_ok) {
+    if (tid == 0) {
+      if (err) atomicExch(err, 5);
+      counters[fb] = gen;
+    }
+    return;
+  }
+  for (int j = tid; j < nmine; j += blockDim.x) {
+    const int64_t row = b + int64_t(j) * kAmBlocks;
+    uint64_t k = 0;
+    for (int q = 0; q < world; ++q)
+      k = am_max(k, __ldcv(reinterpret_cast<const unsigned long long*>(static_cast<const char*>(peers.base[q]) +
+                                                                         slot) +
+                           row));
+    out[row] = am_id(k);
+  }
+  if (tid == 0) counters[fb] = gen;
+}
+
+__global__ void vocab_argmax_decode_kernel(const uint64_t* __restrict__ keys, int64_t rows, int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x;
+  if (i < rows) out[i] = am_id(keys[i]);
+}
+
 }  // namespace
 
-size_t allreduce_region_bytes() { return kArFlagBytes + 4 * kArSlotBytes; }
+size_t allreduce_region_bytes() { return kArFlagBytes + 4 * kArSlotBytes + 2 * kAmSlotBytes; }
 
-size_t allreduce_counter_bytes() { return (kArBlocks + kArMaxRows) * sizeof(uint32_t); }
+size_t allreduce_counter_bytes() { return (kArBlocks + kArMaxRows + kAmBlocks) * sizeof(uint32_t); }
+
+template <typename T>
+int launch_vocab_argmax(const T* x, int64_t rows, int64_t cols, int64_t offset, int rank, int world,
+                        const ArPeers* peers, uint32_t* counters, uint64_t* keys, int32_t* out, int* err,
+                        cudaStream_t st) {
+  if (rows <= 0 || cols <= 0 || offset < 0 || offset + cols > int64_t(UINT32_MAX)) return SB_INVALID_ARGUMENT;
+  const bool exchange = world > 1 && !keys;
+  if (exchange && (!peers || !counters || rows > kAmMaxRows || world > 8 || rank < 0 || rank >= world))
+    return SB_INVALID_ARGUMENT;
+  const ArPeers pr = peers ? *peers : ArPeers{};
+  // The exchange waits on the peers: no programmatic early launch of it.
+  if (exchange)
+    vocab_argmax_kernel<T><<<kAmBlocks, kAmThreads, 0, st>>>(x, rows, cols, offset, rank, world, pr, counters,
+                                                             nullptr, out, err);
+  else
+    launch_pdl(vocab_argmax_kernel<T>, dim3(kAmBlocks), dim3(kAmThreads), 0, st, x, rows, cols, offset, rank,
+               world, pr, counters, keys, out, err);
+  if (cudaGetLastError() != cudaSuccess) return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
+
+template int launch_vocab_argmax<float>(const float*, int64_t, int64_t, int64_t, int, int, const ArPeers*,
+                                        uint32_t*, uint64_t*, int32_t*, int*, cudaStream_t);
+template int launch_vocab_argmax<uint16_t>(const uint16_t*, int64_t, int64_t, int64_t, int, int, const ArPeers*,
+                                           uint32_t*, uint64_t*, int32_t*, int*, cudaStream_t);
+
+int launch_vocab_argmax_decode(const uint64_t* keys, int64_t rows, int32_t* out, cudaStream_t st) {
+  if (rows <= 0) return SB_OK;
+  launch_pdl(vocab_argmax_decode_kernel, dim3(unsigned((rows + 255) / 256)), dim3(256), 0, st, keys, rows, out);
+  if (cudaGetLastError() != cudaSuccess) return SB_INTERNAL;
+  count_launch();
+  return SB_OK;
+}
 
 bool allreduce_add_norm_supported(int64_t rows, int64_t cols, const void* x, const void* r, const void* gamma,
                                   const void* h, const void* n, int world) {

@@ -40,8 +40,8 @@
 // for query tile 0, 6-9 for query tile 1 (TMEM lane quarter = warp % 4).
 // Every mbarrier wait is bounded; one that runs out records error word 4 and
 // the CTA winds down (the TMA thread lets its loads land, the MMA warp waits
-// for its MMAs to finish, the TMEM owner frees its columns).  No TMA
-// multicast.
+// for its MMAs to finish, the TMEM owner frees its columns).  Every TMA load
+// lands in the issuing CTA's own shared memory only.
 #include "common.cuh"
 #include "k_elem.cuh"
 #include "k_tc.cuh"

@@ -134,6 +134,20 @@ int launch_allreduce_add_norm_bf16(const uint16_t* x, const uint16_t* r, const u
                                    uint16_t* n, int64_t rows, int64_t cols, float eps, int rank, int world,
                                    const ArPeers& peers, uint32_t* counters, int* err, cudaStream_t st);
 
+// Distributed argmax over a vocabulary split by rows between the tensor-
+// parallel ranks (k_allreduce.cu).  x is this rank's logits [rows, cols];
+// column c is vocabulary id offset + c.  Every rank gets, per row, the argmax
+// over all ranks' columns with the replicated argmax's rules (NaN skipped,
+// lowest id on ties, 0 for a row of NaNs).  world == 1 needs no peers.  With
+// keys set, the rank's 64-bit keys go there instead (for a u64 max all-reduce
+// by NCCL, then launch_vocab_argmax_decode).
+constexpr int kAmMaxRows = 4096;  // rows of one exchange
+template <typename T>
+int launch_vocab_argmax(const T* x, int64_t rows, int64_t cols, int64_t offset, int rank, int world,
+                        const ArPeers* peers, uint32_t* counters, uint64_t* keys, int32_t* out, int* err,
+                        cudaStream_t st);
+int launch_vocab_argmax_decode(const uint64_t* keys, int64_t rows, int32_t* out, cudaStream_t st);
+
 // Quantisation (k_quant.cu).
 int launch_quant_w4g32(const float* w, int64_t n, int64_t k, uint8_t* packed, uint16_t* scale,
                        cudaStream_t st);

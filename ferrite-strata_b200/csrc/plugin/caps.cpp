@@ -42,6 +42,7 @@ const PatternRule kRules[] = {
     {"fused::attention", true, true, true, false, false, false},
     {"fused::embed", true, true, true, false, false, false},
     {"fused::argmax", true, false, false, true, false, false},
+    {"fused::vocab_argmax", true, false, false, true, false, false},
     {"fused::all_reduce", true, true, true, false, false, false},
     {"fused::last_token", true, true, true, false, false, false},
     {"fused::quantize_w4g32", true, false, false, false, true, false},

@@ -761,6 +761,25 @@ struct Lowerer {
       st.v = {x, out};
       st.reads = {x};
       st.writes = {out};
+    } else if (p == "fused::vocab_argmax") {
+      // This rank's lm_head shard's logits [rows, cols]; column c is
+      // vocabulary id vocab_offset + c.  Output: the global argmax per row.
+      const uint32_t x = in(n, 0);
+      if (!is_float(V(x).dt) || !is_i32(V(out).dt)) return decline("vocab_argmax maps f32/bf16 rows to I32");
+      if (V(out).elements() != rows_of(V(x)))
+        fail(STRATA_INVALID_ARGUMENT, "vocab_argmax output must have one id per row");
+      const int64_t off = n.attr_int("vocab_offset", 0);
+      if (off < 0 || off + last_dim(V(x)) > int64_t(UINT32_MAX))
+        fail(STRATA_INVALID_ARGUMENT, "vocab_argmax vocab_offset is out of range");
+      st.kind = SK::VocabArgmax;
+      st.bf16 = is_bf16(V(x).dt);
+      st.i[0] = rows_of(V(x));
+      st.i[1] = last_dim(V(x));
+      st.i[2] = off;
+      st.scratch_bytes = uint64_t(st.i[0]) * sizeof(uint64_t);  // keys, for the NCCL path
+      st.v = {x, out};
+      st.reads = {x};
+      st.writes = {out};
     } else if (p == "fused::last_token") {
       const uint32_t x = in(n, 0);
       if (!float_unary_ok(x, out)) return decline("last_token needs f32 or bf16");
@@ -1114,6 +1133,28 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
         const void* src = p.at(st.v[0]);
         if (dst != src && cudaMemcpyAsync(dst, src, size_t(st.i[0]), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
           rc = SB_INTERNAL;
+        break;
+      }
+      case SK::VocabArgmax: {
+        const int64_t rows = st.i[0], cols = st.i[1], off = st.i[2];
+        int32_t* out = P<int32_t>(p, st.v[1]);
+        const void* x = p.at(st.v[0]);
+        const bool peer = ctx.world > 1 && ctx.ar_ready && rows <= sb::kAmMaxRows;
+        const bool nccl = ctx.world > 1 && !peer && ctx.comm;
+        if (ctx.world > 1 && !peer && !nccl)
+          fail(STRATA_INTERNAL, "vocab_argmax `" + st.label + "` needs the tensor-parallel communicator");
+        uint64_t* keys = nccl ? reinterpret_cast<uint64_t*>(static_cast<char*>(p.exe.ws) + st.scratch_off) : nullptr;
+        const int world = ctx.world > 1 ? ctx.world : 1;
+        rc = st.bf16 ? sb::launch_vocab_argmax<uint16_t>(static_cast<const uint16_t*>(x), rows, cols, off, ctx.rank,
+                                                         world, &ctx.ar_peers, ctx.ar_counters, keys, out, ctx.d_err, s)
+                     : sb::launch_vocab_argmax<float>(static_cast<const float*>(x), rows, cols, off, ctx.rank, world,
+                                                      &ctx.ar_peers, ctx.ar_counters, keys, out, ctx.d_err, s);
+        if (rc == 0 && nccl) {
+          const ncclResult_t r = ctx.nccl.all_reduce(keys, keys, size_t(rows), ncclUint64, ncclMax, ctx.comm, s);
+          if (r != ncclSuccess)
+            fail(STRATA_INTERNAL, std::string("ncclAllReduce failed: ") + ctx.nccl.error_string(r));
+          rc = sb::launch_vocab_argmax_decode(keys, rows, out, s);
+        }
         break;
       }
       case SK::AllReduce: {

@@ -74,7 +74,7 @@ struct Ctx {
 enum class SK {
   Linear, RmsNorm, Rope, SwiGLU, Binary, Unary, Softmax, LayerNorm, Transpose, Slice,
   Broadcast, Copy, Embed, Argmax, LastToken, GemmF32, KvAppend, Attention, AllReduce, AllReduceAddNorm,
-  Quant4, Quant8, Dequant4, Dequant8, QkvRope,
+  Quant4, Quant8, Dequant4, Dequant8, QkvRope, VocabArgmax,
 };
 
 struct Step {

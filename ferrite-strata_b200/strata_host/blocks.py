@@ -18,6 +18,8 @@ fused::attention            q [R,H*d], k [R,G*d], v [R,G*d],           num_heads
                             k_cache, v_cache [B,G,L,d], pos I32 [R]    num_kv_heads, head_dim
 fused::embed                ids I32 [R], table [V,D]
 fused::argmax               x [R,C] -> I32 [R] (lowest index on ties)
+fused::vocab_argmax         logits shard [R,Vr] -> I32 [R]: the argmax   vocab_offset (id of column 0)
+                            over every tensor-parallel rank's shard
 fused::all_reduce           x -> sum of x over the tensor-parallel group
 fused::last_token           x [B*S,C] -> [B,C], each sequence's last row  tokens_per_seq
 ==========================  =========================================  ====================
@@ -26,7 +28,10 @@ fused::last_token           x [B*S,C] -> [B,C], each sequence's last row  tokens
 ``r // (R / B)`` in the caches (an in-place update of two inputs) and then
 attends over positions ``0..pos[r]``; causality comes from the positions.
 Tensor-parallel builds shard q/k/v/gate/up by output column and o/down by
-input row, with an all-reduce after o_proj and after down_proj only.
+input row, with an all-reduce after o_proj and after down_proj only.  With
+the argmax head the lm_head is vocabulary-parallel: each rank holds the rows
+``vocab_shard`` gives it and ``fused::vocab_argmax`` combines the ranks'
+row maxima into the global next-token ids (the logits head stays replicated).
 """
 from __future__ import annotations
 
@@ -88,6 +93,22 @@ def ffn_shard(ffn: int, tp_world: int, tp_rank: int) -> tuple[int, int]:
     if ffn % t:
         raise ValueError("the ffn must divide by the tensor-parallel size")
     return r * (ffn // t), ffn // t
+
+
+def vocab_shard(vocab: int, tp_world: int, tp_rank: int) -> tuple[int, int]:
+    """First vocabulary id and row count of rank ``tp_rank``'s lm_head shard:
+    equal shards of a multiple of 16 rows (the GEMV's output tile), the last
+    rank taking what remains."""
+    per = -(-vocab // (tp_world * 16)) * 16
+    v0 = min(tp_rank * per, vocab)
+    return v0, min(per, vocab - v0)
+
+
+def shard_lm_head(w, s, vocab: int, tp_world: int, tp_rank: int):
+    """Rank ``tp_rank``'s rows of the full lm_head codes ``w`` and scales ``s``
+    (both row-major with one row per vocabulary id, in any weight format)."""
+    v0, n = vocab_shard(vocab, tp_world, tp_rank)
+    return w[v0:v0 + n].copy(), (None if s is None else s[v0:v0 + n].copy())
 
 
 def weight_shapes(shape: DecoderShape, fmt: str, tp_world: int = 1, tp_rank: int = 0) -> dict:
@@ -156,17 +177,22 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
         W["k_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.k_cache")
         W["v_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.v_cache")
         hd.layers.append(LayerHandles(W))
+    # Vocabulary-parallel lm_head (argmax head at tensor-parallel size > 1).
+    vpar = head == "argmax" and t > 1
+    v0, Vr = vocab_shard(shape.vocab, t, tp_rank) if vpar else (0, shape.vocab)
+    if vpar and Vr == 0:
+        raise ValueError(f"a vocabulary of {shape.vocab} leaves rank {tp_rank} of {t} no lm_head rows")
     if head != "none":
         hd.final_norm = b.input(act, (D,), "final_norm")
         lmf = lm_fmt or fmt
         if lmf == "w4g32":
-            hd.lm_w = b.input(W4G32, (shape.vocab, D // 2), "lm_head.w")
-            hd.lm_s = b.input(BF16, (shape.vocab, D // 32), "lm_head.s")
+            hd.lm_w = b.input(W4G32, (Vr, D // 2), "lm_head.w")
+            hd.lm_s = b.input(BF16, (Vr, D // 32), "lm_head.s")
         elif lmf == "w8pc":
-            hd.lm_w = b.input(w8pc(D), (shape.vocab, D), "lm_head.w")
-            hd.lm_s = b.input(F32, (shape.vocab,), "lm_head.s")
+            hd.lm_w = b.input(w8pc(D), (Vr, D), "lm_head.w")
+            hd.lm_s = b.input(F32, (Vr,), "lm_head.s")
         else:
-            hd.lm_w = b.input(act, (shape.vocab, D), "lm_head.w")
+            hd.lm_w = b.input(act, (Vr, D), "lm_head.w")
 
     if embed:
         h = b.node(Op.custom("fused::embed"), [hd.tokens, hd.embed_table], [(act, (R, D))], {}, "embed")[0]
@@ -212,9 +238,12 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
         hf = b.node(Op.custom("fused::rms_norm"), [h, hd.final_norm], [(act, (Rh, D))],
                     {"eps": float(shape.eps)}, "final_norm_op")[0]
         W = {"wlm": hd.lm_w, "slm": hd.lm_s}
-        logits = _linear(b, hf, W, "lm", Rh, shape.vocab, lm_fmt or fmt, act, "lm_head")
+        logits = _linear(b, hf, W, "lm", Rh, Vr, lm_fmt or fmt, act, "lm_head")
         if head == "logits":
             hd.out = logits
+        elif vpar:
+            hd.out = b.node(Op.custom("fused::vocab_argmax"), [logits], [(I32, (Rh,))],
+                            {"vocab_offset": v0}, "vocab_argmax")[0]
         else:
             hd.out = b.node(Op.custom("fused::argmax"), [logits], [(I32, (Rh,))], {}, "argmax")[0]
     b.output(hd.out)

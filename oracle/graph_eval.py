@@ -43,10 +43,11 @@ def _threads() -> int:
     return ora.max_threads()
 
 
-def evaluate(graph, inputs: dict, all_reduce=None) -> dict:
+def evaluate(graph, inputs: dict, all_reduce=None, all_gather=None) -> dict:
     """Run `graph` on the oracle.  `inputs` maps value id -> array; KV caches
     are updated in place in the returned dict.  `all_reduce(name, x)` sums
-    over tensor-parallel ranks (identity when None)."""
+    over tensor-parallel ranks (identity when None); `all_gather(name, x)`
+    returns every rank's x in rank order (a one-element list when None)."""
     vals: dict[int, np.ndarray] = {}
     for i, v in enumerate(graph.values):
         if v.producer is None and i in inputs:
@@ -117,6 +118,19 @@ def evaluate(graph, inputs: dict, all_reduce=None) -> dict:
             res, _rc = ora.embed(ins[0], ins[1])
         elif pid == "fused::argmax":
             res = ora.argmax(ins[0])
+        elif pid == "fused::vocab_argmax":
+            # The argmax over the vocabulary split by rows between the ranks:
+            # the same rules as fused::argmax over the rank-ordered
+            # concatenation of the shards (NaN skipped, lowest id on ties, 0
+            # for a row with no number); alone, this shard's ids start at
+            # vocab_offset.
+            shard = np.asarray(ins[0], np.float32).reshape(-1, ins[0].shape[-1])
+            if all_gather is None:
+                ids = ora.argmax(shard).astype(np.int64)
+                has = ~np.all(np.isnan(shard), axis=1)
+                res = np.where(has, ids + int(n.attrs.get("vocab_offset", 0)), 0).astype(np.int32)
+            else:
+                res = ora.argmax(np.concatenate(all_gather(n.name, shard), axis=1))
         elif pid == "fused::last_token":
             B = graph.values[n.outputs[0]].dims[0]
             x = ins[0].reshape(B, -1, ins[0].shape[-1])

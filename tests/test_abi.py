@@ -83,6 +83,7 @@ def test_pull_query_accepts_every_hot_path_pattern(plugin, dims):
         assert plugin.supports(pid, BF16, dims) == fused
         assert plugin.supports(pid, F32, dims) == fused
     assert plugin.supports("fused::argmax", I32, dims) == fused
+    assert plugin.supports("fused::vocab_argmax", I32, dims) == fused
     assert plugin.supports("ref::add", BF16, dims) == abi.SUPPORT_FALLBACK
     assert plugin.supports("ref::linear", F32, dims) == abi.SUPPORT_FALLBACK
 

@@ -369,3 +369,34 @@ def test_device_quantize_node_is_bit_exact(cuda, plugin):
     want_c, want_s = ora.quant_w4g32(wv)
     assert np.frombuffer(res[c], np.uint8).tobytes() == want_c.tobytes()
     assert np.array_equal(np.asarray(res[s]).view(np.uint16).ravel(), want_s.ravel())
+
+
+@pytest.mark.parametrize("dtype", [BF16, F32])
+@pytest.mark.parametrize("rows,cols,offset", [(1, 4000, 0), (37, 1000, 64000), (300, 16, 31984)])
+def test_vocab_argmax_node_on_one_rank(cuda, plugin, dtype, rows, cols, offset):
+    """fused::vocab_argmax outside a tensor-parallel group: the argmax of the
+    shard plus its first vocabulary id, with the replicated argmax's rules --
+    NaN skipped, the lowest id on ties (-0 and +0 tie), 0 for a row of NaNs."""
+    b = GraphBuilder("vargmax")
+    x = b.input(dtype, (rows, cols), "logits")
+    out = b.node(Op.custom("fused::vocab_argmax"), [x], [(I32, (rows,))], {"vocab_offset": offset}, "va")[0]
+    b.output(out)
+    g = b.build()
+    v = ora.normal(3, (rows, cols))
+    if dtype == BF16:
+        v = ora.round_bf16(v)
+    r = np.arange(rows)
+    v[r, (r * 7) % cols] = 9.0           # a tie of the row maximum ...
+    v[r, (r * 7 + 5) % cols] = 9.0       # ... at a second column
+    v[r, (r * 3 + 1) % cols] = np.nan
+    v[0, :] = np.where(np.arange(cols) % 2, -0.0, 0.0)  # only zeros of both signs
+    if rows > 2:
+        v[2, :] = np.nan
+        v[1, :] = -np.inf
+    res, _ = run_graph(plugin, g, {x: v})
+    got = np.asarray(res[out])
+    want = ora.argmax(v) + offset
+    if rows > 2:
+        want[2] = 0
+    assert got[0] == offset
+    assert np.array_equal(got, want), np.nonzero(got != want)

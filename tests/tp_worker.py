@@ -10,7 +10,13 @@ second argument, a prefill of 2 x 40 rows (more rows than the fused kernel
 takes: NCCL, then the add and the norm).  The step runs three times and every
 run must give the same logits (the exchange's flags and slots alternate
 between runs).  Rank 0 writes its logits and the oracle's logits of the
-unsharded step to the path given on the command line."""
+unsharded step to the path given on the command line.
+
+With ``argmax`` as the second argument the step is the decode step with the
+vocabulary-parallel argmax head: each rank holds its rows of the lm_head, the
+graph also returns the rank's logits shard, and the ranks' ids must be equal
+to each other and to the argmax of the shards gathered in rank order (exact).
+Rank 0 then writes its ids, that argmax and every rank's ids."""
 import datetime
 import os
 import sys
@@ -27,7 +33,7 @@ import torch.distributed as dist  # noqa: E402
 
 from oracle import graph_eval, oracle as ora  # noqa: E402
 from strata_host import BF16, Device, Plugin  # noqa: E402
-from strata_host.blocks import DecoderShape, decoder_graph, shard_layer  # noqa: E402
+from strata_host.blocks import DecoderShape, decoder_graph, shard_layer, shard_lm_head, vocab_shard  # noqa: E402
 from tests.helpers import seeded_graph_inputs, to_device_bytes  # noqa: E402
 
 # 16 query / 8 kv heads of 128, FFN 11008 (the 7B FFN: at 8 ranks its shards are 1408 and 1344
@@ -51,11 +57,18 @@ def main(out_path, mode):
     else:
         full[full_hd.pos] = np.tile(np.arange(seq, dtype=np.int32), batch)
 
-    g, hd = decoder_graph(SHAPE, batch=batch, seq=seq, max_len=MAX_LEN, fmt="w4g32", head="logits",
+    head = "argmax" if mode == "argmax" else "logits"
+    g, hd = decoder_graph(SHAPE, batch=batch, seq=seq, max_len=MAX_LEN, fmt="w4g32", head=head,
                           tp_rank=rank, tp_world=world)
+    lm_w, lm_s = full[full_hd.lm_w], full[full_hd.lm_s]
+    logits_id = None
+    if head == "argmax":
+        lm_w, lm_s = shard_lm_head(lm_w, lm_s, SHAPE.vocab, world, rank)
+        logits_id = g.nodes[-1].inputs[0]
+        g.outputs.append(logits_id)
     host = {hd.tokens: full[full_hd.tokens], hd.pos: full[full_hd.pos],
             hd.embed_table: full[full_hd.embed_table], hd.final_norm: full[full_hd.final_norm],
-            hd.lm_w: full[full_hd.lm_w], hd.lm_s: full[full_hd.lm_s]}
+            hd.lm_w: lm_w, hd.lm_s: lm_s}
     for li in range(SHAPE.layers):
         shard = shard_layer({k: full[v] for k, v in full_hd.layers[li].ids.items()}, SHAPE, "w4g32", rank, world)
         for k, v in hd.layers[li].ids.items():
@@ -78,6 +91,9 @@ def main(out_path, mode):
     for _ in range(3):
         exe.run(arena)
         runs.append(np.array(arena[hd.out]))
+    shard = None
+    if logits_id is not None:
+        shard = ora.from_bf16(np.array(arena[logits_id]).view(np.uint16))
     for i, r in enumerate(runs[1:], 1):
         assert np.array_equal(r, runs[0]), f"rank {rank}: run {i} differs from run 0"
     got = runs[0]
@@ -88,7 +104,21 @@ def main(out_path, mode):
         b.release()
     plugin.close()
 
-    if rank == 0:
+    if head == "argmax":
+        import torch
+        width = vocab_shard(SHAPE.vocab, world, 0)[1]
+        pad = np.zeros((batch, width), np.float32)
+        pad[:, :shard.shape[1]] = shard
+        parts = [torch.empty(batch, width) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(pad))
+        ids = [torch.empty(batch, dtype=torch.int32) for _ in range(world)]
+        dist.all_gather(ids, torch.from_numpy(np.asarray(got, np.int32)))
+        if rank == 0:
+            logits = np.concatenate([p.numpy()[:, :vocab_shard(SHAPE.vocab, world, r)[1]]
+                                     for r, p in enumerate(parts)], axis=1)
+            np.save(out_path, np.stack([np.asarray(got, np.int32), ora.argmax(logits)] +
+                                       [i.numpy() for i in ids]))
+    elif rank == 0:
         want = graph_eval.evaluate(full_g, full)[full_hd.out]
         np.save(out_path, np.stack([np.asarray(got, np.float32), np.asarray(want, np.float32)]))
     dist.barrier()
