@@ -36,11 +36,47 @@ struct PerDeviceOnce {
   }
 };
 
+// A paged KV cache.  With a block table the caches are page pools
+// [num_pages, kv_heads, page_size, head_dim] and position p of sequence s is
+// row p % page_size of page table[s * pages_per_seq + p / page_size], so a
+// sequence's cache grows a page at a time and pages can be handed between
+// sequences by rewriting the table.  page_size is a power of two from 16 to
+// 4096, so a 16-position slab and a 128-position tile never straddle pages
+// and a page is either part of a tile or a whole number of tiles.  With no
+// table (the default) the caches are contiguous [batch, kv_heads, max_len,
+// head_dim].
+#if defined(__CUDACC__)
+#define SB_HOST_DEVICE __host__ __device__
+#else
+#define SB_HOST_DEVICE
+#endif
+struct KvPages {
+  const int32_t* table = nullptr;
+  int page_size = 0;
+  int pages_per_seq = 0;
+  int num_pages = 0;
+  SB_HOST_DEVICE bool paged() const { return table != nullptr; }
+};
+
+inline bool kv_page_size_ok(int64_t ps) { return ps >= 16 && ps <= 4096 && (ps & (ps - 1)) == 0; }
+
 #if !defined(__CUDACC__)
 bool pdl_enabled();
 #endif
 
 #if defined(__CUDACC__)
+// The cache row (head_dim elements) that holds position p of (seq, kvh), or
+// -1 when p lies outside the sequence's pages or its page index is not one of
+// the pool's pages.  Callers check 0 <= p < max_len first.
+__device__ __forceinline__ int64_t kv_row(const KvPages& kp, int seq, int kvh, int kv_heads, int max_len, int p) {
+  if (!kp.table) return (int64_t(seq) * kv_heads + kvh) * max_len + p;
+  const int lp = p / kp.page_size;
+  if (lp >= kp.pages_per_seq) return -1;
+  const int pg = __ldg(kp.table + int64_t(seq) * kp.pages_per_seq + lp);
+  if (pg < 0 || pg >= kp.num_pages) return -1;
+  return (int64_t(pg) * kv_heads + kvh) * kp.page_size + (p & (kp.page_size - 1));
+}
+
 
 __device__ __forceinline__ float bf2f(uint16_t v) { return __uint_as_float(uint32_t(v) << 16); }
 

@@ -74,16 +74,20 @@ template <typename T>
 __global__ void kv_append_kernel(const T* __restrict__ k_new, const T* __restrict__ v_new,
                                  T* __restrict__ k_cache, T* __restrict__ v_cache,
                                  const int32_t* __restrict__ pos, int rows, int tokens_per_seq,
-                                 int kv_heads, int head_dim, int max_len, int* err) {
+                                 int kv_heads, int head_dim, int max_len, KvPages kp, int* err) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x;
   const int p = pos[row];
-  if (p < 0 || p >= max_len) {
-    if (threadIdx.x == 0 && err) atomicExch(err, 2);
+  const int seq = row / tokens_per_seq;
+  // Row of kv head 0; head h is h * page_size (paged) or h * max_len rows on.
+  const bool in_range = p >= 0 && p < max_len;
+  const int64_t r0 = in_range ? kv_row(kp, seq, 0, kv_heads, max_len, p) : -1;
+  if (r0 < 0) {  // error word 2: bad position; 6: its page is missing
+    if (threadIdx.x == 0 && err) atomicExch(err, in_range ? 6 : 2);
     return;
   }
-  const int seq = row / tokens_per_seq;
+  const int64_t hstride = kp.paged() ? kp.page_size : max_len;
   const int width = kv_heads * head_dim;
   constexpr int kVec = 16 / int(sizeof(T));  // elements per 16-byte copy
   const bool vec = head_dim % kVec == 0 &&
@@ -92,7 +96,7 @@ __global__ void kv_append_kernel(const T* __restrict__ k_new, const T* __restric
   if (vec) {
     for (int c = threadIdx.x; c < width / kVec; c += blockDim.x) {
       const int i = c * kVec, h = i / head_dim, d = i - h * head_dim;
-      const int64_t dst = ((int64_t(seq) * kv_heads + h) * max_len + p) * head_dim + d;
+      const int64_t dst = (r0 + h * hstride) * head_dim + d;
       *reinterpret_cast<uint4*>(k_cache + dst) = *reinterpret_cast<const uint4*>(k_new + int64_t(row) * width + i);
       *reinterpret_cast<uint4*>(v_cache + dst) = *reinterpret_cast<const uint4*>(v_new + int64_t(row) * width + i);
     }
@@ -100,7 +104,7 @@ __global__ void kv_append_kernel(const T* __restrict__ k_new, const T* __restric
   }
   for (int i = threadIdx.x; i < width; i += blockDim.x) {
     const int h = i / head_dim, d = i % head_dim;
-    const int64_t dst = ((int64_t(seq) * kv_heads + h) * max_len + p) * head_dim + d;
+    const int64_t dst = (r0 + h * hstride) * head_dim + d;
     k_cache[dst] = k_new[int64_t(row) * width + i];
     v_cache[dst] = v_new[int64_t(row) * width + i];
   }
@@ -559,14 +563,15 @@ int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t head
 int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                         const int32_t* pos, int64_t rows, int64_t tokens_per_seq, int64_t heads,
                         int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
-                        float* scratch, uint16_t* out, int* err, cudaStream_t st) {
+                        float* scratch, uint16_t* out, int* err, cudaStream_t st, const KvPages& kp) {
   if (rows == 0) return SB_OK;
   if (attention_prefill_supported(rows, tokens_per_seq, heads, kv_heads, head_dim))
     return launch_attention_prefill(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim,
-                                    max_len, out, err, st);
+                                    max_len, out, err, st, kp);
   if (attention_tc_supported(heads, kv_heads, head_dim))
     return launch_attention_tc(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, head_dim, max_len,
-                               pos_external, scratch, out, err, st);
+                               pos_external, scratch, out, err, st, kp);
+  if (kp.paged()) return SB_INVALID_ARGUMENT;
   if (kv_heads <= 0 || heads % kv_heads || rows > 65535) return SB_INVALID_ARGUMENT;
   if (kv_heads * ((heads / kv_heads + kMaxGroup - 1) / kMaxGroup) > 65535) return SB_INVALID_ARGUMENT;
   const int splits = attention_v2_splits(rows, kv_heads, max_len);
@@ -609,12 +614,12 @@ uint64_t attention_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, 
 template <typename T>
 int launch_kv_append(const T* k_new, const T* v_new, T* k_cache, T* v_cache, const int32_t* pos,
                      int64_t rows, int64_t tokens_per_seq, int64_t kv_heads, int64_t head_dim,
-                     int64_t max_len, int* err, cudaStream_t st) {
+                     int64_t max_len, int* err, cudaStream_t st, const KvPages& kp) {
   if (rows == 0) return SB_OK;
+  if (kp.paged() && (!kv_page_size_ok(kp.page_size) || int64_t(kp.page_size) * kp.pages_per_seq != max_len))
+    return SB_INVALID_ARGUMENT;
   launch_pdl(kv_append_kernel<T>, dim3(unsigned(rows)), dim3(256), 0, st, k_new, v_new, k_cache, v_cache, pos,
-                                                      int(rows), int(tokens_per_seq),
-                                                      int(kv_heads), int(head_dim),
-                                                      int(max_len), err);
+             int(rows), int(tokens_per_seq), int(kv_heads), int(head_dim), int(max_len), kp, err);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -655,10 +660,10 @@ int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32
 
 template int launch_kv_append<uint16_t>(const uint16_t*, const uint16_t*, uint16_t*, uint16_t*,
                                         const int32_t*, int64_t, int64_t, int64_t, int64_t,
-                                        int64_t, int*, cudaStream_t);
+                                        int64_t, int*, cudaStream_t, const KvPages&);
 template int launch_kv_append<float>(const float*, const float*, float*, float*, const int32_t*,
                                      int64_t, int64_t, int64_t, int64_t, int64_t, int*,
-                                     cudaStream_t);
+                                     cudaStream_t, const KvPages&);
 template int launch_attention<uint16_t>(const uint16_t*, const uint16_t*, const uint16_t*,
                                         const int32_t*, int64_t, int64_t, int64_t, int64_t,
                                         int64_t, int64_t, float*, uint16_t*, int*, cudaStream_t);

@@ -77,15 +77,17 @@ struct PfArgs {
   const int32_t* pos;
   uint16_t* out;
   int* err;
+  KvPages kp;     // paged caches: K/V tiles are loaded a page (or a 128-row part of one) at a time
+  int pool_rows;  // rows of the K/V tensor maps
 };
 
 // One work item: a pair of query tiles of one head of one sequence.  Items
 // are numbered heaviest first (latest query rows need the most KV tiles),
 // heads fastest so that neighbouring items share a kv head's cache in L2.
 struct PfItem {
-  int t0, n_rows, h;
+  int t0, n_rows, h, seq, kvh;
   int64_t row0;
-  int kv_row0;
+  int kv_row0;  // contiguous caches: the map row of position 0 of (seq, kvh)
 };
 
 __device__ __forceinline__ PfItem pf_item(const PfArgs& a, int w) {
@@ -96,8 +98,10 @@ __device__ __forceinline__ PfItem pf_item(const PfArgs& a, int w) {
   it.t0 = pair * 2 * kQ;
   it.n_rows = min(2 * kQ, a.tps - it.t0);
   it.h = h;
+  it.seq = seq;
+  it.kvh = h / (a.heads / a.kv_heads);
   it.row0 = int64_t(seq) * a.tps + it.t0;
-  it.kv_row0 = (seq * a.kv_heads + h / (a.heads / a.kv_heads)) * a.max_len;
+  it.kv_row0 = a.kp.paged() ? 0 : (seq * a.kv_heads + it.kvh) * a.max_len;
   return it;
 }
 
@@ -248,6 +252,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       const int len = max(pf_tile_len(a, cur, 0), pf_tile_len(a, cur, 1));
       const int nt = (len + kKV - 1) / kKV;
       if (nt == 0) continue;
+      // KV tile j of the item (positions [128 j, 128 j + 128)) into dst.  A
+      // paged cache is read a page at a time (boxes of min(page_size, 128)
+      // rows, each landing at its row offset: the 128-byte swizzle is a
+      // function of the shared-memory address, which is 2048-byte aligned
+      // for every box).  A page that is missing from the table or not in the
+      // pool is read past the end of the map, which yields zeros; if the
+      // item needs any of its positions, error word 6 is set.
+      auto kv_tile = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int j) {
+        if (!a.kp.paged()) {
+          for (int kb = 0; kb < L::kKB; ++kb)
+            tma_load_2d(dst + kb * 16384, map, bar, kb * 64, it.kv_row0 + j * kKV);
+          return;
+        }
+        const int br = min(a.kp.page_size, kKV);
+        for (int r = 0; r < kKV; r += br) {
+          const int p = j * kKV + r;
+          const int64_t row = p < a.max_len ? kv_row(a.kp, it.seq, it.kvh, a.kv_heads, a.max_len, p) : -1;
+          if (row < 0 && p < len && a.err) atomicExch(a.err, 6);
+          const int y = row < 0 ? a.pool_rows : int(row);
+          for (int kb = 0; kb < L::kKB; ++kb) tma_load_2d(dst + kb * 16384 + r * 128, map, bar, kb * 64, y);
+        }
+      };
       if (lane == 0) {
         if (nq >= 1 && !mbar_wait(q_empty, (nq - 1) & 1)) ok = false;
         if (ok) {
@@ -265,18 +291,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             break;
           }
           mbar_expect_tx(&k_full[s], L::kTile);
-          for (int kb = 0; kb < L::kKB; ++kb)
-            tma_load_2d(smem + L::kKOff + s * L::kTile + kb * 16384, &kmap, &k_full[s], kb * 64,
-                        it.kv_row0 + j * kKV);
+          kv_tile(&kmap, smem + L::kKOff + s * L::kTile, &k_full[s], j);
           ++nk;
           if (g >= 2 && !mbar_wait(&v_empty[s], ((g - 2) >> 1) & 1)) {
             ok = false;
             break;
           }
           mbar_expect_tx(&v_full[s], L::kTile);
-          for (int kb = 0; kb < L::kKB; ++kb)
-            tma_load_2d(smem + L::kVOff + s * L::kTile + kb * 16384, &vmap, &v_full[s], kb * 64,
-                        it.kv_row0 + j * kKV);
+          kv_tile(&vmap, smem + L::kVOff + s * L::kTile, &v_full[s], j);
           ++nv;
         }
       }
@@ -544,16 +566,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 
-// bf16 [rows, cols] row-major as 64 x 128 tiles, 128-byte swizzled.
-bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
-  return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, 64, 128,
+// bf16 [rows, cols] row-major as 64-column x box_rows tiles, 128-byte swizzled.
+bool make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows = 128) {
+  return make_map_2d(map, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, 64, box_rows,
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <int D>
 int launch_pf(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos, int64_t batch,
               int64_t tps, int64_t heads, int64_t kv_heads, int64_t max_len, uint16_t* out, int* err,
-              cudaStream_t st) {
+              cudaStream_t st, const KvPages& kp) {
   using L = PfLay<D>;
   static PerDeviceOnce configured;
   if (!configured.run([] {
@@ -562,14 +584,17 @@ int launch_pf(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
       }))
     return SB_INTERNAL;
   CUtensorMap qm, km, vm;
-  const uint64_t kv_rows = uint64_t(batch) * uint64_t(kv_heads) * uint64_t(max_len);
-  if (!make_map(&qm, q, uint64_t(batch * tps), uint64_t(heads * D)) || !make_map(&km, kc, kv_rows, D) ||
-      !make_map(&vm, vc, kv_rows, D))
+  const uint64_t kv_rows = kp.paged() ? uint64_t(kp.num_pages) * uint64_t(kv_heads) * uint64_t(kp.page_size)
+                                      : uint64_t(batch) * uint64_t(kv_heads) * uint64_t(max_len);
+  const uint32_t box = kp.paged() ? uint32_t(std::min(kp.page_size, kKV)) : 128u;
+  if (!make_map(&qm, q, uint64_t(batch * tps), uint64_t(heads * D)) || !make_map(&km, kc, kv_rows, D, box) ||
+      !make_map(&vm, vc, kv_rows, D, box))
     return SB_INTERNAL;
   const int pairs = int((tps + 2 * kQ - 1) / (2 * kQ));
   const int64_t items = int64_t(pairs) * heads * batch;
   if (items > int64_t(INT32_MAX)) return SB_INVALID_ARGUMENT;
-  PfArgs args{int(tps), int(heads), int(kv_heads), int(max_len), pairs, int(batch), int(items), pos, out, err};
+  PfArgs args{int(tps), int(heads), int(kv_heads), int(max_len), pairs, int(batch), int(items), pos, out, err,
+              kp, int(kv_rows)};
   const dim3 grid{unsigned(std::min<int64_t>(items, kNumSMs))};
   if (launch_pdl(attn_prefill_tc_kernel<D>, grid, dim3(kPfThreads), size_t(L::kBytes), st, qm, km, vm, args) !=
       cudaSuccess)
@@ -588,16 +613,20 @@ bool attention_prefill_supported(int64_t rows, int64_t tokens_per_seq, int64_t h
 
 int launch_attention_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
                              int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
-                             int64_t max_len, uint16_t* out, int* err, cudaStream_t st) {
+                             int64_t max_len, uint16_t* out, int* err, cudaStream_t st, const KvPages& kp) {
   if (!attention_prefill_supported(rows, tokens_per_seq, heads, kv_heads, head_dim)) return SB_INVALID_ARGUMENT;
+  if (kp.paged() && (!kv_page_size_ok(kp.page_size) || int64_t(kp.page_size) * kp.pages_per_seq != max_len ||
+                     kp.num_pages <= 0 || int64_t(kp.num_pages) * kv_heads * kp.page_size >= int64_t(INT32_MAX)))
+    return SB_INVALID_ARGUMENT;
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!a16(q) || !a16(k_cache) || !a16(v_cache)) return SB_INVALID_ARGUMENT;
   const int64_t batch = rows / tokens_per_seq;
   if (batch * kv_heads * max_len > int64_t(INT32_MAX) || rows + 2 * kQ > int64_t(INT32_MAX))
     return SB_INVALID_ARGUMENT;
   if (head_dim == 128)
-    return launch_pf<128>(q, k_cache, v_cache, pos, batch, tokens_per_seq, heads, kv_heads, max_len, out, err, st);
-  return launch_pf<64>(q, k_cache, v_cache, pos, batch, tokens_per_seq, heads, kv_heads, max_len, out, err, st);
+    return launch_pf<128>(q, k_cache, v_cache, pos, batch, tokens_per_seq, heads, kv_heads, max_len, out, err, st,
+                          kp);
+  return launch_pf<64>(q, k_cache, v_cache, pos, batch, tokens_per_seq, heads, kv_heads, max_len, out, err, st, kp);
 }
 
 }  // namespace sb

@@ -89,7 +89,8 @@ __global__ void __launch_bounds__(kTcWarps * 32)
     attn_tc_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
                    const uint16_t* __restrict__ vc, const int32_t* __restrict__ pos, int tokens_per_seq,
                    int heads, int kv_heads, int max_len, int span, int splits, int pos_external,
-                   int cluster_merge, float* __restrict__ partial, uint16_t* __restrict__ out, int* err) {
+                   int cluster_merge, float* __restrict__ partial, uint16_t* __restrict__ out, int* err,
+                   KvPages kp) {
   using Lay = TcLayout<D>;
   constexpr int kCpr = D / 8;  // 16-byte chunks per row
   extern __shared__ __align__(128) uint8_t smem[];
@@ -99,20 +100,25 @@ __global__ void __launch_bounds__(kTcWarps * 32)
   const int g = lane >> 2, qd = lane & 3;
   uint8_t* ring = smem + warp * Lay::kWarpBytes;
   const int seq = row / tokens_per_seq;
-  const int64_t head_off = (int64_t(seq) * kv_heads + kvh) * int64_t(max_len) * D;
-  const uint8_t* kb = reinterpret_cast<const uint8_t*>(kc + head_off);
-  const uint8_t* vb = reinterpret_cast<const uint8_t*>(vc + head_off);
   const int t0 = split * span;
 
   pdl_trigger();
 
   // Copy slab i of this warp (global slab warp + 4 i of the span): rows below
   // `valid` are read, the rest zero-filled (their scores are masked and their
-  // V rows must be finite zeros).  Always commits one group.
+  // V rows must be finite zeros).  A slab's 16 positions are consecutive rows
+  // of one page (spans are whole multiples of 64 positions, pages of 16 or
+  // more); a slab whose page index is bad is zero-filled and sets error word 6.
+  // Always commits one group.
   auto issue = [&](int i, int lim) {
     const int s = t0 + (warp + kTcWarps * i) * kSlab;
     const int valid = min(kSlab, max(0, lim - s));
     if (valid > 0) {
+      const int64_t srow = kv_row(kp, seq, kvh, kv_heads, max_len, s);
+      const int rd = srow < 0 ? 0 : valid;  // rows read
+      if (srow < 0 && lane == 0 && err) atomicExch(err, 6);
+      const uint8_t* kb = reinterpret_cast<const uint8_t*>(kc + (srow < 0 ? 0 : srow * D));
+      const uint8_t* vb = reinterpret_cast<const uint8_t*>(vc + (srow < 0 ? 0 : srow * D));
       uint8_t* dst = ring + (i % kTcDepth) * Lay::kSlabBytes;
 #pragma unroll
       for (int j = 0; j < 2 * kSlab * kCpr / 32; ++j) {
@@ -120,9 +126,9 @@ __global__ void __launch_bounds__(kTcWarps * 32)
         const int isv = c >= kSlab * kCpr;
         const int cc = c - isv * kSlab * kCpr;
         const int r = cc / kCpr, col = cc % kCpr;
-        const int rr = r < valid ? r : 0;        // a readable address for zero-filled rows
-        const uint8_t* src = (isv ? vb : kb) + int64_t(s + rr) * (D * 2) + col * 16;
-        cp16z(dst + (isv * kSlab + r) * Lay::kRow + col * 16, src, r < valid ? 16 : 0);
+        const int rr = r < rd ? r : 0;           // a readable address for zero-filled rows
+        const uint8_t* src = (isv ? vb : kb) + int64_t(rr) * (D * 2) + col * 16;
+        cp16z(dst + (isv * kSlab + r) * Lay::kRow + col * 16, src, r < rd ? 16 : 0);
       }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(kTcWarps * 32)
 template <int D>
 int launch_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* pos, int64_t rows,
               int64_t tps, int64_t heads, int64_t kv_heads, int64_t max_len, bool pos_external, float* scratch,
-              uint16_t* out, int* err, cudaStream_t st) {
+              uint16_t* out, int* err, cudaStream_t st, const KvPages& kp) {
   using Lay = TcLayout<D>;
   static PerDeviceOnce configured;
   if (!configured.run([] {
@@ -344,7 +350,7 @@ int launch_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
   cfg.attrs = attrs;
   cfg.numAttrs = na;
   if (cudaLaunchKernelEx(&cfg, attn_tc_kernel<D>, q, kc, vc, pos, int(tps), int(heads), int(kv_heads),
-                         int(max_len), span, splits, pos_external ? 1 : 0, cluster_merge, scratch, out, err) !=
+                         int(max_len), span, splits, pos_external ? 1 : 0, cluster_merge, scratch, out, err, kp) !=
       cudaSuccess)
     return SB_INTERNAL;
   count_launch();
@@ -373,15 +379,17 @@ bool attention_tc_supported(int64_t heads, int64_t kv_heads, int64_t head_dim) {
 int launch_attention_tc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
                         int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
                         int64_t max_len, bool pos_external, float* scratch, uint16_t* out, int* err,
-                        cudaStream_t st) {
+                        cudaStream_t st, const KvPages& kp) {
   if (rows == 0) return SB_OK;
   if (!attention_tc_supported(heads, kv_heads, head_dim) || rows > 65535 || kv_heads > 65535)
     return SB_INVALID_ARGUMENT;
+  if (kp.paged() && (!kv_page_size_ok(kp.page_size) || int64_t(kp.page_size) * kp.pages_per_seq != max_len))
+    return SB_INVALID_ARGUMENT;
   if (head_dim == 128)
     return launch_tc<128>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, max_len, pos_external,
-                          scratch, out, err, st);
+                          scratch, out, err, st, kp);
   return launch_tc<64>(q, k_cache, v_cache, pos, rows, tokens_per_seq, heads, kv_heads, max_len, pos_external,
-                       scratch, out, err, st);
+                       scratch, out, err, st, kp);
 }
 
 }  // namespace sb

@@ -63,7 +63,7 @@ uint64_t attention_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, 
 template <typename T>
 int launch_kv_append(const T* k_new, const T* v_new, T* k_cache, T* v_cache, const int32_t* pos,
                      int64_t rows, int64_t tokens_per_seq, int64_t kv_heads, int64_t head_dim,
-                     int64_t max_len, int* err, cudaStream_t st);
+                     int64_t max_len, int* err, cudaStream_t st, const KvPages& kp = KvPages{});
 template <typename T>
 int launch_attention(const T* q, const T* k_cache, const T* v_cache, const int32_t* pos,
                      int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads,
@@ -75,10 +75,13 @@ int attention_chunk(int64_t rows, int64_t kv_heads);
 int attention_v2_splits(int64_t rows, int64_t kv_heads, int64_t max_len);
 uint64_t attention_v2_scratch_bytes(int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
                                     int64_t max_len);
+// A paged cache (kp.paged()) runs only on the tensor-core kernels: prefill
+// when attention_prefill_supported, else decode when attention_tc_supported.
 int launch_attention_v2(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                         const int32_t* pos, int64_t rows, int64_t tokens_per_seq, int64_t heads,
                         int64_t kv_heads, int64_t head_dim, int64_t max_len, bool pos_external,
-                        float* scratch, uint16_t* out, int* err, cudaStream_t st);
+                        float* scratch, uint16_t* out, int* err, cudaStream_t st,
+                        const KvPages& kp = KvPages{});
 
 // Tensor-core bf16 decode attention (k_attn_tc.cu); launch_attention_v2 uses
 // it when supported.  Positions per split and the split-KV merge.
@@ -87,14 +90,15 @@ bool attention_tc_supported(int64_t heads, int64_t kv_heads, int64_t head_dim);
 int launch_attention_tc(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
                         int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
                         int64_t max_len, bool pos_external, float* scratch, uint16_t* out, int* err,
-                        cudaStream_t st);
+                        cudaStream_t st, const KvPages& kp = KvPages{});
 // Prefill attention (k_attn_prefill.cu): 64-row query tiles of one sequence;
 // launch_attention_v2 uses it for 16 or more tokens per sequence.
 bool attention_prefill_supported(int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads,
                                  int64_t head_dim);
 int launch_attention_prefill(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* pos,
                              int64_t rows, int64_t tokens_per_seq, int64_t heads, int64_t kv_heads, int64_t head_dim,
-                             int64_t max_len, uint16_t* out, int* err, cudaStream_t st);
+                             int64_t max_len, uint16_t* out, int* err, cudaStream_t st,
+                             const KvPages& kp = KvPages{});
 int launch_attention_merge_bf16(const float* scratch, int64_t rows, int64_t heads, int64_t head_dim, int splits,
                                 uint16_t* out, cudaStream_t st);
 

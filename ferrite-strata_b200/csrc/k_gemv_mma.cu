@@ -163,14 +163,15 @@ __device__ __forceinline__ void tile_epilogue(const Params& p, const TileRows& t
           so[i] = olo;
           so[i + half] = ohi;
         }
-        if (pos >= 0 && pos < e.max_len) {
-          const int seq = (p.m_base + m) / e.tokens_per_seq;
-          uint16_t* cache = jl == 1 ? e.k_cache : e.v_cache;
-          uint16_t* dst = cache + ((int64_t(seq) * e.hkv + head_in_job) * e.max_len + pos) * hd;
+        const int seq = (p.m_base + m) / e.tokens_per_seq;
+        const bool in_range = pos >= 0 && pos < e.max_len;
+        const int64_t crow = in_range ? kv_row(e.kp, seq, head_in_job, e.hkv, e.max_len, pos) : -1;
+        if (crow >= 0) {
+          uint16_t* dst = (jl == 1 ? e.k_cache : e.v_cache) + crow * hd;
           dst[i] = olo;
           dst[i + half] = ohi;
         } else if (e.err) {
-          atomicExch(e.err, 2);
+          atomicExch(e.err, in_range ? 6 : 2);  // 6: the position's page is missing
         }
       }
     }

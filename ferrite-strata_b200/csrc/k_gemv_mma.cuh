@@ -16,11 +16,12 @@ struct QkvExtra {
   uint16_t* q_out;         // [M, Hq * hd] (roped q)
   uint16_t* k_out;         // optional [M, Hkv * hd] (roped k), may be null
   uint16_t* v_out;         // optional [M, Hkv * hd], may be null
-  uint16_t* k_cache;       // [B, Hkv, L, hd]
+  uint16_t* k_cache;       // [B, Hkv, L, hd], or page pools [pages, Hkv, page_size, hd] with kp's table
   uint16_t* v_cache;
   int hq, hkv, head_dim, max_len, tokens_per_seq;
   double theta;
   int* err;
+  KvPages kp;
 };
 
 struct GemvMmaArgs {

@@ -291,6 +291,13 @@ struct Lowerer {
       f.v = {L.v[0], L.v[1], L.v[2], L.v[5], L.v[6], L.v[9], L.v[10], qr, kc, vc, pos};
       f.reads = {L.v[0], L.v[1], L.v[2], L.v[5], L.v[6], L.v[9], L.v[10], pos, kc, vc};
       f.writes = {qr, kc, vc};
+      f.i[7] = AT.i[7];  // paged caches: page size, pages per sequence, pages, then the table
+      f.i[8] = AT.i[8];
+      f.i[9] = AT.i[9];
+      if (AT.i[7] > 0) {
+        f.v.push_back(AT.v[5]);
+        f.reads.push_back(AT.v[5]);
+      }
       exe.steps[si] = f;
       std::vector<int> drop = {sq, sk, kp};
       std::sort(drop.rbegin(), drop.rend());
@@ -692,7 +699,29 @@ struct Lowerer {
         return decline("attention needs one float dtype throughout and I32 positions");
       if (V(kc).dims.size() != 4 || V(kc).dims != V(vc).dims)
         fail(STRATA_INVALID_ARGUMENT, "kv caches must be [batch, kv_heads, max_len, head_dim]");
-      const int64_t B = V(kc).dims[0], KVH = V(kc).dims[1], L = V(kc).dims[2], D = V(kc).dims[3];
+      // Paged caches (attribute page_size > 0): the caches are page pools
+      // [num_pages, kv_heads, page_size, head_dim] and input 6 is the block
+      // table I32 [batch, pages_per_seq]; a sequence's max_len is
+      // pages_per_seq * page_size.
+      const int64_t ps = n.attr_int("page_size", 0);
+      uint32_t table = kNone;
+      int64_t B = V(kc).dims[0], L = V(kc).dims[2], pps = 0, npages = 0;
+      const int64_t KVH = V(kc).dims[1], D = V(kc).dims[3];
+      if (ps != 0) {
+        if (n.inputs.size() < 7) fail(STRATA_INVALID_ARGUMENT, "paged attention needs a block table (input 6)");
+        table = in(n, 6);
+        if (!is_i32(V(table).dt) || V(table).dims.size() != 2)
+          fail(STRATA_INVALID_ARGUMENT, "the block table must be I32 [batch, pages_per_seq]");
+        if (!sb::kv_page_size_ok(ps) || L != ps)
+          fail(STRATA_INVALID_ARGUMENT, "page_size must be a power of two from 16 to 4096 and the pages' length");
+        if (!is_bf16(dt)) return decline("paged attention runs on bf16 caches only");
+        npages = V(kc).dims[0];
+        B = V(table).dims[0];
+        pps = V(table).dims[1];
+        L = pps * ps;
+        if (npages <= 0 || pps <= 0 || L > INT32_MAX || npages * KVH * ps > INT32_MAX)
+          fail(STRATA_INVALID_ARGUMENT, "paged attention pool or table is empty or too large");
+      }
       const int64_t H = n.attr_int("num_heads", 0);
       if (n.attr_int("num_kv_heads", KVH) != KVH || n.attr_int("head_dim", D) != D)
         fail(STRATA_INVALID_ARGUMENT, "attention attributes disagree with the cache shape");
@@ -712,9 +741,16 @@ struct Lowerer {
       ap.i[2] = KVH;
       ap.i[3] = D;
       ap.i[4] = L;
+      ap.i[7] = ps;
+      ap.i[8] = pps;
+      ap.i[9] = npages;
       ap.v = {k, v, kc, vc, pos};
       ap.reads = {k, v, kc, vc, pos};
       ap.writes = {kc, vc};
+      if (table != kNone) {
+        ap.v.push_back(table);
+        ap.reads.push_back(table);
+      }
       push(std::move(ap));
       st.kind = SK::Attention;
       st.bf16 = is_bf16(dt);
@@ -728,12 +764,19 @@ struct Lowerer {
       // the position were written by earlier steps, so the attention kernel may
       // stream them before the previous kernel finishes.  With several tokens
       // per sequence this step's own append writes those rows.
-      st.i[6] = V(pos).producer < 0 && rows / B == 1 ? 1 : 0;
+      st.i[6] = V(pos).producer < 0 && rows / B == 1 && (table == kNone || V(table).producer < 0) ? 1 : 0;
+      st.i[7] = ps;
+      st.i[8] = pps;
+      st.i[9] = npages;
       st.scratch_bytes = is_bf16(dt) ? sb::attention_v2_scratch_bytes(rows, H, KVH, D, L)
                                      : sb::attention_scratch_bytes(rows, H, KVH, D, L);
       st.v = {q, kc, vc, pos, out};
       st.reads = {q, kc, vc, pos};
       st.writes = {out};
+      if (table != kNone) {
+        st.v.push_back(table);
+        st.reads.push_back(table);
+      }
     } else if (p == "fused::embed") {
       const uint32_t ids = in(n, 0), tab = in(n, 1);
       if (!is_i32(V(ids).dt) || !is_float(V(tab).dt) || !(V(out).dt == V(tab).dt) ||
@@ -959,6 +1002,20 @@ T* P(const Ptrs& p, uint32_t v) {
   return static_cast<T*>(p.at(v));
 }
 
+// The paged-cache descriptor of an append, attention or fused q/k/v step
+// (i[7] page size, i[8] pages per sequence, i[9] pages; the table is operand
+// `vi`), or the contiguous default.
+sb::KvPages pages_of(const Ptrs& p, const Step& st, size_t vi) {
+  sb::KvPages kp;
+  if (st.i[7] > 0 && vi < st.v.size()) {
+    kp.table = P<const int32_t>(p, st.v[vi]);
+    kp.page_size = int(st.i[7]);
+    kp.pages_per_seq = int(st.i[8]);
+    kp.num_pages = int(st.i[9]);
+  }
+  return kp;
+}
+
 void check_rc(int rc, const Step& st) {
   if (rc == 0) return;
   fail(rc == SB_INVALID_ARGUMENT ? STRATA_INVALID_ARGUMENT : STRATA_INTERNAL,
@@ -1003,14 +1060,15 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
     case SK::KvAppend:
       return sb::launch_kv_append<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]), P<T>(p, st.v[3]),
                                      P<int32_t>(p, st.v[4]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
-                                     ctx.d_err, s);
+                                     ctx.d_err, s, pages_of(p, st, 5));
     case SK::Attention: {
       float* scratch = st.scratch_bytes ? reinterpret_cast<float*>(static_cast<char*>(p.exe.ws) + st.scratch_off)
                                         : nullptr;
       if constexpr (std::is_same<T, uint16_t>::value)
         return sb::launch_attention_v2(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]),
                                        P<int32_t>(p, st.v[3]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
-                                       st.i[5], st.i[6] != 0, scratch, P<T>(p, st.v[4]), ctx.d_err, s);
+                                       st.i[5], st.i[6] != 0, scratch, P<T>(p, st.v[4]), ctx.d_err, s,
+                                       pages_of(p, st, 5));
       return sb::launch_attention<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), P<T>(p, st.v[2]),
                                      P<int32_t>(p, st.v[3]), st.i[0], st.i[1], st.i[2], st.i[3], st.i[4],
                                      st.i[5], scratch, P<T>(p, st.v[4]), ctx.d_err, s);
@@ -1119,6 +1177,7 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
         e.tokens_per_seq = int(st.i[6]);
         e.theta = st.d;
         e.err = ctx.d_err;
+        e.kp = pages_of(p, st, 11);
         if (!sb::gemv_mma_supported(ga))
           fail(STRATA_INTERNAL, "fused q/k/v projection `" + st.label + "` has an unsupported layout");
         rc = sb::launch_gemv_mma(ga, s);

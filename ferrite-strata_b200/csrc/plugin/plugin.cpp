@@ -165,6 +165,7 @@ void Ctx::check_device_error(const char* where) {
       fail(STRATA_INTERNAL, std::string(where) + ": a tensor-parallel peer did not reach the all-reduce in time");
     const char* what = word == 2 ? "a position is outside the KV cache"
                      : word == 3 ? "a token id is outside the embedding table"
+                     : word == 6 ? "a block-table entry that a position needs is not a page of the pool"
                                  : "a kernel rejected its input";
     fail(STRATA_INVALID_ARGUMENT, std::string(where) + ": " + what);
   }

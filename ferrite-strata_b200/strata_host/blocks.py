@@ -16,6 +16,8 @@ fused::rope                 x [R,H*d], pos I32 [R]                     head_dim,
 fused::swiglu               gate, up (same shape)
 fused::attention            q [R,H*d], k [R,G*d], v [R,G*d],           num_heads,
                             k_cache, v_cache [B,G,L,d], pos I32 [R]    num_kv_heads, head_dim
+                            paged: pools [P,G,ps,d], pos, then a       page_size (ps)
+                            block table I32 [B, L/ps]
 fused::embed                ids I32 [R], table [V,D]
 fused::argmax               x [R,C] -> I32 [R] (lowest index on ties)
 fused::vocab_argmax         logits shard [R,Vr] -> I32 [R]: the argmax   vocab_offset (id of column 0)
@@ -75,6 +77,7 @@ class DecoderHandles:
     embed_table: int = -1
     out: int = -1               # argmax ids, logits, or the last hidden state
     hidden_out: int = -1
+    block_table: int = -1       # paged caches: I32 [batch, pages_per_seq], shared by every layer
 
 
 def ffn_shard(ffn: int, tp_world: int, tp_rank: int) -> tuple[int, int]:
@@ -150,13 +153,20 @@ def _linear(b: GraphBuilder, x: int, W: dict, key: str, m: int, n: int, fmt: str
 def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fmt: str = "w4g32",
                   layers: int | None = None, embed: bool = True, head: str = "argmax",
                   lm_fmt: str | None = None, tp_rank: int = 0, tp_world: int = 1,
-                  last_token: bool = False, name: str = "decoder"):
+                  last_token: bool = False, kv_page: int = 0, kv_pages: int | None = None,
+                  name: str = "decoder"):
     """One forward step of ``layers`` decoder blocks over ``batch * seq`` rows.
 
     ``seq == 1`` is a decode step; ``seq > 1`` a prefill from position 0 (the
     caller fills ``pos``).  ``head``: "argmax" (next-token ids), "logits", or
     "none" (the last hidden state is the output).  ``last_token`` runs the
     head on each sequence's last row only (prefill logits for the next token).
+    ``kv_page`` > 0 pages the KV cache: each layer's k/v caches become page
+    pools ``[kv_pages, kv_heads, kv_page, head_dim]`` (``kv_pages`` defaults
+    to ``batch * ceil(max_len / kv_page)``) and one block table
+    ``I32 [batch, ceil(max_len / kv_page)]`` (``block_table``) maps every
+    sequence's positions to pages; a sequence's capacity is then a whole
+    number of pages.
     """
     layers = shape.layers if layers is None else layers
     act = F32 if fmt == "f32" else BF16
@@ -171,11 +181,21 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
     else:
         hd.tokens = b.input(act, (R, D), "x")
     hd.pos = b.input(I32, (R,), "pos")
+    attn_attrs = {}
+    if kv_page:
+        pps = -(-max_len // kv_page)
+        npages = batch * pps if kv_pages is None else kv_pages
+        hd.block_table = b.input(I32, (batch, pps), "block_table")
+        attn_attrs = {"page_size": kv_page}
     wshapes = weight_shapes(shape, fmt, t, tp_rank)
     for li in range(layers):
         W = {k: b.input(dt, dims, f"l{li}.{k}") for k, (dt, dims) in wshapes.items()}
-        W["k_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.k_cache")
-        W["v_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.v_cache")
+        if kv_page:
+            W["k_cache"] = b.input(act, (npages, G // t, kv_page, d), f"l{li}.k_pages")
+            W["v_cache"] = b.input(act, (npages, G // t, kv_page, d), f"l{li}.v_pages")
+        else:
+            W["k_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.k_cache")
+            W["v_cache"] = b.input(act, (batch, G // t, max_len, d), f"l{li}.v_cache")
         hd.layers.append(LayerHandles(W))
     # Vocabulary-parallel lm_head (argmax head at tensor-parallel size > 1).
     vpar = head == "argmax" and t > 1
@@ -210,9 +230,9 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
         rope_attrs = {"head_dim": d, "theta": float(shape.theta)}
         qr = b.node(Op.custom("fused::rope"), [q, hd.pos], [(act, (R, Hl * d))], rope_attrs, p + "q_rope")[0]
         kr = b.node(Op.custom("fused::rope"), [k, hd.pos], [(act, (R, Gl * d))], rope_attrs, p + "k_rope")[0]
-        o = b.node(Op.custom("fused::attention"), [qr, kr, v, W["k_cache"], W["v_cache"], hd.pos],
-                   [(act, (R, Hl * d))], {"num_heads": Hl, "num_kv_heads": Gl, "head_dim": d},
-                   p + "attention")[0]
+        ains = [qr, kr, v, W["k_cache"], W["v_cache"], hd.pos] + ([hd.block_table] if kv_page else [])
+        o = b.node(Op.custom("fused::attention"), ains, [(act, (R, Hl * d))],
+                   {"num_heads": Hl, "num_kv_heads": Gl, "head_dim": d, **attn_attrs}, p + "attention")[0]
         a = _linear(b, o, W, "o", R, D, fmt, act, p + "o_proj")
         if t > 1:
             a = b.node(Op.custom("fused::all_reduce"), [a], [(act, (R, D))], {}, p + "o_allreduce")[0]

@@ -99,8 +99,39 @@ def evaluate(graph, inputs: dict, all_reduce=None, all_gather=None) -> dict:
             res = ora.rope(ins[0], ins[1], int(n.attrs["head_dim"]), float(n.attrs.get("theta", 10000.0)))
         elif pid == "fused::swiglu":
             res = ora.swiglu(ins[0], ins[1])
+        elif pid == "fused::attention" and int(n.attrs.get("page_size", 0)) > 0:
+            # Paged caches: page pools [pages, G, page_size, d] and a block
+            # table [B, pages_per_seq]; position p of sequence s is row
+            # p % page_size of page table[s, p // page_size].  The append
+            # writes each new row into its page, then attention reads each
+            # sequence's pages in table order, exactly as the contiguous
+            # cache below.
+            q, kn, vn, kp, vp, pos, table = ins[:7]
+            H, G, d = int(n.attrs["num_heads"]), int(n.attrs["num_kv_heads"]), int(n.attrs["head_dim"])
+            ps = int(n.attrs["page_size"])
+            B, pps = table.shape
+            rows = q.size // (H * d)
+            seq = np.arange(rows, dtype=np.int32) // (rows // B)
+            knr = kn.reshape(rows, G, d)
+            vnr = vn.reshape(rows, G, d)
+            for r in range(rows):
+                p = int(pos[r])
+                if 0 <= p < pps * ps:
+                    pg = int(table[seq[r], p // ps])
+                    if 0 <= pg < kp.shape[0]:
+                        kp[pg, :, p % ps, :] = knr[r]
+                        vp[pg, :, p % ps, :] = vnr[r]
+            kc = np.zeros((B, G, pps * ps, d), kp.dtype)
+            vc = np.zeros_like(kc)
+            for s in range(B):
+                for lp in range(pps):
+                    pg = int(table[s, lp])
+                    if 0 <= pg < kp.shape[0]:
+                        kc[s, :, lp * ps:(lp + 1) * ps, :] = kp[pg]
+                        vc[s, :, lp * ps:(lp + 1) * ps, :] = vp[pg]
+            res = ora.attention(q, kc, vc, seq, pos, H, G, d, threads=_threads())
         elif pid == "fused::attention":
-            q, kn, vn, kc, vc, pos = ins
+            q, kn, vn, kc, vc, pos = ins[:6]
             H, G, d = int(n.attrs["num_heads"]), int(n.attrs["num_kv_heads"]), int(n.attrs["head_dim"])
             B = kc.shape[0]
             rows = q.size // (H * d)

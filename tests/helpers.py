@@ -48,6 +48,8 @@ def seeded_graph_inputs(graph, seed_base: int = 1, weight_std: float = 0.02,
             vals[i] = ora.normal(act_seed, v.dims)
         elif "norm" in name:
             vals[i] = 1.0 + ora.normal(seed, v.dims, std=0.02)
+        elif name.endswith("pages"):  # paged cache pools: every page random
+            vals[i] = ora.normal(seed, v.dims)
         elif name.endswith("cache"):
             c = np.zeros(v.dims, np.float32)
             if cache_fill:
@@ -86,3 +88,40 @@ def to_device_bytes(v, arr) -> bytes:
     if v.dtype.element == ELEM["i32"]:
         return np.ascontiguousarray(arr, np.int32).tobytes()
     return np.ascontiguousarray(arr).tobytes()
+
+
+def page_table(batch: int, pages_per_seq: int, num_pages: int, seed: int = 5) -> np.ndarray:
+    """A block table I32 [batch, pages_per_seq] that gives every sequence
+    distinct pages of a pool of num_pages, in a seeded random order (pages
+    of one sequence are neither consecutive nor ordered)."""
+    assert num_pages >= batch * pages_per_seq
+    perm = np.random.default_rng(seed).permutation(num_pages)[:batch * pages_per_seq]
+    return perm.reshape(batch, pages_per_seq).astype(np.int32)
+
+
+def to_pages(cache: np.ndarray, table: np.ndarray, num_pages: int, fill_seed: int | None = None) -> np.ndarray:
+    """Contiguous caches [B, G, L, d] scattered into a page pool
+    [num_pages, G, page, d] through the table (page = L / pages_per_seq).
+    Pages no sequence uses hold N(0, 1) noise from fill_seed (zeros if None),
+    so a kernel that reads a wrong page shows it."""
+    B, G, L, d = cache.shape
+    pps = table.shape[1]
+    page = L // pps
+    pool = np.zeros((num_pages, G, page, d), np.float32)
+    if fill_seed is not None:
+        pool[:] = ora.normal(fill_seed, pool.shape)
+    for b in range(B):
+        for lp in range(pps):
+            pool[table[b, lp]] = cache[b, :, lp * page:(lp + 1) * page, :]
+    return pool
+
+
+def from_pages(pool: np.ndarray, table: np.ndarray) -> np.ndarray:
+    """The contiguous caches [B, G, pages_per_seq * page, d] a pool holds."""
+    B, pps = table.shape
+    _, G, page, d = pool.shape
+    out = np.zeros((B, G, pps * page, d), pool.dtype)
+    for b in range(B):
+        for lp in range(pps):
+            out[b, :, lp * page:(lp + 1) * page, :] = pool[table[b, lp]]
+    return out

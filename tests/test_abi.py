@@ -13,7 +13,7 @@ import pytest
 
 from strata_host import BF16, F32, I32, W4G32, DType, GraphBuilder, Op, StrataError, w8pc
 from strata_host import abi
-from strata_host.blocks import BLOCK_512, LLAMA_7B, LLAMA_70B, decoder_graph
+from strata_host.blocks import BLOCK_512, LLAMA_7B, LLAMA_70B, DecoderShape, decoder_graph
 from strata_host.ir import SECTION_GRAPH, encode_graph, frame
 from tests.conftest import LIB, ROOT
 
@@ -342,3 +342,31 @@ def test_decode_and_prefill_layers_lower_to_their_fused_plans(plugin):
         return two - one, one
     assert per_layer(batch=2, seq=1, max_len=256, fmt="w4g32", head="argmax") == (7, 11)
     assert per_layer(batch=2, seq=96, max_len=96, fmt="w8pc", head="logits", last_token=True) == (10, 14)
+    # paged caches lower to the same plans (the table rides along with the append and attention)
+    assert per_layer(batch=2, seq=1, max_len=256, fmt="w4g32", head="argmax", kv_page=16) == (7, 11)
+    assert per_layer(batch=2, seq=96, max_len=96, fmt="w8pc", head="logits", last_token=True,
+                     kv_page=32) == (10, 14)
+
+
+@pytest.mark.parametrize("page", [16, 64, 128, 1024])
+@pytest.mark.parametrize("seq", [1, 160])
+def test_paged_cache_graphs_compile(plugin, page, seq):
+    g = decoder_graph(LLAMA_7B, batch=3, seq=seq, max_len=320, fmt="w4g32", layers=1, kv_page=page,
+                      kv_pages=2 * 3 * (-(-320 // page)))[0]
+    exe = plugin.compile(g)
+    assert exe is not None
+    exe.free()
+
+
+def test_paged_cache_rules(plugin):
+    """Pages must be a power of two from 16 to 4096 and the pools' third
+    dimension; paged f32 caches are declined (the paged kernels are bf16)."""
+    small = DecoderShape(256, 4, 2, 64, 512, 0, 1)
+    with pytest.raises(StrataError):
+        plugin.compile(decoder_graph(small, batch=2, seq=1, max_len=96, fmt="w4g32", embed=False, head="none",
+                                     kv_page=48)[0])
+    with pytest.raises(StrataError):
+        plugin.compile(decoder_graph(small, batch=2, seq=1, max_len=96, fmt="w4g32", embed=False, head="none",
+                                     kv_page=8)[0])
+    g = decoder_graph(small, batch=2, seq=1, max_len=96, fmt="f32", embed=False, head="none", kv_page=16)[0]
+    assert plugin.compile(g) is None
