@@ -160,16 +160,19 @@ class Model:
     is the hidden state and its output the last layer's hidden state."""
 
     def __init__(self, plugin, torch, batch, rank, world, layers, fmt="w4g32", seq=1, head="argmax",
-                 shape=LLAMA_7B, kv_fill=KV_FILL):
+                 shape=LLAMA_7B, kv_fill=KV_FILL, kv_page=0):
         from strata_host import Device
         self.plugin, self.torch, self.batch, self.seq = plugin, torch, batch, seq
         prefill = seq > 1
         max_len = seq if prefill else kv_fill + 64
+        if kv_page:  # a whole number of pages per sequence
+            max_len = -(-max_len // kv_page) * kv_page
         self.embed = shape.vocab > 0
         if not self.embed:
             head = "none"
         g, hd = decoder_graph(shape, batch=batch, seq=seq, max_len=max_len, fmt=fmt, layers=layers,
-                              embed=self.embed, head=head, tp_rank=rank, tp_world=world, last_token=prefill)
+                              embed=self.embed, head=head, tp_rank=rank, tp_world=world, last_token=prefill,
+                              kv_page=kv_page)
         self.graph, self.hd = g, hd
         lib = C.CDLL(plugin.path)
         q4 = lib.strata_b200_quant_w4g32
@@ -218,6 +221,10 @@ class Model:
             else:
                 self.tensors[i] = torch.randn(v.dims, generator=gen, device=dev).to(torch.bfloat16)
         torch.cuda.synchronize()
+        if kv_page:  # every sequence's pages scattered over the pool in a seeded order
+            n = self.tensors[hd.block_table].numel()
+            perm = torch.randperm(n, generator=gen, device=dev).to(torch.int32)
+            self.tensors[hd.block_table].copy_(perm.view(self.tensors[hd.block_table].shape))
         if prefill:  # each prompt from position 0
             self.tensors[hd.pos].copy_(torch.arange(seq, device=dev, dtype=torch.int32).repeat(batch))
         else:
@@ -393,6 +400,7 @@ def decode_config(args, shape, kv_fill, world, sb):
                         f"{head}), batch {args.batch}, KV cache {kv_fill} prefilled",
             "model": args.model, "batch": args.batch, "kv_len": kv_fill, "layers": args.layers,
             "parallelism": f"tp{world}",
+            "kv_cache": f"paged, {args.kv_page}-position pages" if args.kv_page else "contiguous",
             "l2": f"inputs larger than L2: {sb / 1e9:.2f} GB streamed per step"}
 
 
@@ -627,6 +635,8 @@ def main():
     ap.add_argument("--seq", type=int, default=2048, help="tokens per prompt with --prefill")
     ap.add_argument("--sweep", action="store_true",
                     help="time the quantized Linear sweep (K = N = 4096, M in {1, 16, 128, 2048}, int4 and int8)")
+    ap.add_argument("--kv-page", type=int, default=0,
+                    help="decode with a paged KV cache of this page size (block table, shuffled pages)")
     ap.add_argument("--profile-step", action="store_true",
                     help="after the warm-up, run --steps steps between cudaProfilerStart/Stop and exit "
                          "(for ncu --profile-from-start off)")
@@ -666,7 +676,8 @@ def main():
         dist.broadcast(uid, 0)
         plugin.tp_init(rank, world, bytes(uid.cpu().numpy().tobytes()))
 
-    model = Model(plugin, torch, args.batch, rank, world, args.layers, shape=shape, kv_fill=kv_fill)
+    model = Model(plugin, torch, args.batch, rank, world, args.layers, shape=shape, kv_fill=kv_fill,
+                  kv_page=args.kv_page)
     stream = torch.cuda.ExternalStream(plugin.stream())
 
     def barrier():

@@ -113,7 +113,8 @@ int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t*
 int launch_gemm_tc_swiglu(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w_gate, const uint16_t* w_up,
                           int64_t n, const float* s_gate, const float* s_up, uint16_t* y, int64_t ldy, int* err,
                           cudaStream_t st);
-// Weights as bf16 [n, k]: fmt 1 = int8 codes (exact), fmt 0 = int4 code * bf16 group scale.
+// Weights as bf16 [n, k]: fmt 1 = int8 codes (exact), fmt 0 = int4 code * bf16 group scale,
+// fmt 2 / 3 = MXFP8 / MXFP4 code * E8M0 scale (exact).
 int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, int64_t k, uint16_t* out,
                          cudaStream_t st);
 

@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "k_elem.cuh"
+#include "k_int4.cuh"
 #include "k_tc.cuh"
 
 namespace sb {
@@ -318,6 +319,36 @@ __global__ void w4g32_to_bf16_kernel(const uint8_t* __restrict__ packed, const u
   }
 }
 
+// MX codes (fmt 2: E4M3 bytes; fmt 3: E2M1 nibbles, even k low) times their
+// E8M0 scale: exact in f32, and the product of a code and a power of two is
+// a bf16 value, so the expansion is exact.
+template <int FMT>
+__global__ void mx_to_bf16_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scale, int64_t n,
+                                  int64_t k, uint16_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();  // `out` may still be read by the previous GEMM
+  constexpr int kPer = FMT == 2 ? 4 : 8;  // codes per 32-bit word
+  const int64_t words = n * k / kPer;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < words; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint32_t u = __ldg(reinterpret_cast<const uint32_t*>(codes) + i);
+    const int64_t e0 = i * kPer, row = e0 / k, col = e0 % k;
+    const float s = e8m0_f32(scale[row * (k / 32) + col / 32]);
+    if constexpr (FMT == 2) {
+      const uint32_t w0 = uint32_t(f2bf(e4m3_f32(u & 0xFF) * s)) | (uint32_t(f2bf(e4m3_f32((u >> 8) & 0xFF) * s)) << 16);
+      const uint32_t w1 =
+          uint32_t(f2bf(e4m3_f32((u >> 16) & 0xFF) * s)) | (uint32_t(f2bf(e4m3_f32(u >> 24) * s)) << 16);
+      reinterpret_cast<uint2*>(out)[i] = make_uint2(w0, w1);
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        w[e] = uint32_t(f2bf(e2m1_f32((u >> (8 * e)) & 0xF) * s)) |
+               (uint32_t(f2bf(e2m1_f32((u >> (8 * e + 4)) & 0xF) * s)) << 16);
+      reinterpret_cast<uint4*>(out)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
 using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -425,6 +456,11 @@ int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, i
     if (k % 32) return SB_INVALID_ARGUMENT;
     e = launch_pdl(w4g32_to_bf16_kernel, dim3(blocks), dim3(threads), 0, st, static_cast<const uint8_t*>(w),
                    static_cast<const uint16_t*>(scale), n, k, out);
+  } else if (fmt == 2 || fmt == 3) {  // MX: code * 2^(e - 127), exact
+    if (k % 32) return SB_INVALID_ARGUMENT;
+    auto kern = fmt == 2 ? mx_to_bf16_kernel<2> : mx_to_bf16_kernel<3>;
+    e = launch_pdl(kern, dim3(blocks), dim3(threads), 0, st, static_cast<const uint8_t*>(w),
+                   static_cast<const uint8_t*>(scale), n, k, out);
   } else {
     return SB_INVALID_ARGUMENT;
   }

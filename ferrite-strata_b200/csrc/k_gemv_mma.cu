@@ -1,5 +1,6 @@
-// Tensor-core GEMV for decode (M <= 16 rows of x per launch), int4 group-32
-// and int8 per-channel weights, with fused epilogues.
+// Tensor-core GEMV for decode (M <= 16 rows of x per launch), int4 group-32,
+// int8 per-channel and MX (MXFP8 / MXFP4, E8M0 scales per 32) weights, with
+// fused epilogues.
 //
 // Work decomposition.  The output is cut into 16-row mma.m16n8k16 tiles.  The
 // grid is persistent (at most one wave of resident blocks); block b computes
@@ -211,13 +212,17 @@ __device__ __forceinline__ void finish_tile(const Params& p, const TileRows& tr,
 // row r XOR-swizzled by r & 7: copies write whole rows and an ldmatrix 8x8
 // matrix (8 rows of one piece) lands in 8 different bank groups.  int4
 // stages also hold the bf16 scales [16 rows][kChunk].
+// FMT: 0 int4 g32 (bf16 scales), 1 int8 per channel (f32 scale in the
+// epilogue), 2 MXFP8 (E4M3 codes), 3 MXFP4 (E2M1 codes, two per byte); the
+// MX formats have one E8M0 scale byte per row and group of 32.
 template <int FMT>
 struct Stage {
-  static constexpr int kBPG = FMT == 0 ? 16 : 32;                    // bytes per row per group
+  static constexpr bool kNibbles = FMT == 0 || FMT == 3;             // two codes per byte
+  static constexpr int kBPG = kNibbles ? 16 : 32;                    // bytes per row per group
   static constexpr int kRowBytes = kChunk * kBPG;                    // 128 / 256
   static constexpr int kPieces = kRowBytes / 16;                     // 8 / 16
   static constexpr int kW = kTileRows * kRowBytes;                   // weight bytes
-  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : 0;   // scale bytes
+  static constexpr int kS = FMT == 0 ? kTileRows * kChunk * 2 : FMT >= 2 ? kTileRows * kChunk : 0;  // scale bytes
   static constexpr int kBytes = kW + kS;
   static constexpr int kDepth = 2;                                   // stages per warp
 };
@@ -229,7 +234,10 @@ __device__ __forceinline__ int piece_off(int row, int piece) {
 }
 
 __host__ __device__ constexpr size_t warp_smem_bytes(int fmt) {
-  return fmt == 0 ? size_t(Stage<0>::kDepth) * Stage<0>::kBytes : size_t(Stage<1>::kDepth) * Stage<1>::kBytes;
+  return fmt == 0   ? size_t(Stage<0>::kDepth) * Stage<0>::kBytes
+         : fmt == 1 ? size_t(Stage<1>::kDepth) * Stage<1>::kBytes
+         : fmt == 2 ? size_t(Stage<2>::kDepth) * Stage<2>::kBytes
+                    : size_t(Stage<3>::kDepth) * Stage<3>::kBytes;
 }
 
 // One int4 group of the tile for every n-tile: dequantise the words of rows
@@ -288,11 +296,11 @@ __global__ void __launch_bounds__(W * 32, W == 16 ? 1 : W == 12 ? 2 : NT <= 2 ? 
     const TileRows tr = tile_rows<MODE>(p, y);
     wlo = p.w[tr.job_lo] + int64_t(tr.row_lo + rs) * row_bytes + int64_t(gb) * S::kBPG;
     whi = p.w[tr.job_hi] + int64_t(tr.row_hi + rs) * row_bytes + int64_t(gb) * S::kBPG;
-    if constexpr (FMT == 0) {
+    if constexpr (FMT == 0 || FMT >= 2) {
       const int r = lane & 15;
       const int job = r < 8 ? tr.job_lo : tr.job_hi;
       const int row = r < 8 ? tr.row_lo + r : tr.row_hi + r - 8;
-      srow = static_cast<const uint8_t*>(p.s[job]) + (int64_t(row) * p.groups + gb) * 2;
+      srow = static_cast<const uint8_t*>(p.s[job]) + (int64_t(row) * p.groups + gb) * (FMT == 0 ? 2 : 1);
     }
   };
   if (i_tile < p.tiles) set_rows(i_tile);
@@ -324,6 +332,13 @@ __global__ void __launch_bounds__(W * 32, W == 16 ? 1 : W == 12 ? 2 : NT <= 2 ? 
             if (2 * pr < nj) cp_async4(sdst + pr * 4, ssrc + pr * 4);
           }
         }
+      } else if constexpr (FMT >= 2) {
+        // E8M0 bytes, 8 per row and chunk: lane copies 4 of row lane & 15
+        // (group counts and slice starts are multiples of 4, so every copy
+        // is whole and 4-byte aligned).
+        const int half = lane >> 4;
+        if (4 * half < nj)
+          cp_async4(dst + S::kW + (lane & 15) * kChunk + half * 4, srow + i_c * kChunk + half * 4);
       }
       if (++i_c == nchunks) {
         i_c = 0;
@@ -345,7 +360,7 @@ __global__ void __launch_bounds__(W * 32, W == 16 ? 1 : W == 12 ? 2 : NT <= 2 ? 
   const uint16_t* xbase[NT];
 #pragma unroll
   for (int t = 0; t < NT; ++t)
-    xbase[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k + int64_t(gb) * 32 + (FMT == 0 ? 8 * q : 4 * q);
+    xbase[t] = p.x + int64_t(min(t * 8 + g, p.m - 1)) * p.k + int64_t(gb) * 32 + (S::kNibbles ? 8 * q : 4 * q);
   const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix mi, row rr
   int slot = 0, buf = 0;
 
@@ -390,6 +405,74 @@ __global__ void __launch_bounds__(W * 32, W == 16 ? 1 : W == 12 ? 2 : NT <= 2 ? 
 #pragma unroll
                 for (int t = 0; t < NT; ++t) xg[t][0] = ldg16(xbase[t] + (c * kChunk + j + jj) * 32);
                 int4_group<NT>(acc, f[2 * jj], f[2 * jj + 1], slo, shi, jj, xg, 0);
+              }
+            }
+          }
+        }
+      } else if constexpr (FMT == 2) {
+        // MXFP8: int8's layout (two 16 B halves per row and group, one k16
+        // step each); each group's two MMAs go to a fresh fragment of values
+        // times 2^-120, which is scaled by 2^120 and then by the group's
+        // E8M0 scale, so every scale from 2^-126 to 2^127 is exact.
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j) {
+          if (j < nj) {
+            const int gi = c * kChunk + j;
+            uint32_t f[4];
+            ldsm_x4(f, st + piece_off<2>((mi & 1) * 8 + rr, 2 * j + (mi >> 1)));
+            const float sl = e8m0_scale(st[S::kW + g * kChunk + j], 0);
+            const float sh = e8m0_scale(st[S::kW + (g + 8) * kChunk + j], 0);
+            uint32_t a[2][4];
+#pragma unroll
+            for (int s2 = 0; s2 < 2; ++s2) {
+              a[s2][0] = e4m3_pair02(f[2 * s2]);
+              a[s2][1] = e4m3_pair02(f[2 * s2 + 1]);
+              a[s2][2] = e4m3_pair13(f[2 * s2]);
+              a[s2][3] = e4m3_pair13(f[2 * s2 + 1]);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+              for (int s2 = 0; s2 < 2; ++s2) {
+                const uint2 xv = __ldg(reinterpret_cast<const uint2*>(xbase[t] + gi * 32 + 16 * s2));
+                mma_bf16(d, a[s2][0], a[s2][1], a[s2][2], a[s2][3], prmt(xv.x, xv.y, 0x5410),
+                         prmt(xv.x, xv.y, 0x7632));
+              }
+              acc[t][0] = fmaf(d[0] * 0x1p120f, sl, acc[t][0]);
+              acc[t][1] = fmaf(d[1] * 0x1p120f, sl, acc[t][1]);
+              acc[t][2] = fmaf(d[2] * 0x1p120f, sh, acc[t][2]);
+              acc[t][3] = fmaf(d[3] * 0x1p120f, sh, acc[t][3]);
+            }
+          }
+        }
+      } else if constexpr (FMT == 3) {
+        // MXFP4: int4's layout (thread (g, q) gets word q of a group: codes
+        // 8q..8q+7); the pairs are adjacent codes, so the activations need
+        // no permute.  Values come out doubled: the scale is 2^(e - 128).
+#pragma unroll
+        for (int j = 0; j < kChunk; j += 2) {
+          if (j < nj) {  // nj is a multiple of 4
+            uint32_t f[4];
+            ldsm_x4(f, st + piece_off<3>((mi & 1) * 8 + rr, j + (mi >> 1)));
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+              const int gi = c * kChunk + j + jj;
+              const float sl = e8m0_scale(st[S::kW + g * kChunk + j + jj], 1);
+              const float sh = e8m0_scale(st[S::kW + (g + 8) * kChunk + j + jj], 1);
+              uint32_t pl[4], ph[4];
+              e2m1_pairs(f[2 * jj], pl);
+              e2m1_pairs(f[2 * jj + 1], ph);
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                const uint4 xv = ldg16(xbase[t] + gi * 32);
+                float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                mma_bf16(d, pl[0], ph[0], pl[1], ph[1], xv.x, xv.y);
+                mma_bf16(d, pl[2], ph[2], pl[3], ph[3], xv.z, xv.w);
+                acc[t][0] = fmaf(d[0], sl, acc[t][0]);
+                acc[t][1] = fmaf(d[1], sl, acc[t][1]);
+                acc[t][2] = fmaf(d[2], sh, acc[t][2]);
+                acc[t][3] = fmaf(d[3], sh, acc[t][3]);
               }
             }
           }
@@ -444,6 +527,7 @@ int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
   }
   p.gpw = (p.groups + W - 1) / W;
   p.gpw += p.gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
+  if (FMT >= 2) p.gpw = (p.gpw + 3) & ~3;  // E8M0 scales are copied 4 bytes (groups) at a time
   // Whole 8-group slices: each row's scales of a chunk are one aligned
   // 16-byte copy.
   p.scale16 = FMT == 0 && scale16_ok && p.groups % (8 * W) == 0 ? 1 : 0;
@@ -526,8 +610,13 @@ int dispatch_nt(const Params& p, GemvMode mode, bool scale16_ok, bool pdl, cudaS
 
 bool gemv_mma_supported(const GemvMmaArgs& a) {
   const LinearBatch& b = a.lb;
-  if (b.fmt != WFormat::W4G32 && b.fmt != WFormat::W8PC) return false;
+  const bool mx = b.fmt == WFormat::MXFP8 || b.fmt == WFormat::MXFP4;
+  if (b.fmt != WFormat::W4G32 && b.fmt != WFormat::W8PC && !mx) return false;
   if (b.k % 32 || b.m <= 0) return false;
+  // MX scales are copied 4 groups at a time: whole multiples of 4 groups.
+  if (mx && b.k % 128) return false;
+  for (int j = 0; mx && j < b.njobs; ++j)
+    if (reinterpret_cast<uintptr_t>(b.jobs[j].s) & 3) return false;
   // int4 scales are copied as 4-byte bf16 pairs: rows of an even number of
   // groups keep every pair aligned (an odd count goes to the CUDA-core GEMV).
   if (b.fmt == WFormat::W4G32 && (b.k / 32) % 2) return false;
@@ -558,7 +647,7 @@ bool gemv_mma_supported(const GemvMmaArgs& a) {
 int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
   if (!gemv_mma_supported(a)) return SB_INVALID_ARGUMENT;
   const LinearBatch& b = a.lb;
-  const int fmt = b.fmt == WFormat::W4G32 ? 0 : 1;
+  const int fmt = b.fmt == WFormat::W4G32 ? 0 : b.fmt == WFormat::W8PC ? 1 : b.fmt == WFormat::MXFP8 ? 2 : 3;
   const int groups = b.k / 32;
   bool scale16_ok = fmt == 0;
   for (int j = 0; j < b.njobs && scale16_ok; ++j)
@@ -599,10 +688,12 @@ int launch_gemv_mma(const GemvMmaArgs& a, cudaStream_t st) {
       p.qkv.v_out = e.v_out ? e.v_out + int64_t(m0) * e.hkv * e.head_dim : nullptr;
     }
     int rc;
-    if (fmt == 0)
-      rc = dispatch_nt<0>(p, a.mode, scale16_ok, a.pdl, st);
-    else
-      rc = dispatch_nt<1>(p, a.mode, scale16_ok, a.pdl, st);
+    switch (fmt) {
+      case 0: rc = dispatch_nt<0>(p, a.mode, scale16_ok, a.pdl, st); break;
+      case 1: rc = dispatch_nt<1>(p, a.mode, scale16_ok, a.pdl, st); break;
+      case 2: rc = dispatch_nt<2>(p, a.mode, false, a.pdl, st); break;
+      default: rc = dispatch_nt<3>(p, a.mode, false, a.pdl, st); break;
+    }
     if (rc) return rc;
   }
   return SB_OK;

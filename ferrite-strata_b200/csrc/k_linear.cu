@@ -274,6 +274,7 @@ int launch_linear(const LinearBatch& b, cudaStream_t st) {
     case WFormat::W4G32: return launch_fmt<WFormat::W4G32>(b, st);
     case WFormat::W8PC: return launch_fmt<WFormat::W8PC>(b, st);
     case WFormat::BF16: return launch_fmt<WFormat::BF16>(b, st);
+    default: break;  // MX weights run on the tensor-core GEMV only
   }
   return SB_INVALID_ARGUMENT;
 }

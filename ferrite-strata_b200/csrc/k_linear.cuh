@@ -5,7 +5,9 @@
 
 namespace sb {
 
-enum class WFormat : int { W4G32 = 0, W8PC = 1, BF16 = 2 };
+// MXFP8: E4M3 codes [N, K]; MXFP4: E2M1 codes packed two per byte [N, K/2];
+// both with one E8M0 scale byte per row and group of 32 along K.
+enum class WFormat : int { W4G32 = 0, W8PC = 1, BF16 = 2, MXFP8 = 3, MXFP4 = 4 };
 enum class Epilogue : int { None = 0, Residual = 1, SwiGLU = 2 };
 
 // One weight matrix applied to the shared activation x[M, K].

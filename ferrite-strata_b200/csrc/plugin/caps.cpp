@@ -36,6 +36,8 @@ const PatternRule kRules[] = {
     // The decoder-block patterns this backend fuses.
     {"fused::linear_w4g32", true, false, true, false, false, false},
     {"fused::linear_w8pc", true, false, true, false, false, false},
+    {"fused::linear_mxfp8", true, false, true, false, false, false},
+    {"fused::linear_mxfp4", true, false, true, false, false, false},
     {"fused::rms_norm", true, true, true, false, false, false},
     {"fused::rope", true, true, true, false, false, false},
     {"fused::swiglu", true, true, true, false, false, false},
@@ -73,6 +75,9 @@ uint32_t mask_bit(uint32_t abi_elem) {
     case STRATA_ELEM_I8: return 1u << 8;
     case STRATA_ELEM_I32: return 1u << 10;
     case STRATA_ELEM_U8: return 1u << 12;
+    case STRATA_ELEM_F8E4M3: return 1u << 1;
+    case STRATA_ELEM_F8E8M0: return 1u << 6;
+    case STRATA_ELEM_F4E2M1: return 1u << 7;
   }
   return 0;
 }
@@ -158,8 +163,11 @@ std::vector<uint8_t> build_caps(const Ctx& ctx) {
   w.u32(uint32_t(kMaxRank));                                   // max_rank
   w.u64(~uint64_t(0));                                         // max_dim
   w.u64(~uint64_t(0));                                         // max_nodes
+  // Tensors of these element types can reach a compiled graph (the MX
+  // formats as linear weights and scales).
   w.u32(mask_bit(F32) | mask_bit(BF16) | mask_bit(STRATA_ELEM_I8) | mask_bit(STRATA_ELEM_I32) |
-        mask_bit(STRATA_ELEM_U8));
+        mask_bit(STRATA_ELEM_U8) | mask_bit(STRATA_ELEM_F8E4M3) | mask_bit(STRATA_ELEM_F8E8M0) |
+        mask_bit(STRATA_ELEM_F4E2M1));
   w.u8(1);  // accepts_unpartitioned
   return std::move(w.data());
 }

@@ -103,12 +103,22 @@ struct Lowerer {
 
   bool is_linear(const Node& n) const {
     return n.op == STRATA_OP_CUSTOM &&
-           (n.pattern == "fused::linear_w4g32" || n.pattern == "fused::linear_w8pc");
+           (n.pattern == "fused::linear_w4g32" || n.pattern == "fused::linear_w8pc" ||
+            n.pattern == "fused::linear_mxfp8" || n.pattern == "fused::linear_mxfp4");
+  }
+
+  static sb::WFormat linear_format(const std::string& pattern) {
+    if (pattern == "fused::linear_w4g32") return sb::WFormat::W4G32;
+    if (pattern == "fused::linear_mxfp8") return sb::WFormat::MXFP8;
+    if (pattern == "fused::linear_mxfp4") return sb::WFormat::MXFP4;
+    return sb::WFormat::W8PC;
   }
 
   bool linear_shapes(const Node& n, int64_t& M, int64_t& K, int64_t& N, std::string* why) const {
     const uint32_t x = n.inputs[0], w = n.inputs[1], s = n.inputs[2], y = n.outputs[0];
-    const bool w4 = n.pattern == "fused::linear_w4g32";
+    const sb::WFormat fmt = linear_format(n.pattern);
+    const bool w4 = fmt == sb::WFormat::W4G32;
+    const bool mx = fmt == sb::WFormat::MXFP8 || fmt == sb::WFormat::MXFP4;
     if (!is_bf16(V(x).dt) || !is_bf16(V(y).dt)) {
       *why = "quantised linears take and return bf16";
       return false;
@@ -120,7 +130,24 @@ struct Lowerer {
       *why = "linear output rows do not match input rows";
       return false;
     }
-    if (w4) {
+    if (mx) {
+      // MX (dtype.rs DType::microscaled): E4M3 codes [N, K], or E2M1 codes
+      // [N, K] (stored two per byte); E8M0 scales [N, K/32].  The decode
+      // GEMV copies the scales 4 groups at a time: K % 128 == 0.
+      const uint32_t want = fmt == sb::WFormat::MXFP8 ? STRATA_ELEM_F8E4M3 : STRATA_ELEM_F4E2M1;
+      if (V(w).dt.elem != want || V(w).dims != std::vector<int64_t>{N, K} || K % 128) {
+        *why = "MX weights must be f8e4m3 (mxfp8) or f4e2m1 (mxfp4) codes of shape [N, K] with K % 128 == 0";
+        return false;
+      }
+      if (V(s).dt.elem != STRATA_ELEM_F8E8M0 || V(s).dims != std::vector<int64_t>{N, K / 32}) {
+        *why = "MX scales must be f8e8m0 [N, K/32]";
+        return false;
+      }
+      if (N % 16) {
+        *why = "MX linears need output features in multiples of 16";
+        return false;
+      }
+    } else if (w4) {
       if (!is_w4(V(w).dt) || V(w).dims != std::vector<int64_t>{N, K / 2} || K % 32) {
         *why = "int4 weights must be U8 Block{32, symmetric} of shape [N, K/2] with K % 32 == 0";
         return false;
@@ -162,7 +189,7 @@ struct Lowerer {
     Step st;
     st.kind = SK::Linear;
     st.bf16 = true;
-    st.fmt = n.pattern == "fused::linear_w4g32" ? sb::WFormat::W4G32 : sb::WFormat::W8PC;
+    st.fmt = linear_format(n.pattern);
     st.i[0] = M;
     st.i[1] = K;
     st.v.push_back(n.inputs[0]);
@@ -249,7 +276,7 @@ struct Lowerer {
     for (size_t si = 0; si < exe.steps.size(); ++si) {
       Step& L = exe.steps[si];
       if (L.kind != SK::Linear || L.njobs != 3 || L.epi != sb::Epilogue::None ||
-          (L.fmt != sb::WFormat::W4G32 && L.fmt != sb::WFormat::W8PC) || L.i[0] > sb::kGemvMaxRows)
+          L.fmt == sb::WFormat::BF16 || L.i[0] > sb::kGemvMaxRows)
         continue;  // prefill-sized batches keep separate GEMM, rope and append steps
       const uint32_t yq = L.v[3], yk = L.v[7], yv = L.v[11];
       if (cons[yq].size() != 1 || cons[yk].size() != 1 || cons[yv].size() != 1) continue;
@@ -646,7 +673,7 @@ struct Lowerer {
   bool lower_custom(int ni) {
     const Node& n = g.nodes[ni];
     const std::string& p = n.pattern;
-    if (p == "fused::linear_w4g32" || p == "fused::linear_w8pc") return lower_linear(ni);
+    if (is_linear(n)) return lower_linear(ni);
     const uint32_t out = n.outputs.empty() ? kNone : n.outputs[0];
     Step st;
     st.label = n.name;
@@ -1087,7 +1114,7 @@ int enqueue_gemm(Ctx& ctx, Exe& exe, const Step& st, const sb::LinearBatch& b, c
   uint64_t wmax = 0;
   for (int j = 0; j < b.njobs; ++j) wmax = std::max<uint64_t>(wmax, uint64_t(b.jobs[j].n) * uint64_t(b.k) * 2);
   const uint64_t wslot = (wmax + 255) / 256 * 256;
-  const int fmt = b.fmt == sb::WFormat::W8PC ? 1 : 0;
+  const int fmt = b.fmt == sb::WFormat::W8PC ? 1 : b.fmt == sb::WFormat::MXFP8 ? 2 : b.fmt == sb::WFormat::MXFP4 ? 3 : 0;
   auto scale_of = [&](const sb::LinearJob& J) {
     return b.fmt == sb::WFormat::W8PC ? static_cast<const float*>(J.s) : nullptr;
   };

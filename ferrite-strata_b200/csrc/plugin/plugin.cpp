@@ -16,6 +16,7 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -321,7 +322,13 @@ static std::unique_ptr<StrataExecutable> compile_graph_section(const uint8_t* se
   holder->exe.g = decode_graph(sec, sec_len);
   holder->exe.label = "b200::" + holder->exe.g.name;
   std::string reason;
-  if (!lower(holder->exe.g, holder->exe, &reason)) return nullptr;
+  if (!lower(holder->exe.g, holder->exe, &reason)) {
+    // DECLINED carries no error object (status.rs); STRATA_B200_EXPLAIN=1
+    // prints the reason for whoever is wiring a graph up.
+    if (env_int("STRATA_B200_EXPLAIN", 0))
+      std::fprintf(stderr, "strata_b200: declined `%s`: %s\n", holder->exe.g.name.c_str(), reason.c_str());
+    return nullptr;
+  }
   return holder;
 }
 
@@ -521,7 +528,7 @@ static int32_t sb_alloc(void* ctx, const StrataAllocDesc* d, StrataBuffer** out,
         fail(STRATA_RESOURCE_EXHAUSTED, "allocation size overflows");
       n *= d->dims[i];
     }
-    const uint64_t bytes = n * dt.elem_bytes();
+    const uint64_t bytes = dt.byte_len(n);
     std::lock_guard<std::mutex> lk(c->mu);
     c->ensure_device();
     auto buf = std::make_unique<StrataBuffer>();

@@ -69,6 +69,10 @@ struct DType {
     return elem == o.elem && qkind == o.qkind && block == o.block && sym == o.sym;
   }
   size_t elem_bytes() const;
+  // Bytes of n elements as stored here: f4e2m1 codes are packed two per byte
+  // (the reference's ElementType::size_in_bytes reports 2 per element,
+  // dtype.rs; its larger buffers are accepted).
+  uint64_t byte_len(uint64_t n) const { return elem == 13 ? (n + 1) / 2 : n * elem_bytes(); }
   bool is_int() const;
 };
 
@@ -83,7 +87,7 @@ struct Value {
     for (auto d : dims) n *= d;
     return n;
   }
-  uint64_t bytes() const { return uint64_t(elements()) * dt.elem_bytes(); }
+  uint64_t bytes() const { return dt.byte_len(uint64_t(elements())); }
 };
 
 struct Attr {

@@ -11,6 +11,10 @@ pattern                     inputs                                     attribute
 fused::linear_w4g32         x bf16 [M,K], codes U8{32} [N,K/2],        bits=4, group_size=32
                             scales bf16 [N,K/32]
 fused::linear_w8pc          x bf16 [M,K], codes I8{K} [N,K], f32 [N]   bits=8
+fused::linear_mxfp8         x bf16 [M,K], codes f8e4m3 [N,K],          block_size=32
+                            scales f8e8m0:mx32 [N,K/32]
+fused::linear_mxfp4         x bf16 [M,K], codes f4e2m1:mx32 [N,K]      block_size=32
+                            (two per byte), scales f8e8m0:mx32
 fused::rms_norm             x [R,C], gamma [C]                         eps
 fused::rope                 x [R,H*d], pos I32 [R]                     head_dim, theta
 fused::swiglu               gate, up (same shape)
@@ -39,7 +43,11 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 
-from .ir import BF16, F32, I32, W4G32, DType, GraphBuilder, Op, w8pc
+from .ir import BF16, E2M1, E4M3, E8M0, F32, I32, W4G32, DType, GraphBuilder, Op, w8pc
+
+# MX weight formats: element dtype of the codes (the scales are E8M0, one per
+# 32 codes along K).
+MX_CODES = {"mxfp8": E4M3, "mxfp4": E2M1}
 
 
 @dataclass(frozen=True)
@@ -132,6 +140,9 @@ def weight_shapes(shape: DecoderShape, fmt: str, tp_world: int = 1, tp_rank: int
         elif fmt == "w8pc":
             out["w" + key] = (w8pc(k), (n, k))
             out["s" + key] = (F32, (n,))
+        elif fmt in MX_CODES:
+            out["w" + key] = (MX_CODES[fmt], (n, k))
+            out["s" + key] = (E8M0, (n, k // 32))
         elif fmt in ("f32", "bf16"):
             out["w" + key] = (act, (n, k))
         else:
@@ -147,6 +158,9 @@ def _linear(b: GraphBuilder, x: int, W: dict, key: str, m: int, n: int, fmt: str
     if fmt == "w8pc":
         return b.node(Op.custom("fused::linear_w8pc"), [x, W["w" + key], W["s" + key]],
                       [(BF16, (m, n))], {"bits": 8}, name)[0]
+    if fmt in MX_CODES:
+        return b.node(Op.custom(f"fused::linear_{fmt}"), [x, W["w" + key], W["s" + key]],
+                      [(BF16, (m, n))], {"block_size": 32}, name)[0]
     return b.node(Op("linear", weight=W["w" + key]), [x], [(act, (m, n))], {}, name)[0]
 
 
@@ -211,6 +225,9 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
         elif lmf == "w8pc":
             hd.lm_w = b.input(w8pc(D), (Vr, D), "lm_head.w")
             hd.lm_s = b.input(F32, (Vr,), "lm_head.s")
+        elif lmf in MX_CODES:
+            hd.lm_w = b.input(MX_CODES[lmf], (Vr, D), "lm_head.w")
+            hd.lm_s = b.input(E8M0, (Vr, D // 32), "lm_head.s")
         else:
             hd.lm_w = b.input(act, (Vr, D), "lm_head.w")
 

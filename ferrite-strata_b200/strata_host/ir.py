@@ -42,9 +42,28 @@ class DType:
             raise ValueError("a quantisation spec on a non-integer element type is a contradiction")
         return DType(e, QUANT_BLOCK, block_size, int(symmetric))
 
+    @staticmethod
+    def microscaled(name: str, block_size: int = 32) -> "DType":
+        """f8e8m0 or f4e2m1 sharing one E8M0 exponent per block of 32
+        (DType::microscaled, dtype.rs)."""
+        e = ELEM[name]
+        if e not in (ELEM["f8e8m0"], ELEM["f4e2m1"]) or block_size != 32:
+            raise ValueError("only f8e8m0 / f4e2m1 with a block of 32 are microscaled")
+        return DType(e, QUANT_MX, block_size, 0)
+
     @property
     def nbytes(self) -> int:
+        """Bytes per element as the reference sizes them (f4e2m1: 2)."""
         return ELEM_BYTES[self.element]
+
+    def byte_len(self, elements: int) -> int:
+        """Bytes a tensor of `elements` values occupies here: f4e2m1 codes
+        are packed two per byte (even index in the low nibble), where the
+        reference's ElementType::size_in_bytes reports 2 bytes per element;
+        a buffer of the reference's size is accepted (it is larger)."""
+        if self.element == ELEM["f4e2m1"]:
+            return (elements + 1) // 2
+        return elements * ELEM_BYTES[self.element]
 
     def to_raw(self) -> abi.StrataDType:
         d = abi.StrataDType()
@@ -59,6 +78,9 @@ F32 = DType.plain("f32")
 BF16 = DType.plain("bf16")
 I32 = DType.quantised("i32", 1)          # token ids and positions
 W4G32 = DType.quantised("u8", 32)        # packed int4 codes, group 32 along k
+E4M3 = DType.plain("f8e4m3")             # MXFP8 weight codes
+E2M1 = DType.microscaled("f4e2m1")       # MXFP4 weight codes, two per byte
+E8M0 = DType.microscaled("f8e8m0")       # MX block scales, one per 32 codes along k
 
 
 def w8pc(k: int) -> DType:
@@ -142,7 +164,7 @@ class Value:
 
     @property
     def nbytes(self) -> int:
-        return self.elements * self.dtype.nbytes
+        return self.dtype.byte_len(self.elements)
 
 
 @dataclass

@@ -306,10 +306,10 @@ class Plugin:
         rc = self.vt.alloc(self.ctx, C.byref(desc), C.byref(out), C.byref(err))
         if rc != abi.OK or not out.value:
             raise self.take_error(err.value, rc if rc != abi.OK else abi.INTERNAL)
-        n = dtype.nbytes
+        n = 1
         for d in dims:
             n *= d
-        return Buffer(self, out.value, n)
+        return Buffer(self, out.value, dtype.byte_len(n))
 
     def upload(self, dtype: DType, dims, data: HostData) -> Buffer:
         buf = self.alloc(dtype, dims)

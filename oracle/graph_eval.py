@@ -18,7 +18,7 @@ import numpy as np
 
 from . import oracle as ora
 
-F32_E, BF16_E, I32_E = 4, 14, 8
+F32_E, BF16_E, I32_E, F4E2M1_E = 4, 14, 8, 13
 
 
 def _is_bf16(dt) -> bool:
@@ -51,7 +51,10 @@ def evaluate(graph, inputs: dict, all_reduce=None, all_gather=None) -> dict:
     vals: dict[int, np.ndarray] = {}
     for i, v in enumerate(graph.values):
         if v.producer is None and i in inputs:
-            vals[i] = _norm_in(v, inputs[i]).reshape(v.dims)
+            dims = tuple(v.dims)
+            if v.dtype.element == F4E2M1_E:  # codes packed two per byte along the last axis
+                dims = dims[:-1] + ((dims[-1] + 1) // 2,)
+            vals[i] = _norm_in(v, inputs[i]).reshape(dims)
 
     def out_dt(n, i=0):
         return graph.values[n.outputs[i]].dtype
@@ -90,6 +93,9 @@ def evaluate(graph, inputs: dict, all_reduce=None, all_gather=None) -> dict:
         elif pid == "fused::linear_w4g32":
             x = ins[0].reshape(-1, ins[0].shape[-1])
             res = ora.linear_w4g32(x, ins[1], ora.to_bf16(ins[2]), threads=_threads())
+        elif pid in ("fused::linear_mxfp8", "fused::linear_mxfp4"):
+            x = ins[0].reshape(-1, ins[0].shape[-1])
+            res = ora.linear_mx(x, ins[1], ins[2], pid.rsplit("_", 1)[1], threads=_threads())
         elif pid == "fused::linear_w8pc":
             x = ins[0].reshape(-1, ins[0].shape[-1])
             res = ora.linear_w8pc(x, ins[1], ins[2], threads=_threads())

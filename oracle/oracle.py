@@ -53,6 +53,13 @@ def lib():
             "ora_slice_cols": (i64, [P, i64, i64, i64, i64, i64, P]),
             "ora_quant_w8pc": (None, [P, i64, i64, P, P]),
             "ora_quant_w4g32": (None, [P, i64, i64, P, P]),
+            "ora_quant_mx": (None, [P, i64, i64, C.c_int, P, P]),
+            "ora_dequant_mx": (None, [P, P, i64, i64, C.c_int, P]),
+            "ora_linear_mx_mt": (None, [P, P, P, C.c_int, i64, i64, i64, P, C.c_int]),
+            "ora_e4m3_to_f32": (C.c_float, [C.c_uint8]),
+            "ora_e2m1_to_f32": (C.c_float, [C.c_uint8]),
+            "ora_f32_to_e4m3": (C.c_uint8, [C.c_float]),
+            "ora_f32_to_e2m1": (C.c_uint8, [C.c_float]),
             "ora_dequant_w8pc": (None, [P, P, i64, i64, P]),
             "ora_dequant_w4g32": (None, [P, P, i64, i64, P]),
             "ora_rms_norm": (None, [P, P, i64, i64, f32, P]),
@@ -243,6 +250,43 @@ def dequant_w4g32(packed, s):
     n, k = packed.shape[0], packed.shape[1] * 2
     out = np.empty((n, k), dtype=np.float32)
     lib().ora_dequant_w4g32(_p(packed), _p(s), n, k, _p(out))
+    return out
+
+
+MX_FORMATS = {"mxfp8": 0, "mxfp4": 1}
+
+
+def quant_mx(w, fmt: str):
+    """MX quantisation (block 32 along k): E4M3 codes [n, k] (mxfp8) or E2M1
+    codes packed two per byte [n, k/2] (mxfp4), and E8M0 scales [n, k/32]."""
+    w = _f32(w)
+    n, k = w.shape
+    f = MX_FORMATS[fmt]
+    codes = np.zeros((n, k if f == 0 else k // 2), dtype=np.uint8)
+    s = np.empty((n, k // 32), dtype=np.uint8)
+    lib().ora_quant_mx(_p(w), n, k, f, _p(codes), _p(s))
+    return codes, s
+
+
+def dequant_mx(codes, s, fmt: str):
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    s = np.ascontiguousarray(s, dtype=np.uint8)
+    f = MX_FORMATS[fmt]
+    n = codes.shape[0]
+    k = codes.shape[1] * (1 if f == 0 else 2)
+    out = np.empty((n, k), dtype=np.float32)
+    lib().ora_dequant_mx(_p(codes), _p(s), n, k, f, _p(out))
+    return out
+
+
+def linear_mx(x, codes, s, fmt: str, threads: int = 1):
+    x = _f32(x)
+    codes = np.ascontiguousarray(codes, dtype=np.uint8)
+    s = np.ascontiguousarray(s, dtype=np.uint8)
+    m, k = x.shape
+    n = codes.shape[0]
+    out = np.empty((m, n), dtype=np.float32)
+    lib().ora_linear_mx_mt(_p(x), _p(codes), _p(s), MX_FORMATS[fmt], m, k, n, _p(out), max(1, threads))
     return out
 
 

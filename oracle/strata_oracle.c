@@ -451,6 +451,142 @@ void ora_argmax(const float *x, int64_t rows, int64_t cols, int32_t *out) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* MX weights (OCP Microscaling Formats v1.0, restated; the reference names  */
+/* the element types in dtype.rs:41-85 but computes none of them).           */
+/* A block of 32 codes along k shares one E8M0 scale 2^(e - 127) (code 255  */
+/* is NaN).  FP8 E4M3: sign, 4-bit exponent (bias 7), 3-bit mantissa,       */
+/* largest 448, 0x7f / 0xff NaN.  FP4 E2M1: sign, 2-bit exponent (bias 1),  */
+/* 1-bit mantissa: 0, 0.5, 1, 1.5, 2, 3, 4, 6; packed two per byte with the */
+/* even k in the low nibble.  The block scale is 2^(floor(log2(amax)) -     */
+/* emax), emax = 8 (E4M3) or 2 (E2M1), an all-zero block taking code 0;    */
+/* each value divided by it rounds to nearest even, saturating at the       */
+/* format's largest magnitude.  Dequantisation, code * 2^(e - 127), is      */
+/* exact in f32 and in bf16.                                                */
+/* ------------------------------------------------------------------------ */
+
+float ora_e4m3_to_f32(uint8_t c) {
+  const int e = (c >> 3) & 15, m = c & 7;
+  float v;
+  if ((c & 0x7f) == 0x7f) return NAN;
+  if (e == 0)
+    v = ldexpf((float)m, -9);
+  else
+    v = ldexpf(1.0f + (float)m / 8.0f, e - 7);
+  return (c & 0x80) ? -v : v;
+}
+
+float ora_e2m1_to_f32(uint8_t c) {
+  static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+  const float v = mag[c & 7];
+  return (c & 8) ? -v : v;
+}
+
+uint8_t ora_f32_to_e4m3(float x) {
+  if (isnan(x)) return 0x7f;
+  const uint8_t sign = signbit(x) ? 0x80 : 0;
+  const float a = fabsf(x);
+  if (a >= 448.0f) return sign | 0x7e;
+  if (a < ldexpf(1.0f, -6)) {  /* subnormal range: steps of 2^-9 */
+    const int m = (int)rintf(ldexpf(a, 9));
+    return sign | (uint8_t)m;  /* m == 8 is the smallest normal, code 0x08 */
+  }
+  int e;
+  frexpf(a, &e); /* a = f * 2^e, f in [0.5, 1) */
+  e -= 1;        /* a in [2^e, 2^(e+1)) */
+  int m = (int)rintf((ldexpf(a, -e) - 1.0f) * 8.0f);
+  if (m == 8) {
+    m = 0;
+    e += 1;
+  }
+  if (e + 7 > 15 || (e + 7 == 15 && m == 7)) return sign | 0x7e;
+  return sign | (uint8_t)(((e + 7) << 3) | m);
+}
+
+uint8_t ora_f32_to_e2m1(float x) {
+  const uint8_t sign = signbit(x) ? 8 : 0;
+  const float a = fabsf(x);
+  uint8_t idx;
+  /* nearest of 0, .5, 1, 1.5, 2, 3, 4, 6; a tie goes to the even mantissa */
+  if (isnan(x)) idx = 0;
+  else if (a <= 0.25f) idx = 0;
+  else if (a < 0.75f) idx = 1;
+  else if (a <= 1.25f) idx = 2;
+  else if (a < 1.75f) idx = 3;
+  else if (a <= 2.5f) idx = 4;
+  else if (a < 3.5f) idx = 5;
+  else if (a <= 5.0f) idx = 6;
+  else idx = 7;
+  return sign | idx;
+}
+
+/* The E8M0 scale code of a block whose largest magnitude is amax. */
+static uint8_t mx_scale_code(float amax, int emax) {
+  if (!(amax > 0.0f)) return 0;
+  int e;
+  frexpf(amax, &e);
+  int x = (e - 1) - emax + 127;
+  if (x < 0) x = 0;
+  if (x > 254) x = 254;
+  return (uint8_t)x;
+}
+
+static float e8m0_to_f32(uint8_t s) { return s == 255 ? NAN : ldexpf(1.0f, (int)s - 127); }
+
+/* fmt 0: E4M3 codes [n, k]; fmt 1: E2M1 codes packed [n, k/2].  Scales
+   [n, k/32]. */
+void ora_quant_mx(const float *w, int64_t n, int64_t k, int fmt, uint8_t *codes, uint8_t *scales) {
+  const int64_t blocks = k / 32;
+  for (int64_t r = 0; r < n; ++r)
+    for (int64_t b = 0; b < blocks; ++b) {
+      const float *src = w + r * k + b * 32;
+      float amax = 0.0f;
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(src[i]));
+      const uint8_t sc = mx_scale_code(amax, fmt == 0 ? 8 : 2);
+      scales[r * blocks + b] = sc;
+      const int shift = 127 - (int)sc; /* divide by 2^(sc - 127) exactly */
+      for (int i = 0; i < 32; ++i) {
+        const float q = ldexpf(src[i], shift);
+        if (fmt == 0) {
+          codes[r * k + b * 32 + i] = ora_f32_to_e4m3(q);
+        } else {
+          const uint8_t c = ora_f32_to_e2m1(q);
+          uint8_t *dst = codes + r * (k / 2) + b * 16 + i / 2;
+          *dst = (i & 1) ? (uint8_t)((*dst & 0x0f) | (c << 4)) : (uint8_t)((*dst & 0xf0) | c);
+        }
+      }
+    }
+}
+
+static inline float mx_code(const uint8_t *codes, int64_t k, int fmt, int64_t r, int64_t c) {
+  if (fmt == 0) return ora_e4m3_to_f32(codes[r * k + c]);
+  const uint8_t b = codes[r * (k / 2) + c / 2];
+  return ora_e2m1_to_f32((c & 1) ? (b >> 4) : (b & 15));
+}
+
+void ora_dequant_mx(const uint8_t *codes, const uint8_t *scales, int64_t n, int64_t k, int fmt, float *w) {
+  for (int64_t r = 0; r < n; ++r)
+    for (int64_t c = 0; c < k; ++c)
+      w[r * k + c] = mx_code(codes, k, fmt, r, c) * e8m0_to_f32(scales[r * (k / 32) + c / 32]);
+}
+
+/* y = x . dequant(W)^T, each weight dequantised exactly and accumulated in
+   k order in f32, as the int4 linear above. */
+static void linear_mx_row(const float *xr, const uint8_t *codes, const uint8_t *scales, int64_t k, int fmt,
+                          int64_t c, float *out) {
+  float acc = 0.0f;
+  for (int64_t i = 0; i < k; ++i)
+    acc += xr[i] * (mx_code(codes, k, fmt, c, i) * e8m0_to_f32(scales[c * (k / 32) + i / 32]));
+  *out = acc;
+}
+
+void ora_linear_mx_mt(const float *x, const uint8_t *codes, const uint8_t *scales, int fmt, int64_t m, int64_t k,
+                      int64_t n, float *out, int threads) {
+#pragma omp parallel for collapse(2) schedule(static) num_threads(threads)
+  for (int64_t r = 0; r < m; ++r)
+    for (int64_t c = 0; c < n; ++c) linear_mx_row(x + r * k, codes, scales, k, fmt, c, out + r * n + c);
+}
+
+/* ------------------------------------------------------------------------ */
 /* Deterministic inputs: splitmix64 + Box-Muller                            */
 /* ------------------------------------------------------------------------ */
 

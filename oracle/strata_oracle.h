@@ -128,6 +128,17 @@ int ora_embed(const int32_t *ids, int64_t rows, const float *table,
 /* Argmax per row; the lowest index wins ties; NaN never wins. */
 void ora_argmax(const float *x, int64_t rows, int64_t cols, int32_t *out);
 
+/* ---- MX weights (OCP Microscaling v1.0; block 32 along k, E8M0 scales) -- */
+float ora_e4m3_to_f32(uint8_t c);
+float ora_e2m1_to_f32(uint8_t c);
+uint8_t ora_f32_to_e4m3(float x); /* nearest even, saturating at 448 */
+uint8_t ora_f32_to_e2m1(float x); /* nearest even, saturating at 6 */
+/* fmt 0: E4M3 codes [n, k]; fmt 1: E2M1 codes packed [n, k/2] (even k low) */
+void ora_quant_mx(const float *w, int64_t n, int64_t k, int fmt, uint8_t *codes, uint8_t *scales);
+void ora_dequant_mx(const uint8_t *codes, const uint8_t *scales, int64_t n, int64_t k, int fmt, float *w);
+void ora_linear_mx_mt(const float *x, const uint8_t *codes, const uint8_t *scales, int fmt, int64_t m, int64_t k,
+                      int64_t n, float *out, int threads);
+
 /* ---- deterministic inputs ------------------------------------------------ */
 /* splitmix64 stream feeding Box-Muller in double; returns N(mean, std) as f32
  * (rounded from double).  Shared by tests and bench so GPU and CPU inputs are

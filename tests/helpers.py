@@ -63,6 +63,12 @@ def seeded_graph_inputs(graph, seed_base: int = 1, weight_std: float = 0.02,
             packed, s = ora.quant_w4g32(w)
             vals[i] = packed
             vals[i + 1] = s  # the scale input is declared right after its codes
+        elif v.dtype.element in (ELEM["f8e4m3"], ELEM["f4e2m1"]):  # MX codes, then their E8M0 scales
+            n, k = v.dims
+            w = ora.normal(seed, (n, k), std=weight_std)
+            codes, s = ora.quant_mx(w, "mxfp8" if v.dtype.element == ELEM["f8e4m3"] else "mxfp4")
+            vals[i] = codes
+            vals[i + 1] = s
         elif v.dtype.element == ELEM["i8"]:
             n, k = v.dims
             w = ora.normal(seed, (n, k), std=weight_std)

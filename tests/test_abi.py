@@ -67,8 +67,12 @@ def test_capability_blob(plugin):
                 "fused::swiglu", "fused::attention", "fused::embed", "fused::all_reduce"):
         assert levels[(pid, 14)] == abi.SUPPORT_FUSED
     assert levels[("ref::linear", 4)] == abi.SUPPORT_FALLBACK
-    # dtype mask bits are ElementType::all() positions: f32, bf16, i8, i32, u8
-    assert caps.dtype_mask == (1 << 3) | (1 << 5) | (1 << 8) | (1 << 10) | (1 << 12)
+    # dtype mask bits are ElementType::all() positions: f32, bf16, i8, i32, u8, and the MX
+    # formats f8e4m3, f8e8m0, f4e2m1
+    assert caps.dtype_mask == ((1 << 3) | (1 << 5) | (1 << 8) | (1 << 10) | (1 << 12) |
+                               (1 << 1) | (1 << 6) | (1 << 7))
+    for pid in ("fused::linear_mxfp8", "fused::linear_mxfp4"):
+        assert levels[(pid, 14)] == abi.SUPPORT_FUSED
 
 
 ALL_CLASSES = [(), (0, 4), (1, 4096), (64,), (8, 4096), (2, 3, 4), (2, 3, 4, 5), (2,) * 5, (2,) * 8]
