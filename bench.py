@@ -545,15 +545,17 @@ SWEEP_METRIC = "quantized Linear sweep, K = N = 4096 (us per launch, % of roofli
 
 
 def run_sweep(args):
-    """Config 2: one quantized Linear node per case, int4 g32 and int8 per-channel weights,
-    K = N = 4096, M in {1, 16, 128, 2048}, through the C-ABI entry points
-    (strata_b200_linear_w4g32 / _w8pc: the tensor-core GEMV up to 64 rows, the tcgen05 GEMM
-    above).  Weight copies rotate so every launch streams its weights from HBM."""
+    """Config 2: one quantized Linear node per case, int4 g32 and int8 per-channel weights
+    (plus MXFP8 / MXFP4 weights with E8M0 block scales), K = N = 4096, M in {1, 16, 128, 2048},
+    through the C-ABI entry points (strata_b200_linear_w4g32 / _w8pc / _mxfp8 / _mxfp4: the
+    tensor-core GEMV up to 64 rows, the tcgen05 GEMM above).  Weight copies rotate so every
+    launch streams its weights from HBM."""
     import torch
     torch.cuda.set_device(0)
     lib = C.CDLL(os.path.join(PKG, "libstrata_b200.so"))
     P, I64 = C.c_void_p, C.c_int64
-    for f in (lib.strata_b200_linear_w4g32, lib.strata_b200_linear_w8pc):
+    for f in (lib.strata_b200_linear_w4g32, lib.strata_b200_linear_w8pc, lib.strata_b200_linear_mxfp8,
+              lib.strata_b200_linear_mxfp4):
         f.argtypes = [P, I64, I64, P, P, I64, P, P, P]
         f.restype = C.c_int32
     bw, bw_kind = load_peaks()
@@ -566,13 +568,22 @@ def run_sweep(args):
     K = N = 4096
     stream = torch.cuda.current_stream()
     cases = []
-    for fmt in ("w4g32", "w8pc"):
-        wbytes = N * K // 2 + N * (K // 32) * 2 if fmt == "w4g32" else N * K + N * 4
+    for fmt in ("w4g32", "w8pc", "mxfp8", "mxfp4"):
+        wbytes = {"w4g32": N * K // 2 + N * (K // 32) * 2, "w8pc": N * K + N * 4,
+                  "mxfp8": N * K + N * (K // 32), "mxfp4": N * K // 2 + N * (K // 32)}[fmt]
         copies = max(2, (2 * l2) // wbytes + 1)
         if fmt == "w4g32":
             ws = [torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda") for _ in range(copies)]
             ss = [(torch.rand((N, K // 32), device="cuda") * 0.01).to(torch.bfloat16) for _ in range(copies)]
             fn = lib.strata_b200_linear_w4g32
+        elif fmt in ("mxfp8", "mxfp4"):  # random finite codes, E8M0 scales around 2^-7
+            cb = K if fmt == "mxfp8" else K // 2
+            ws = [torch.randint(0, 256, (N, cb), dtype=torch.uint8, device="cuda") for _ in range(copies)]
+            if fmt == "mxfp8":  # no NaN codes (0x7f / 0xff)
+                for w_ in ws:
+                    w_[(w_ & 0x7F) == 0x7F] = 0
+            ss = [torch.randint(110, 130, (N, K // 32), dtype=torch.uint8, device="cuda") for _ in range(copies)]
+            fn = lib.strata_b200_linear_mxfp8 if fmt == "mxfp8" else lib.strata_b200_linear_mxfp4
         else:
             ws = [torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda") for _ in range(copies)]
             ss = [torch.rand((N,), device="cuda") * 0.01 for _ in range(copies)]
@@ -634,7 +645,8 @@ def main():
                     help="time the int8 prefill configuration instead of decode")
     ap.add_argument("--seq", type=int, default=2048, help="tokens per prompt with --prefill")
     ap.add_argument("--sweep", action="store_true",
-                    help="time the quantized Linear sweep (K = N = 4096, M in {1, 16, 128, 2048}, int4 and int8)")
+                    help="time the quantized Linear sweep (K = N = 4096, M in {1, 16, 128, 2048}, "
+                         "int4, int8, MXFP8, MXFP4)")
     ap.add_argument("--kv-page", type=int, default=0,
                     help="decode with a paged KV cache of this page size (block table, shuffled pages)")
     ap.add_argument("--profile-step", action="store_true",

@@ -67,7 +67,8 @@ static int32_t linear_common(WFormat fmt, const uint16_t* x, int64_t m, int64_t 
                                  st);
     void* tmp = nullptr;
     if (cudaMallocAsync(&tmp, size_t(n) * size_t(k) * 2, st) != cudaSuccess) return SB_RESOURCE_EXHAUSTED;
-    int rc = launch_codes_to_bf16(w, s, fmt == WFormat::W8PC ? 1 : 0, n, k, static_cast<uint16_t*>(tmp), st);
+    const int cf = fmt == WFormat::W8PC ? 1 : fmt == WFormat::MXFP8 ? 2 : fmt == WFormat::MXFP4 ? 3 : 0;
+    int rc = launch_codes_to_bf16(w, s, cf, n, k, static_cast<uint16_t*>(tmp), st);
     if (rc == SB_OK)
       rc = launch_gemm_tc_bf16(x, m, k, static_cast<const uint16_t*>(tmp), n,
                                fmt == WFormat::W8PC ? static_cast<const float*>(s) : nullptr, residual, n, y, n,
@@ -98,6 +99,18 @@ int32_t strata_b200_linear_w8pc(const uint16_t* x, int64_t m, int64_t k, const i
                                 const float* scale, int64_t n, const uint16_t* residual,
                                 uint16_t* y, void* stream) {
   return linear_common(WFormat::W8PC, x, m, k, q, scale, n, residual, y, stream);
+}
+
+int32_t strata_b200_linear_mxfp8(const uint16_t* x, int64_t m, int64_t k, const uint8_t* codes,
+                                 const uint8_t* scale_e8m0, int64_t n, const uint16_t* residual, uint16_t* y,
+                                 void* stream) {
+  return linear_common(WFormat::MXFP8, x, m, k, codes, scale_e8m0, n, residual, y, stream);
+}
+
+int32_t strata_b200_linear_mxfp4(const uint16_t* x, int64_t m, int64_t k, const uint8_t* codes,
+                                 const uint8_t* scale_e8m0, int64_t n, const uint16_t* residual, uint16_t* y,
+                                 void* stream) {
+  return linear_common(WFormat::MXFP4, x, m, k, codes, scale_e8m0, n, residual, y, stream);
 }
 
 int32_t strata_b200_rms_norm_bf16(const uint16_t* x, const uint16_t* gamma, int64_t rows,

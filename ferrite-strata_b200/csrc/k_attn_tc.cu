@@ -360,11 +360,15 @@ int launch_tc(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const i
 }  // namespace
 
 int attention_tc_span(int64_t rows, int64_t kv_heads, int64_t max_len) {
-  // About four CTAs per SM, at most one cluster's worth of splits, whole
-  // slabs of 64 positions per CTA.
+  // About one wave (two 104 KB CTAs per SM), at most one cluster's worth of
+  // splits, whole slabs of 64 positions per CTA.  Splitting further only
+  // adds cluster merges: at 2049 cached positions, 256 (row, kv head) pairs
+  // (7B batch 8; 70B batch 32 GQA) ran in 51 / 101 us with 2 splits against
+  // 54 / 112 us with 3 and 60 / 119 us with 4; 32 pairs (7B batch 1) kept
+  // improving up to 7-8 splits (26 -> 11 us).
   const int64_t pairs = rows * kv_heads;
   const int64_t most = (max_len + 63) / 64;
-  int64_t splits = (4 * kNumSMs + pairs - 1) / pairs;
+  int64_t splits = (2 * kNumSMs + pairs - 1) / pairs;
   if (splits > kMaxSplits) splits = kMaxSplits;
   if (splits > most) splits = most;
   if (splits < 1) splits = 1;

@@ -98,6 +98,23 @@ int32_t strata_b200_linear_w8pc(const uint16_t *x, int64_t m, int64_t k,
                                 int64_t n, const uint16_t *residual,
                                 uint16_t *y, void *stream);
 
+/* The same with MX weights (OCP Microscaling; the element types of
+ * crates/ferrite-strata/src/dtype.rs:41-85, DType::microscaled): codes E4M3
+ * [n, k] one byte each (mxfp8) or E2M1 [n, k] packed two per byte, even k in
+ * the low nibble (mxfp4); scales E8M0 [n, k/32], one byte each.  Weights are
+ * dequantised exactly (code * 2^(e - 127)).  k % 128 == 0 and n % 16 == 0 for
+ * m <= 64 (the tensor-core GEMV). */
+int32_t strata_b200_linear_mxfp8(const uint16_t *x, int64_t m, int64_t k,
+                                 const uint8_t *codes,
+                                 const uint8_t *scale_e8m0, int64_t n,
+                                 const uint16_t *residual, uint16_t *y,
+                                 void *stream);
+int32_t strata_b200_linear_mxfp4(const uint16_t *x, int64_t m, int64_t k,
+                                 const uint8_t *codes,
+                                 const uint8_t *scale_e8m0, int64_t n,
+                                 const uint16_t *residual, uint16_t *y,
+                                 void *stream);
+
 /* y[m, n] = sum_k x[m, k] * w[n, k]  (+ residual[m, n] when non-null) with
  * bf16 weights [n, k]: the reference's f32 `linear` (crates/ferrite-strata-cpu/
  * src/backend.rs:607-637) in bf16 storage with f32 accumulation.  k must be a

@@ -24,6 +24,8 @@ def lib(cuda):
         "strata_b200_dequant_w8pc": [P, P, I64, I64, P, P],
         "strata_b200_linear_w4g32": [P, I64, I64, P, P, I64, P, P, P],
         "strata_b200_linear_w8pc": [P, I64, I64, P, P, I64, P, P, P],
+        "strata_b200_linear_mxfp8": [P, I64, I64, P, P, I64, P, P, P],
+        "strata_b200_linear_mxfp4": [P, I64, I64, P, P, I64, P, P, P],
         "strata_b200_linear_bf16": [P, I64, I64, P, I64, P, P, P],
         "strata_b200_rms_norm_bf16": [P, P, I64, I64, F, P, P],
         "strata_b200_rope_bf16": [P, P, I64, I64, I64, F, P, P],
@@ -281,3 +283,24 @@ def test_embed_and_argmax_are_exact(cuda, lib):
     got = am.cpu().numpy()
     assert np.array_equal(got, ora.argmax(ora.from_bf16(logits)))
     assert got[0] == 5 and got[1] == 77
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "mxfp4"])
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (24, 256, 11008), (64, 48, 384), (200, 512, 1024)])
+def test_linear_mx_entry_points(cuda, lib, fmt, m, n, k):
+    """strata_b200_linear_mxfp8 / _mxfp4 with a residual: the GEMV (K-slices
+    of 11008 = 86 four-group blocks, partial chunks at K = 384) and, past 64
+    rows, the exact bf16 expansion and the tcgen05 GEMM."""
+    torch = cuda
+    x = _x_bf16(m, k, seed=6)
+    codes, s = ora.quant_mx(ora.normal(8, (n, k), std=0.02), fmt)
+    res = ora.to_bf16(ora.normal(9, (m, n)))
+    xd, cd, sd = dev(torch, x.view(np.int16)), dev(torch, codes), dev(torch, s)
+    rd = dev(torch, res.view(np.int16))
+    y = torch.empty((m, n), dtype=torch.int16, device="cuda")
+    fn = lib.strata_b200_linear_mxfp8 if fmt == "mxfp8" else lib.strata_b200_linear_mxfp4
+    ok(fn(ptr(xd), m, k, ptr(cd), ptr(sd), n, ptr(rd), ptr(y), stream(torch)))
+    torch.cuda.synchronize()
+    got = ora.from_bf16(y.cpu().numpy().view(np.uint16))
+    want = ora.linear_mx(ora.from_bf16(x), codes, s, fmt, threads=ora.max_threads()) + ora.from_bf16(res)
+    assert_close(got, want, TOL_BF16, f"{fmt} m={m} n={n} k={k}")
