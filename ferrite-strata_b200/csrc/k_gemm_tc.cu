@@ -8,13 +8,14 @@
 // launch_codes_to_bf16), so the per-channel scale is applied in f32 in the
 // epilogue and the product matches the oracle's code * scale.
 //
-// Persistent: one CTA per SM walks 128 x 256 tiles of y (tokens x features):
+// Persistent: one CTA per SM walks 128 x BN tiles of y (tokens x features; BN
+// 256 for prefill-sized launches, down to 32 for small ones, choose_bn):
 //   warp 0      one thread issues TMA loads of the x tile (128 x 64) and the
-//               w tile (256 x 64), 128-byte swizzled, into a 4-stage ring
-//               that runs continuously across the CTA's tiles;
-//   warp 1      allocates 512 TMEM columns (two f32 accumulators: TMEM lane =
+//               w tile (BN x 64), 128-byte swizzled, into a 4- to 8-stage
+//               ring that runs continuously across the CTA's tiles;
+//   warp 1      allocates 2 BN TMEM columns (two f32 accumulators: TMEM lane =
 //               token row, column = feature) and one thread issues
-//               tcgen05.mma (M 128, N 256, K 16; four per stage) and
+//               tcgen05.mma (M 128, N BN, K 16; four per stage) and
 //               tcgen05.commit to release each stage and each finished
 //               accumulator;
 //   warps 2-5   the epilogue: tcgen05.ld 32 columns at a time from their
@@ -35,15 +36,22 @@ namespace sb {
 
 namespace {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64, kGStages = 4;
+constexpr int kBM = 128, kBK = 64;
 constexpr int kGThreads = 192;
 constexpr int kABytes = kBM * kBK * 2;            // 16 KB
-constexpr int kBBytes = kBN * kBK * 2;            // 32 KB
-constexpr int kGStageBytes = kABytes + kBBytes;   // 48 KB
-constexpr int kGSmem = kGStages * kGStageBytes + 1024 + 256;  // ring + alignment + barriers
-constexpr uint32_t kTmemCols = 2 * kBN;        // two accumulators of 256 f32 columns
 
-constexpr uint32_t kIdesc = tc::idesc_bf16(kBM, kBN);
+// Tile width BN (256, 128, 64 or 32 weight rows): narrower tiles give small-M
+// launches enough tiles to fill the SMs, and use the shared memory they free
+// for a deeper ring.
+template <int BN>
+struct GL {
+  static constexpr int kBBytes = BN * kBK * 2;                                  // 32 KB at BN = 256
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = BN == 256 ? 4 : BN == 128 ? 6 : 8;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 + 256;             // ring + alignment + barriers
+  static constexpr uint32_t kTmemCols = 2 * BN;                                // two f32 accumulators
+  static constexpr uint32_t kIdesc = tc::idesc_bf16(kBM, BN);
+};
 
 struct GemmArgs {
   int m, n, k;               // n: output features (for SwiGLU: of the gate and of the up matrix)
@@ -58,17 +66,17 @@ struct GemmArgs {
 
 using namespace tc;
 
-// Epilogue of one tile for one token row: TMEM columns [col0, col0 + 256) of
+// Epilogue of one tile for one token row: TMEM columns [col0, col0 + BN) of
 // this warp's lane quarter.  EPI 0: y = scale * acc (+ residual); EPI 1: the
-// gate in columns 0..127 and the up in 128..255, each rounded to bf16 as the
-// graph's gate and up values are, then silu(gate) * up.
-template <int EPI>
+// gate in columns 0..BN/2-1 and the up in BN/2..BN-1, each rounded to bf16 as
+// the graph's gate and up values are, then silu(gate) * up.
+template <int EPI, int BN>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, uint32_t taddr, int row, int n0) {
   if constexpr (EPI == 1) {
-    for (int c = 0; c < kBN / 64; ++c) {
+    for (int c = 0; c < BN / 64; ++c) {
       uint32_t gr[32], ur[32];
       tmem_ld32(taddr + uint32_t(c * 32), gr);
-      tmem_ld32(taddr + uint32_t(kBN / 2 + c * 32), ur);
+      tmem_ld32(taddr + uint32_t(BN / 2 + c * 32), ur);
       const int nb = n0 + c * 32;
       if (row >= p.m || nb >= p.n) continue;
       uint16_t* yr = p.y + int64_t(row) * p.ldy + nb;
@@ -97,7 +105,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, uint32_t taddr,
       }
     }
   } else {
-    for (int c = 0; c < kBN / 32; ++c) {
+    for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
       tmem_ld32(taddr + uint32_t(c * 32), r);
       const int nb = n0 + c * 32;
@@ -141,16 +149,19 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& p, uint32_t taddr,
 
 // Persistent: CTA b computes tiles b, b + grid, ... (features fastest, so a
 // wave of CTAs shares its x rows and walks all of W).  Two TMEM accumulators
-// of 256 columns alternate between tiles: the epilogue warps drain tile i
+// of BN columns alternate between tiles: the epilogue warps drain tile i
 // while the MMA thread fills the other accumulator with tile i + 1.
 //
 // EPI 0: y = scale * (x W^T) (+ residual).  EPI 1 (SwiGLU): the B tile is
-// 128 rows of the gate matrix over 128 rows of the up matrix for the same
-// output features, and y = silu(gate) * up for those 128 features.
-template <int EPI>
+// BN/2 rows of the gate matrix over BN/2 rows of the up matrix for the same
+// output features, and y = silu(gate) * up for those BN/2 features.
+template <int EPI, int BN>
 __global__ void __launch_bounds__(kGThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_w2, const GemmArgs p) {
+  using L = GL<BN>;
+  constexpr int kGStages = L::kStages, kGStageBytes = L::kStageBytes, kBBytes = L::kBBytes;
+  constexpr uint32_t kTmemCols = L::kTmemCols, kIdesc = L::kIdesc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kGStages * kGStageBytes);
@@ -161,7 +172,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
   __shared__ int s_fail;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kOutCols = EPI == 1 ? kBN / 2 : kBN;  // output features per tile
+  constexpr int kOutCols = EPI == 1 ? BN / 2 : BN;  // output features per tile
   const int tiles_n = (p.n + kOutCols - 1) / kOutCols;
   const int tiles = tiles_n * ((p.m + kBM - 1) / kBM);
   const int nk = (p.k + kBK - 1) / kBK;
@@ -233,7 +244,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
           break;
         }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t acc = tmem + uint32_t(b * kBN);
+        const uint32_t acc = tmem + uint32_t(b * BN);
         for (int kb = 0; kb < nk; ++kb, ++c) {
           const int s = int(c % kGStages);
           if (!mbar_wait(&full[s], (c / kGStages) & 1)) {
@@ -264,8 +275,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kOutCols;
-      gemm_epilogue<EPI>(p, tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * kBN), m0 + quarter * 32 + lane,
-                         n0);
+      gemm_epilogue<EPI, BN>(p, tmem + (uint32_t(quarter * 32) << 16) + uint32_t(b * BN), m0 + quarter * 32 + lane,
+                             n0);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
@@ -389,21 +400,45 @@ bool gemm_tc_supported(int64_t m, int64_t n, int64_t k, const void* x, const voi
 
 namespace {
 
-template <int EPI>
-int launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mw2, const GemmArgs& a, int tiles_n,
+template <int EPI, int BN>
+int launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap& mw2, const GemmArgs& a,
                 cudaStream_t st) {
   static PerDeviceOnce configured;
   if (!configured.run([] {
-        return cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) ==
-               cudaSuccess;
+        return cudaFuncSetAttribute(gemm_tc_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    GL<BN>::kSmem) == cudaSuccess;
       }))
     return SB_INTERNAL;
-  const int tiles = tiles_n * ((a.m + kBM - 1) / kBM);
+  constexpr int cols = EPI == 1 ? BN / 2 : BN;
+  const int tiles = (a.n + cols - 1) / cols * ((a.m + kBM - 1) / kBM);
   const dim3 grid{unsigned(tiles < kNumSMs ? tiles : kNumSMs), 1u, 1u};  // persistent: one CTA per SM
-  if (launch_pdl(gemm_tc_kernel<EPI>, grid, dim3(kGThreads), size_t(kGSmem), st, mx, mw, mw2, a) != cudaSuccess)
+  if (launch_pdl(gemm_tc_kernel<EPI, BN>, grid, dim3(kGThreads), size_t(GL<BN>::kSmem), st, mx, mw, mw2, a) !=
+      cudaSuccess)
     return SB_INTERNAL;
   count_launch();
   return SB_OK;
+}
+
+// The tile width for an m x n launch (n output features; a SwiGLU tile holds
+// BN/2 of them): a persistent CTA's time goes with (tiles per CTA, rounded
+// up) x (BN + 32) -- the B tile plus about 32 rows' worth of A tile and
+// epilogue -- so small m takes narrow tiles that fill the 148 SMs, and
+// prefill-sized m keeps 256 (at m = 16384 every 7B projection does).  Ties
+// keep the wider tile.
+int choose_bn(int64_t m, int64_t n, bool swiglu) {
+  int best = 256;
+  int64_t best_cost = -1;
+  for (int bn : {256, 128, 64, 32}) {
+    if (swiglu && bn < 64) continue;
+    const int64_t cols = swiglu ? bn / 2 : bn;
+    const int64_t tiles = (n + cols - 1) / cols * ((m + kBM - 1) / kBM);
+    const int64_t cost = (tiles + kNumSMs - 1) / kNumSMs * (bn + 32);
+    if (best_cost < 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -411,8 +446,9 @@ int launch_gemm(const CUtensorMap& mx, const CUtensorMap& mw, const CUtensorMap&
 int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w, int64_t n, const float* scale,
                         const uint16_t* residual, int64_t ldr, uint16_t* y, int64_t ldy, int* err, cudaStream_t st) {
   if (!gemm_tc_supported(m, n, k, x, w)) return SB_INVALID_ARGUMENT;
+  const int bn = choose_bn(m, n, false);
   CUtensorMap mx, mw;
-  if (!make_map(&mx, x, m, k, kBM) || !make_map(&mw, w, n, k, kBN)) return SB_INTERNAL;
+  if (!make_map(&mx, x, m, k, kBM) || !make_map(&mw, w, n, k, uint32_t(bn))) return SB_INTERNAL;
   GemmArgs a{};
   a.m = int(m);
   a.n = int(n);
@@ -423,15 +459,22 @@ int launch_gemm_tc_bf16(const uint16_t* x, int64_t m, int64_t k, const uint16_t*
   a.y = y;
   a.ldy = int(ldy);
   a.err = err;
-  return launch_gemm<0>(mx, mw, mw, a, int((n + kBN - 1) / kBN), st);
+  switch (bn) {
+    case 32: return launch_gemm<0, 32>(mx, mw, mw, a, st);
+    case 64: return launch_gemm<0, 64>(mx, mw, mw, a, st);
+    case 128: return launch_gemm<0, 128>(mx, mw, mw, a, st);
+    default: return launch_gemm<0, 256>(mx, mw, mw, a, st);
+  }
 }
 
 int launch_gemm_tc_swiglu(const uint16_t* x, int64_t m, int64_t k, const uint16_t* w_gate, const uint16_t* w_up,
                           int64_t n, const float* s_gate, const float* s_up, uint16_t* y, int64_t ldy, int* err,
                           cudaStream_t st) {
   if (!gemm_tc_supported(m, n, k, x, w_gate) || !gemm_tc_supported(m, n, k, x, w_up)) return SB_INVALID_ARGUMENT;
+  const int bn = choose_bn(m, n, true);
   CUtensorMap mx, mg, mu;
-  if (!make_map(&mx, x, m, k, kBM) || !make_map(&mg, w_gate, n, k, kBN / 2) || !make_map(&mu, w_up, n, k, kBN / 2))
+  if (!make_map(&mx, x, m, k, kBM) || !make_map(&mg, w_gate, n, k, uint32_t(bn / 2)) ||
+      !make_map(&mu, w_up, n, k, uint32_t(bn / 2)))
     return SB_INTERNAL;
   GemmArgs a{};
   a.m = int(m);
@@ -442,7 +485,11 @@ int launch_gemm_tc_swiglu(const uint16_t* x, int64_t m, int64_t k, const uint16_
   a.y = y;
   a.ldy = int(ldy);
   a.err = err;
-  return launch_gemm<1>(mx, mg, mu, a, int((n + kBN / 2 - 1) / (kBN / 2)), st);
+  switch (bn) {
+    case 64: return launch_gemm<1, 64>(mx, mg, mu, a, st);
+    case 128: return launch_gemm<1, 128>(mx, mg, mu, a, st);
+    default: return launch_gemm<1, 256>(mx, mg, mu, a, st);
+  }
 }
 
 int launch_codes_to_bf16(const void* w, const void* scale, int fmt, int64_t n, int64_t k, uint16_t* out,
