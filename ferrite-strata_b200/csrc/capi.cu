@@ -4,6 +4,9 @@
 #include "k_gemv_mma.cuh"
 
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 
 namespace sb {
 std::atomic<uint64_t> g_launches{0};
@@ -20,6 +23,27 @@ bool pdl_enabled() {
 using namespace sb;
 
 static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Weight-expansion scratch of the linear entry points: one grow-only device
+// buffer per (device, stream).  Work on one stream runs in order, so a buffer
+// is never used by two launches at once; one that must grow is released with
+// cudaFreeAsync on its stream (after the work already queued there) and
+// replaced.  The buffers live until the process exits.
+static void* linear_scratch(cudaStream_t st, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> bufs;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  auto& e = bufs[{dev, st}];
+  if (e.first && e.second >= bytes) return e.first;
+  if (e.first) cudaFreeAsync(e.first, st);
+  e = {nullptr, 0};
+  void* p = nullptr;
+  if (cudaMallocAsync(&p, bytes, st) != cudaSuccess) return nullptr;
+  e = {p, bytes};
+  return p;
+}
 
 extern "C" {
 
@@ -58,22 +82,21 @@ static int32_t linear_common(WFormat fmt, const uint16_t* x, int64_t m, int64_t 
   b.jobs[0] = LinearJob{w, s, int(n), y, int(n), residual, int(n)};
   if (m > kGemvMaxRows && gemm_tc_supported(m, n, k, x, w)) {
     // Prefill-sized batches: tcgen05 GEMM over bf16 weights.  Quantized
-    // weights are first expanded into a stream-ordered temporary (int8: the
+    // weights are first expanded into the stream's cached scratch (int8: the
     // exact codes, scaled per channel in the GEMM epilogue; int4: code * group
-    // scale rounded to bf16).
+    // scale rounded to bf16; MX: code * 2^(e - 127), exact).
     const cudaStream_t st = S(stream);
     if (fmt == WFormat::BF16)
       return launch_gemm_tc_bf16(x, m, k, static_cast<const uint16_t*>(w), n, nullptr, residual, n, y, n, nullptr,
                                  st);
-    void* tmp = nullptr;
-    if (cudaMallocAsync(&tmp, size_t(n) * size_t(k) * 2, st) != cudaSuccess) return SB_RESOURCE_EXHAUSTED;
+    void* tmp = linear_scratch(st, size_t(n) * size_t(k) * 2);
+    if (!tmp) return SB_RESOURCE_EXHAUSTED;
     const int cf = fmt == WFormat::W8PC ? 1 : fmt == WFormat::MXFP8 ? 2 : fmt == WFormat::MXFP4 ? 3 : 0;
     int rc = launch_codes_to_bf16(w, s, cf, n, k, static_cast<uint16_t*>(tmp), st);
     if (rc == SB_OK)
       rc = launch_gemm_tc_bf16(x, m, k, static_cast<const uint16_t*>(tmp), n,
                                fmt == WFormat::W8PC ? static_cast<const float*>(s) : nullptr, residual, n, y, n,
                                nullptr, st);
-    cudaFreeAsync(tmp, st);
     return rc;
   }
   GemvMmaArgs ga{};

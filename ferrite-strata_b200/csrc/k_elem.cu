@@ -106,32 +106,49 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g
 }
 
 // Rotate-half RoPE; angles in double, as the oracle computes them.
+constexpr int kRopeRows = 4;  // rows whose cos/sin tables one pass computes (fewer for huge head_dim)
+
 template <typename T>
 __global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__ pos, int64_t rows,
-                            int heads, int head_dim, double theta, T* __restrict__ y) {
+                            int heads, int head_dim, double theta, T* __restrict__ y, int nr,
+                            const double* __restrict__ inv_freq) {
   pdl_trigger();
-  pdl_wait();
-  // One row at a time per block: the row's cos/sin for each frequency are
-  // computed once (in double, as the oracle does) and shared by every head.
-  extern __shared__ double cs[];  // [half] cos, then [half] sin
+  // The inverse frequencies theta^(-2j/d) (from the executable's host-computed
+  // table, else pow in double) do not depend on the previous kernel: once per
+  // block, before the wait.  Then nr rows at a time: every thread computes one
+  // (row, j) angle's cos/sin in double, rounded to f32, and the rows' heads are
+  // rotated in f32 (B200's FP64 pipe would bound a double rotation; the f32
+  // one differs from the oracle's double arithmetic by about 2^-24 relative,
+  // far inside bf16 output precision).
+  extern __shared__ double sh[];  // inv[half], then cs[nr][2][half] as f32
   const int half = head_dim / 2;
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    __syncthreads();  // the previous row's table is no longer read
-    for (int j = threadIdx.x; j < half; j += blockDim.x) {
-      const double inv = pow(theta, -2.0 * double(j) / double(head_dim));
-      double s, c;
-      sincos(double(pos[row]) * inv, &s, &c);
-      cs[j] = c;
-      cs[half + j] = s;
+  double* inv = sh;
+  float* cs = reinterpret_cast<float*>(sh + half);
+  for (int j = threadIdx.x; j < half; j += blockDim.x)
+    inv[j] = inv_freq ? inv_freq[j] : pow(theta, -2.0 * double(j) / double(head_dim));
+  pdl_wait();
+  const int per_row = heads * half;
+  for (int64_t row0 = int64_t(blockIdx.x) * nr; row0 < rows; row0 += int64_t(gridDim.x) * nr) {
+    __syncthreads();  // inv is written; the previous rows' table is no longer read
+    for (int t = threadIdx.x; t < nr * half; t += blockDim.x) {
+      const int r = t / half, j = t - r * half;
+      if (row0 + r < rows) {
+        double sn, c;
+        sincos(double(pos[row0 + r]) * inv[j], &sn, &c);
+        cs[(2 * r) * half + j] = float(c);
+        cs[(2 * r + 1) * half + j] = float(sn);
+      }
     }
     __syncthreads();
-    const int64_t base = row * int64_t(heads) * head_dim;
-    for (int i = threadIdx.x; i < heads * half; i += blockDim.x) {
+    for (int t = threadIdx.x; t < nr * per_row; t += blockDim.x) {
+      const int r = t / per_row, i = t - r * per_row;
+      if (row0 + r >= rows) break;
       const int h = i / half, j = i - h * half;
-      const int64_t b = base + int64_t(h) * head_dim;
-      const double x1 = ld(x, b + j), x2 = ld(x, b + j + half), c = cs[j], s = cs[half + j];
-      st(y, b + j, float(x1 * c - x2 * s));
-      st(y, b + j + half, float(x2 * c + x1 * s));
+      const int64_t b = (row0 + r) * int64_t(heads) * head_dim + int64_t(h) * head_dim;
+      const float x1 = ld(x, b + j), x2 = ld(x, b + j + half);
+      const float c = cs[(2 * r) * half + j], sn = cs[(2 * r + 1) * half + j];
+      st(y, b + j, fmaf(x1, c, -x2 * sn));
+      st(y, b + j + half, fmaf(x2, c, x1 * sn));
     }
   }
 }
@@ -435,7 +452,16 @@ inline unsigned grid_for(int64_t n, int threads = 256) {
   return unsigned(b < 1 ? 1 : b);
 }
 
-inline int row_threads(int64_t cols) {
+// Threads per row for rms_norm.  With many bf16 rows of whole 16-byte chunks
+// (enough blocks to fill the GPU), four chunks per thread -- 128 threads for
+// 4096 columns, 256 for 8192 -- so each thread has four loads in flight and
+// the block reduction is short (16384 x 4096: 86 -> 32 us).  A few rows
+// (decode) are latency-bound and keep one chunk per thread.
+inline int row_threads(int64_t cols, bool chunked = false) {
+  if (chunked) {
+    const int64_t t = ((cols / 8 + 3) / 4 + 31) / 32 * 32;
+    return int(t < 64 ? 64 : t > 1024 ? 1024 : t);
+  }
   if (cols >= 1024) return 512;
   if (cols >= 256) return 256;
   return 128;
@@ -447,19 +473,28 @@ template <typename T>
 int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float eps, T* y,
                     cudaStream_t st) {
   if (rows == 0 || cols == 0) return SB_OK;
-  launch_pdl(rms_norm_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols)), 0, st, x, g, cols, eps, y);
+  const bool chunked = sizeof(T) == 2 && cols % 8 == 0 && rows >= 4 * kNumSMs;
+  launch_pdl(rms_norm_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols, chunked)), 0, st, x, g, cols, eps, y);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
 
 template <typename T>
 int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int64_t head_dim,
-                double theta, T* y, cudaStream_t st) {
+                double theta, T* y, cudaStream_t st, const double* inv_freq) {
   if (head_dim % 2) return SB_INVALID_ARGUMENT;
   if (rows * heads * (head_dim / 2) == 0) return SB_OK;
-  const unsigned blocks = unsigned(rows < 8 * kNumSMs ? rows : 8 * kNumSMs);
-  launch_pdl(rope_kernel<T>, dim3(blocks), dim3(256), size_t(head_dim) * sizeof(double), st, x, pos, rows,
-             int(heads), int(head_dim), theta, y);
+  // Rows per pass: as many as fit in the default 48 KB of dynamic shared
+  // memory, up to kRopeRows.
+  const int64_t half = head_dim / 2;
+  const int64_t fit = (48 * 1024 / int64_t(sizeof(double)) / half - 1) / 2;
+  if (fit < 1) return SB_INVALID_ARGUMENT;
+  const int nr = int(fit < kRopeRows ? fit : kRopeRows);
+  const int64_t groups = (rows + nr - 1) / nr;
+  const unsigned blocks = unsigned(groups < 8 * kNumSMs ? groups : 8 * kNumSMs);
+  const size_t smem = size_t(half) * (1 + 2 * nr) * sizeof(double);
+  launch_pdl(rope_kernel<T>, dim3(blocks), dim3(256), smem, st, x, pos, rows, int(heads), int(head_dim), theta, y,
+             nr, inv_freq);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -591,7 +626,7 @@ int launch_convert(int dir, const void* x, int64_t n, void* y, cudaStream_t st) 
   template int launch_last_rows<T>(const T*, int64_t, int64_t, int64_t, T*, cudaStream_t);       \
   template int launch_rms_norm<T>(const T*, const T*, int64_t, int64_t, float, T*, cudaStream_t); \
   template int launch_rope<T>(const T*, const int32_t*, int64_t, int64_t, int64_t, double, T*,  \
-                              cudaStream_t);                                                   \
+                              cudaStream_t, const double*);                                    \
   template int launch_swiglu<T>(const T*, const T*, int64_t, T*, cudaStream_t);                 \
   template int launch_binary<T>(int, const T*, const T*, T*, const BcastShape&, cudaStream_t);  \
   template int launch_unary<T>(int, const T*, int64_t, T*, cudaStream_t);                       \

@@ -22,7 +22,7 @@ int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float ep
                     cudaStream_t st);
 template <typename T>
 int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int64_t head_dim,
-                double theta, T* y, cudaStream_t st);
+                double theta, T* y, cudaStream_t st, const double* inv_freq = nullptr);
 template <typename T>
 int launch_swiglu(const T* gate, const T* up, int64_t n, T* y, cudaStream_t st);
 // op: 0 = add, 1 = mul

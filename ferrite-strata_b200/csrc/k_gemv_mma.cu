@@ -145,7 +145,7 @@ __device__ __forceinline__ void tile_epilogue(const Params& p, const TileRows& t
       double xlo = bf2f(f2bf(vlo)), xhi = bf2f(f2bf(vhi));
       const int pos = e.pos[m];
       if (jl < 2) {
-        const double inv = pow(e.theta, -2.0 * double(i) / double(hd));
+        const double inv = e.inv_freq ? e.inv_freq[i] : pow(e.theta, -2.0 * double(i) / double(hd));
         double sn, cs;
         sincos(double(pos) * inv, &sn, &cs);
         const double a = xlo * cs - xhi * sn, b = xhi * cs + xlo * sn;

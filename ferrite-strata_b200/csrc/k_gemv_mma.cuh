@@ -22,6 +22,7 @@ struct QkvExtra {
   double theta;
   int* err;
   KvPages kp;
+  const double* inv_freq;  // [head_dim / 2] theta^(-2j/d), or null: computed with pow
 };
 
 struct GemvMmaArgs {

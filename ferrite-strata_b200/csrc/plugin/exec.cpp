@@ -11,6 +11,7 @@
 //   * a linear whose only consumer is a residual add writes x + W.x directly.
 #include <algorithm>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <type_traits>
@@ -51,6 +52,21 @@ struct Lowerer {
   bool decline(const std::string& why) {
     *reason = why;
     return false;
+  }
+
+  // RoPE inverse frequencies theta^(-2j/d), j < d/2, in double with the host
+  // pow (the oracle's, oracle/strata_oracle.c ora_rope), stored once among the
+  // executable's constants: the kernels read them instead of calling pow per
+  // element.  Returns their offset there.
+  uint64_t rope_table(double theta, int64_t hd) {
+    std::vector<uint8_t>& c = exe.consts;
+    const uint64_t off = (c.size() + 7) / 8 * 8;
+    c.resize(off + size_t(hd / 2) * sizeof(double));
+    for (int64_t j = 0; j < hd / 2; ++j) {
+      const double v = std::pow(theta, -2.0 * double(j) / double(hd));
+      std::memcpy(c.data() + off + size_t(j) * sizeof(double), &v, sizeof(double));
+    }
+    return off;
   }
 
   uint32_t in(const Node& n, size_t i) const {
@@ -314,6 +330,7 @@ struct Lowerer {
       f.i[5] = AT.i[5];      // max_len
       f.i[6] = AT.i[1];      // tokens per sequence
       f.d = RQ.attr_float("theta", 10000.0);
+      f.const_off = exe.steps[sq].const_off;  // the q RoPE's table (same theta and head_dim)
       const uint32_t kc = A.inputs[3], vc = A.inputs[4], pos = A.inputs[5];
       f.v = {L.v[0], L.v[1], L.v[2], L.v[5], L.v[6], L.v[9], L.v[10], qr, kc, vc, pos};
       f.reads = {L.v[0], L.v[1], L.v[2], L.v[5], L.v[6], L.v[9], L.v[10], pos, kc, vc};
@@ -704,6 +721,7 @@ struct Lowerer {
       st.i[1] = last_dim(V(x)) / hd;
       st.i[2] = hd;
       st.d = n.attr_float("theta", 10000.0);
+      st.const_off = rope_table(st.d, hd);
       st.v = {x, pos, out};
       st.reads = {x, pos};
       st.writes = {out};
@@ -992,7 +1010,8 @@ void plan_workspace(Exe& exe) {
     if (exe.steps[s].scratch_bytes) release(exe.steps[s].scratch_off, exe.steps[s].scratch_bytes);
     for (auto v : dying[s]) release(uint64_t(exe.ws_off[v]), g.values[v].bytes());
   }
-  exe.ws_bytes = top;
+  exe.consts_off = (top + 255) / 256 * 256;
+  exe.ws_bytes = exe.consts.empty() ? top : exe.consts_off + exe.consts.size();
 }
 
 }  // namespace
@@ -1027,6 +1046,13 @@ struct Ptrs {
 template <typename T>
 T* P(const Ptrs& p, uint32_t v) {
   return static_cast<T*>(p.at(v));
+}
+
+// A step's table among the executable's constants, or null.
+template <typename T>
+const T* const_table(const Exe& exe, const Step& st) {
+  if (st.const_off == UINT64_MAX || !exe.ws) return nullptr;
+  return reinterpret_cast<const T*>(static_cast<const char*>(exe.ws) + exe.consts_off + st.const_off);
 }
 
 // The paged-cache descriptor of an append, attention or fused q/k/v step
@@ -1067,7 +1093,7 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
                                     P<T>(p, st.v[2]), s);
     case SK::Rope:
       return sb::launch_rope<T>(P<T>(p, st.v[0]), P<int32_t>(p, st.v[1]), st.i[0], st.i[1], st.i[2], st.d,
-                                P<T>(p, st.v[2]), s);
+                                P<T>(p, st.v[2]), s, const_table<double>(p.exe, st));
     case SK::SwiGLU:
       return sb::launch_swiglu<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), st.i[0], P<T>(p, st.v[2]), s);
     case SK::Transpose:
@@ -1205,6 +1231,7 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
         e.theta = st.d;
         e.err = ctx.d_err;
         e.kp = pages_of(p, st, 11);
+        e.inv_freq = const_table<double>(exe, st);
         if (!sb::gemv_mma_supported(ga))
           fail(STRATA_INTERNAL, "fused q/k/v projection `" + st.label + "` has an unsupported layout");
         rc = sb::launch_gemv_mma(ga, s);

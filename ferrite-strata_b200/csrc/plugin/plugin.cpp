@@ -663,7 +663,13 @@ void enqueue_run(Ctx& c, const StrataRunArgs* a) {
     if (e.needed_input[v] && !ext[v] && e.g.values[v].bytes() > 0)
       fail(STRATA_INVALID_ARGUMENT, "no buffer for input `" + e.g.values[v].name + "` of `" + e.label + "`");
   c.ensure_device();
-  if (!e.ws && e.ws_bytes) cuda_check(cudaMalloc(&e.ws, e.ws_bytes), "workspace cudaMalloc");
+  if (!e.ws && e.ws_bytes) {
+    cuda_check(cudaMalloc(&e.ws, e.ws_bytes), "workspace cudaMalloc");
+    if (!e.consts.empty())
+      cuda_check(cudaMemcpy(static_cast<char*>(e.ws) + e.consts_off, e.consts.data(), e.consts.size(),
+                            cudaMemcpyHostToDevice),
+                 "uploading the executable's constants");
+  }
 
   if (!graphs_enabled()) {
     enqueue(c, e, ext);

@@ -89,6 +89,7 @@ struct Step {
   sb::Epilogue epi = sb::Epilogue::None;
   int njobs = 0;
   uint64_t scratch_off = 0, scratch_bytes = 0;
+  uint64_t const_off = UINT64_MAX;     // offset of this step's table in the executable's constants
   std::vector<uint32_t> reads, writes;  // for liveness; writes may include in-place inputs
   int node = -1;                       // originating graph node
   std::string label;
@@ -104,6 +105,10 @@ struct Exe {
   std::vector<int64_t> ws_off;      // value -> workspace offset, -1 if none
   uint64_t ws_bytes = 0;
   void* ws = nullptr;
+  // Tables computed on the host at lowering (RoPE inverse frequencies), placed
+  // after the workspace at consts_off and uploaded with it.
+  std::vector<uint8_t> consts;
+  uint64_t consts_off = 0;
   std::vector<bool> is_output;
   std::vector<bool> needed_input;   // graph inputs some step reads
   // CUDA graph cache, keyed by the external pointers of a run.
