@@ -51,9 +51,12 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 # these files are unchanged since it was measured.
 GEMV_SOURCES = ("ferrite-strata_b200/csrc/k_gemv_mma.cu", "ferrite-strata_b200/csrc/k_int4.cuh")
 # DRAM bytes read + written by one launch of the gate/up GEMV with the SwiGLU
-# epilogue (ncu: dram__bytes_read.sum + dram__bytes_write.sum of one launch
-# among weight sets larger than L2), keyed by (source digest, M, N, K).
-GEMV_TRAFFIC = {}
+# epilogue (ncu: dram__bytes_read.sum + dram__bytes_write.sum of one launch,
+# cold cache, in a 2-layer decode step), keyed by (source digest, M, N, K).
+GEMV_TRAFFIC = {
+    ("5b752ad245761274", 8, 22016, 4096): 50817280 + 2816,
+    ("5b752ad245761274", 1, 22016, 4096): 50759936 + 9216,
+}
 
 
 def gemv_source_digest():

@@ -65,6 +65,19 @@ bool pdl_enabled();
 #endif
 
 #if defined(__CUDACC__)
+// cos and sin of the RoPE angle pos * inv (radians) as f32.  The angle is
+// formed and reduced modulo 2 pi in double (a few FP64 operations; exact to
+// far below f32 resolution for any position), then evaluated by the f32
+// sincosf on |r| <= pi, whose error of about one f32 ulp is what rounding a
+// double-precision result to f32 costs anyway.  A double sincos per (row,
+// frequency) instead bounds RoPE on B200's narrow FP64 pipe.
+__device__ __forceinline__ void rope_cos_sin(int pos, double inv, float& c, float& s) {
+  const double a = double(pos) * inv;
+  const double k = rint(a * 0.15915494309189535);  // turns: a / (2 pi)
+  const float r = float(fma(-k, 6.283185307179586, a));
+  sincosf(r, &s, &c);
+}
+
 // The cache row (head_dim elements) that holds position p of (seq, kvh), or
 // -1 when p lies outside the sequence's pages or its page index is not one of
 // the pool's pages.  Callers check 0 <= p < max_len first.

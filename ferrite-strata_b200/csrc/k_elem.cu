@@ -116,10 +116,10 @@ __global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__
   // The inverse frequencies theta^(-2j/d) (from the executable's host-computed
   // table, else pow in double) do not depend on the previous kernel: once per
   // block, before the wait.  Then nr rows at a time: every thread computes one
-  // (row, j) angle's cos/sin in double, rounded to f32, and the rows' heads are
-  // rotated in f32 (B200's FP64 pipe would bound a double rotation; the f32
-  // one differs from the oracle's double arithmetic by about 2^-24 relative,
-  // far inside bf16 output precision).
+  // (row, j) angle's cos/sin (rope_cos_sin: reduced in double, evaluated in
+  // f32), and the rows' heads are rotated in f32 (B200's FP64 pipe would
+  // bound double arithmetic here; the f32 results differ from the oracle's
+  // double ones by about 2^-24 relative, far inside bf16 output precision).
   extern __shared__ double sh[];  // inv[half], then cs[nr][2][half] as f32
   const int half = head_dim / 2;
   double* inv = sh;
@@ -128,18 +128,41 @@ __global__ void rope_kernel(const T* __restrict__ x, const int32_t* __restrict__
     inv[j] = inv_freq ? inv_freq[j] : pow(theta, -2.0 * double(j) / double(head_dim));
   pdl_wait();
   const int per_row = heads * half;
+  const bool vec8 = sizeof(T) == 2 && half % 8 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
   for (int64_t row0 = int64_t(blockIdx.x) * nr; row0 < rows; row0 += int64_t(gridDim.x) * nr) {
     __syncthreads();  // inv is written; the previous rows' table is no longer read
     for (int t = threadIdx.x; t < nr * half; t += blockDim.x) {
       const int r = t / half, j = t - r * half;
-      if (row0 + r < rows) {
-        double sn, c;
-        sincos(double(pos[row0 + r]) * inv[j], &sn, &c);
-        cs[(2 * r) * half + j] = float(c);
-        cs[(2 * r + 1) * half + j] = float(sn);
-      }
+      if (row0 + r < rows) rope_cos_sin(pos[row0 + r], inv[j], cs[(2 * r) * half + j], cs[(2 * r + 1) * half + j]);
     }
     __syncthreads();
+    if (vec8) {
+      // bf16 rows with half a multiple of 8: 8 pairs per step, as two 16-byte
+      // loads and two 16-byte stores, so each thread has whole lines in flight.
+      const int per_head = half / 8, units = heads * per_head;
+      for (int t = threadIdx.x; t < nr * units; t += blockDim.x) {
+        const int r = t / units, u = t - r * units;
+        if (row0 + r >= rows) break;
+        const int h = u / per_head, j0 = (u - h * per_head) * 8;
+        const int64_t b = (row0 + r) * int64_t(heads) * head_dim + int64_t(h) * head_dim + j0;
+        const uint4 a = *reinterpret_cast<const uint4*>(x + b), bb = *reinterpret_cast<const uint4*>(x + b + half);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {bb.x, bb.y, bb.z, bb.w};
+        const float* cr = cs + (2 * r) * half + j0;
+        const float* sr = cs + (2 * r + 1) * half + j0;
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x1a = bf_lo(aw[e]), x1b = bf_hi(aw[e]), x2a = bf_lo(bw[e]), x2b = bf_hi(bw[e]);
+          const float ca = cr[2 * e], cb = cr[2 * e + 1], sa = sr[2 * e], sb2 = sr[2 * e + 1];
+          lo[e] = pack_bf2(fmaf(x1a, ca, -x2a * sa), fmaf(x1b, cb, -x2b * sb2));
+          hi[e] = pack_bf2(fmaf(x2a, ca, x1a * sa), fmaf(x2b, cb, x1b * sb2));
+        }
+        *reinterpret_cast<uint4*>(y + b) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(y + b + half) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      }
+      continue;
+    }
     for (int t = threadIdx.x; t < nr * per_row; t += blockDim.x) {
       const int r = t / per_row, i = t - r * per_row;
       if (row0 + r >= rows) break;

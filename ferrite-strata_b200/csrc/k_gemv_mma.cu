@@ -146,8 +146,9 @@ __device__ __forceinline__ void tile_epilogue(const Params& p, const TileRows& t
       const int pos = e.pos[m];
       if (jl < 2) {
         const double inv = e.inv_freq ? e.inv_freq[i] : pow(e.theta, -2.0 * double(i) / double(hd));
-        double sn, cs;
-        sincos(double(pos) * inv, &sn, &cs);
+        float snf, csf;
+        rope_cos_sin(pos, inv, csf, snf);
+        const double sn = snf, cs = csf;
         const double a = xlo * cs - xhi * sn, b = xhi * cs + xlo * sn;
         xlo = double(float(a));
         xhi = double(float(b));
