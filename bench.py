@@ -633,6 +633,50 @@ def run_sweep(args):
     return 0
 
 
+def run_breakdown(args, plugin, model, shape, kv_fill, world, rank, barrier):
+    """Per step-class device time of the decode step: every run is eager and
+    each step is bracketed by CUDA events on the plugin's stream (so the
+    classes' times add up to a little more than the graph-replayed step,
+    which overlaps neighbouring kernels).  The maximum over ranks per class."""
+    import torch
+    import torch.distributed as dist
+    lib = C.CDLL(plugin.path)
+    fn = lib.strata_b200_step_times
+    fn.argtypes = [C.c_char_p, C.c_uint64, C.c_int32]
+    fn.restype = C.c_uint64
+    for _ in range(args.warmup):
+        model.bound.run()
+    barrier()
+    fn(None, 0, 1)  # reset
+    for _ in range(args.steps):
+        model.bound.run()
+    barrier()
+    buf = C.create_string_buffer(int(fn(None, 0, 0)) + 1)
+    fn(buf, len(buf), 1)
+    mine = {k: (v[0] / args.steps, v[1] * 1e3 / args.steps) for k, v in json.loads(buf.value.decode()).items()}
+    every = [mine]
+    if world > 1:
+        every = [None] * world
+        dist.all_gather_object(every, mine)
+    if rank == 0:
+        classes = sorted({k for d in every for k in d})
+        out = {k: {"steps_per_step": max(d.get(k, (0, 0))[0] for d in every),
+                   "us_per_step": round(max(d.get(k, (0, 0))[1] for d in every), 2)} for k in classes}
+        total = sum(v["us_per_step"] for v in out.values())
+        print(json.dumps({"metric": "decode step breakdown (eager, CUDA events between steps)",
+                          "unit": "us per step, max over ranks", "n_gpus": world, "steps": args.steps,
+                          "config": decode_config(args, shape, kv_fill, world,
+                                                  step_bytes(shape, args.batch, kv_fill) * args.layers // shape.layers),
+                          "classes": dict(sorted(out.items(), key=lambda kv: -kv[1]["us_per_step"])),
+                          "sum_us_per_step": round(total, 1)}))
+    model.close()
+    plugin.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -650,6 +694,10 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="time the quantized Linear sweep (K = N = 4096, M in {1, 16, 128, 2048}, "
                          "int4, int8, MXFP8, MXFP4)")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="instead of the timed run: device time per step class (GEMVs, attention, "
+                         "all-reduce + add + norm, ...) of the decode step, run eagerly with CUDA events "
+                         "between steps; under torchrun rank 0 prints the maximum over ranks")
     ap.add_argument("--kv-page", type=int, default=0,
                     help="decode with a paged KV cache of this page size (block table, shuffled pages)")
     ap.add_argument("--profile-step", action="store_true",
@@ -683,6 +731,8 @@ def main():
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
     os.environ["STRATA_B200_DEVICE"] = str(local)
+    if args.breakdown:
+        os.environ["STRATA_B200_STEP_TIMES"] = "1"  # read once, when the library loads
     plugin = Plugin(os.path.join(PKG, "libstrata_b200.so"))
     if world > 1:
         uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
@@ -707,6 +757,9 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.breakdown:
+        return run_breakdown(args, plugin, model, shape, kv_fill, world, rank, barrier)
 
     # ---- device-timed steps (inputs resident, CUDA-graph replay) -------------
     for _ in range(args.warmup):

@@ -12,6 +12,8 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cmath>
+#include <mutex>
+#include <cstdio>
 #include <cstring>
 #include <map>
 #include <type_traits>
@@ -1172,9 +1174,115 @@ int enqueue_gemm(Ctx& ctx, Exe& exe, const Step& st, const sb::LinearBatch& b, c
 
 }  // namespace
 
+namespace {
+
+// The class a step's device time is reported under.
+const char* step_class(const Step& st) {
+  switch (st.kind) {
+    case SK::Linear:
+      if (st.scratch_bytes) return st.epi == sb::Epilogue::SwiGLU ? "gemm:swiglu" : "gemm";
+      return st.epi == sb::Epilogue::SwiGLU ? "gemv:swiglu" : st.epi == sb::Epilogue::Residual ? "gemv:residual" : "gemv";
+    case SK::QkvRope: return "gemv:qkv_rope_append";
+    case SK::Attention: return "attention";
+    case SK::KvAppend: return "kv_append";
+    case SK::AllReduce: return "all_reduce";
+    case SK::AllReduceAddNorm: return "all_reduce_add_norm";
+    case SK::RmsNorm: return "rms_norm";
+    case SK::Rope: return "rope";
+    case SK::Embed: return "embed";
+    case SK::Argmax: return "argmax";
+    case SK::VocabArgmax: return "vocab_argmax";
+    case SK::LastToken: return "last_token";
+    case SK::Binary: return "add_mul";
+    default: return "other";
+  }
+}
+
+void ev_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) fail(STRATA_INTERNAL, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+struct StepClock {
+  std::mutex mu;
+  std::map<std::string, std::pair<uint64_t, double>> acc;  // class -> (steps, ms)
+};
+
+StepClock& step_clock() {
+  static StepClock c;
+  return c;
+}
+
+// Events around every step of one eager run; destroyed on every path.
+struct StepEvents {
+  std::vector<cudaEvent_t> ev;
+  explicit StepEvents(size_t n) : ev(n, nullptr) {
+    for (auto& e : ev) ev_check(cudaEventCreate(&e), "cudaEventCreate");
+  }
+  ~StepEvents() {
+    for (auto e : ev)
+      if (e) cudaEventDestroy(e);
+  }
+};
+
+}  // namespace
+
+bool step_times_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("STRATA_B200_STEP_TIMES");
+    return v && *v && *v != '0';
+  }();
+  return on;
+}
+
+std::string step_times_json(bool reset) {
+  StepClock& c = step_clock();
+  std::lock_guard<std::mutex> lk(c.mu);
+  std::string out = "{";
+  char buf[96];
+  bool first = true;
+  for (const auto& kv : c.acc) {
+    std::snprintf(buf, sizeof(buf), "%s\"%s\": [%llu, %.6f]", first ? "" : ", ", kv.first.c_str(),
+                  static_cast<unsigned long long>(kv.second.first), kv.second.second);
+    out += buf;
+    first = false;
+  }
+  out += "}";
+  if (reset) c.acc.clear();
+  return out;
+}
+
+namespace {
+
+void enqueue_steps(Ctx& ctx, Exe& exe, const std::vector<void*>& ext, StepEvents* events);
+
+}  // namespace
+
 void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
+  if (!step_times_enabled()) {
+    enqueue_steps(ctx, exe, ext, nullptr);
+    return;
+  }
+  StepEvents events(exe.steps.size() + 1);
+  ev_check(cudaEventRecord(events.ev[0], ctx.stream), "cudaEventRecord");
+  enqueue_steps(ctx, exe, ext, &events);
+  ev_check(cudaEventSynchronize(events.ev.back()), "cudaEventSynchronize");
+  StepClock& c = step_clock();
+  std::lock_guard<std::mutex> lk(c.mu);
+  for (size_t i = 0; i < exe.steps.size(); ++i) {
+    float ms = 0.0f;
+    ev_check(cudaEventElapsedTime(&ms, events.ev[i], events.ev[i + 1]), "cudaEventElapsedTime");
+    auto& a = c.acc[step_class(exe.steps[i])];
+    a.first += 1;
+    a.second += double(ms);
+  }
+}
+
+namespace {
+
+void enqueue_steps(Ctx& ctx, Exe& exe, const std::vector<void*>& ext, StepEvents* events) {
   Ptrs p{exe, ext};
   cudaStream_t s = ctx.stream;
+  size_t si = 0;
   for (const Step& st : exe.steps) {
     int rc = 0;
     switch (st.kind) {
@@ -1335,7 +1443,11 @@ void enqueue(Ctx& ctx, Exe& exe, const std::vector<void*>& ext) {
         break;
     }
     check_rc(rc, st);
+    ++si;
+    if (events) ev_check(cudaEventRecord(events->ev[si], s), "cudaEventRecord");
   }
 }
+
+}  // namespace
 
 }  // namespace sbp

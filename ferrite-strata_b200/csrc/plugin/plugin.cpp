@@ -95,7 +95,7 @@ int env_int(const char* name, int dflt) {
   return v && *v ? std::atoi(v) : dflt;
 }
 
-bool graphs_enabled() { return env_int("STRATA_B200_CUDA_GRAPHS", 1) != 0; }
+bool graphs_enabled() { return env_int("STRATA_B200_CUDA_GRAPHS", 1) != 0 && !step_times_enabled(); }
 
 // Cache of device allocations by rounded size, so per-run buffers (the
 // reference host allocates one per value per run) do not hit cudaMalloc.
@@ -955,6 +955,19 @@ static StrataPluginVersionExt g_version_ext = {
 };
 
 extern "C" {
+// Per-class device time of the steps run since the last reset (see
+// step_times_enabled), as JSON into buf (NUL-terminated when it fits).
+// Returns the bytes the JSON needs, without the NUL.
+__attribute__((visibility("default"))) uint64_t strata_b200_step_times(char* buf, uint64_t cap, int32_t reset) {
+  const std::string j = sbp::step_times_json(reset != 0);
+  if (buf && cap) {
+    const size_t n = j.size() < cap ? j.size() : size_t(cap - 1);
+    std::memcpy(buf, j.data(), n);
+    buf[n] = '\0';
+  }
+  return j.size();
+}
+
 __attribute__((visibility("default"))) StrataPluginV1 strata_plugin_v1 = {
     sizeof(StrataPluginV1),
     reinterpret_cast<StrataExtBase*>(&g_version_ext),

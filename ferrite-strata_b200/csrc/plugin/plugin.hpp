@@ -97,6 +97,13 @@ struct Step {
 
 constexpr uint32_t kNone = 0xffffffffu;
 
+// Per-class device time of executed steps, for profiling a whole step from
+// the outside (STRATA_B200_STEP_TIMES=1: runs are eager, each step is
+// bracketed by CUDA events, and the totals accumulate until read).
+bool step_times_enabled();
+// {"class": [steps, milliseconds], ...} since the last reset.
+std::string step_times_json(bool reset);
+
 struct Exe {
   Graph g;
   std::string label;

@@ -70,6 +70,19 @@ typedef struct StrataB200DeviceExt {
 } StrataB200DeviceExt;
 
 /* ------------------------------------------------------------------------ */
+/* Step profile                                                             */
+/* ------------------------------------------------------------------------ */
+
+/* With STRATA_B200_STEP_TIMES=1 in the environment when the library loads,
+ * every run is eager (no CUDA graph) and each of its steps is bracketed by
+ * CUDA events on the plugin's stream; the device time accumulates per step
+ * class ("gemv:swiglu", "attention", "all_reduce_add_norm", ...).  This
+ * writes {"class": [steps, milliseconds], ...} into buf (NUL-terminated when
+ * it fits), clears the totals when reset is non-zero, and returns the bytes
+ * the JSON needs.  No counterpart in the reference. */
+uint64_t strata_b200_step_times(char *buf, uint64_t cap, int32_t reset);
+
+/* ------------------------------------------------------------------------ */
 /* Kernel-level entry points                                                */
 /* ------------------------------------------------------------------------ */
 
