@@ -374,3 +374,18 @@ def test_paged_cache_rules(plugin):
                                      kv_page=8)[0])
     g = decoder_graph(small, batch=2, seq=1, max_len=96, fmt="f32", embed=False, head="none", kv_page=16)[0]
     assert plugin.compile(g) is None
+
+
+def test_step_times_export_answers_without_a_gpu():
+    """strata_b200_step_times: JSON of the per-class totals (none yet: "{}"),
+    the bytes needed returned even when the buffer is too small."""
+    lib = C.CDLL(LIB)
+    fn = lib.strata_b200_step_times
+    fn.argtypes = [C.c_char_p, C.c_uint64, C.c_int32]
+    fn.restype = C.c_uint64
+    need = fn(None, 0, 0)
+    buf = C.create_string_buffer(int(need) + 1)
+    assert fn(buf, len(buf), 1) == need
+    assert buf.value.decode() == "{}"
+    small = C.create_string_buffer(1)
+    assert fn(small, 1, 0) == need and small.value == b""
