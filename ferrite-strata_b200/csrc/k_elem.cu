@@ -46,11 +46,13 @@ __device__ float block_max(float v, float* red) {
   return warp_max(t);
 }
 
+// g_ready: gamma is not written by the kernels this one depends on (a graph
+// input), so it is read before griddepcontrol.wait and arrives while the
+// previous kernel finishes.
 template <typename T>
 __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g, int64_t cols,
-                                float eps, T* __restrict__ y) {
+                                float eps, T* __restrict__ y, int g_ready) {
   pdl_trigger();
-  pdl_wait();
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * cols;
@@ -62,6 +64,13 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g
     if (cols % 8 == 0 && chunks <= int64_t(kMax) * blockDim.x &&
         ((reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(y)) & 15) ==
             0) {
+      uint4 gv[kMax];
+#pragma unroll
+      for (int u = 0; u < kMax; ++u) {
+        const int64_t c = threadIdx.x + int64_t(u) * blockDim.x;
+        gv[u] = g_ready && c < chunks ? __ldg(reinterpret_cast<const uint4*>(g) + c) : make_uint4(0, 0, 0, 0);
+      }
+      pdl_wait();
       uint4 v[kMax];
       float ss = 0.0f;
 #pragma unroll
@@ -81,7 +90,7 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g
       for (int u = 0; u < kMax; ++u) {
         const int64_t c = threadIdx.x + int64_t(u) * blockDim.x;
         if (c < chunks) {
-          const uint4 g4 = __ldg(reinterpret_cast<const uint4*>(g) + c);
+          const uint4 g4 = g_ready ? gv[u] : __ldg(reinterpret_cast<const uint4*>(g) + c);
           const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, gw[4] = {g4.x, g4.y, g4.z, g4.w};
           uint32_t o[4];
 #pragma unroll
@@ -94,6 +103,7 @@ __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ g
       return;
     }
   }
+  pdl_wait();
   float ss = 0.0f;
   for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
     const float v = ld(xr, c);
@@ -494,10 +504,11 @@ inline int row_threads(int64_t cols, bool chunked = false) {
 
 template <typename T>
 int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float eps, T* y,
-                    cudaStream_t st) {
+                    cudaStream_t st, bool g_ready) {
   if (rows == 0 || cols == 0) return SB_OK;
   const bool chunked = sizeof(T) == 2 && cols % 8 == 0 && rows >= 4 * kNumSMs;
-  launch_pdl(rms_norm_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols, chunked)), 0, st, x, g, cols, eps, y);
+  launch_pdl(rms_norm_kernel<T>, dim3(unsigned(rows)), dim3(row_threads(cols, chunked)), 0, st, x, g, cols, eps, y,
+             g_ready ? 1 : 0);
   SB_LAUNCH_CHECK();
   return SB_OK;
 }
@@ -647,7 +658,7 @@ int launch_convert(int dir, const void* x, int64_t n, void* y, cudaStream_t st) 
 
 #define SB_INST(T)                                                                              \
   template int launch_last_rows<T>(const T*, int64_t, int64_t, int64_t, T*, cudaStream_t);       \
-  template int launch_rms_norm<T>(const T*, const T*, int64_t, int64_t, float, T*, cudaStream_t); \
+  template int launch_rms_norm<T>(const T*, const T*, int64_t, int64_t, float, T*, cudaStream_t, bool); \
   template int launch_rope<T>(const T*, const int32_t*, int64_t, int64_t, int64_t, double, T*,  \
                               cudaStream_t, const double*);                                    \
   template int launch_swiglu<T>(const T*, const T*, int64_t, T*, cudaStream_t);                 \

@@ -18,8 +18,10 @@ struct BcastShape {
 };
 
 template <typename T>
+// g_ready: gamma is written by none of the kernels this launch depends on
+// (it is read before the programmatic-launch wait).
 int launch_rms_norm(const T* x, const T* g, int64_t rows, int64_t cols, float eps, T* y,
-                    cudaStream_t st);
+                    cudaStream_t st, bool g_ready = false);
 template <typename T>
 int launch_rope(const T* x, const int32_t* pos, int64_t rows, int64_t heads, int64_t head_dim,
                 double theta, T* y, cudaStream_t st, const double* inv_freq = nullptr);

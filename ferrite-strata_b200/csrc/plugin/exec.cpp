@@ -706,6 +706,7 @@ struct Lowerer {
       st.i[0] = rows_of(V(x));
       st.i[1] = last_dim(V(x));
       st.d = n.attr_float("eps", 1e-5);
+      st.i[2] = V(gm).producer < 0 ? 1 : 0;  // gamma is a graph input: read before the wait
       st.v = {x, gm, out};
       st.reads = {x, gm};
       st.writes = {out};
@@ -1092,7 +1093,7 @@ int run_float(Ctx& ctx, const Step& st, const Ptrs& p) {
                                       st.i[1], float(st.d), P<T>(p, st.v[3]), s);
     case SK::RmsNorm:
       return sb::launch_rms_norm<T>(P<T>(p, st.v[0]), P<T>(p, st.v[1]), st.i[0], st.i[1], float(st.d),
-                                    P<T>(p, st.v[2]), s);
+                                    P<T>(p, st.v[2]), s, st.i[2] != 0);
     case SK::Rope:
       return sb::launch_rope<T>(P<T>(p, st.v[0]), P<int32_t>(p, st.v[1]), st.i[0], st.i[1], st.i[2], st.d,
                                 P<T>(p, st.v[2]), s, const_table<double>(p.exe, st));
