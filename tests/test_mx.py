@@ -184,3 +184,57 @@ def test_mx_decoder_step_matches_oracle(cuda, plugin, fmt, batch, seq):
     res, _ = run_graph(plugin, g, host)
     ref = graph_eval.evaluate(g, {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in host.items()})
     assert_close(as_f32(g.values[hd.out], res[hd.out]), ref[hd.out], TOL_BF16, f"{fmt} logits")
+
+
+def _grid(fmt):
+    """Every finite value of the element format, with its code, by the
+    format's definition (independent of the oracle's arithmetic)."""
+    vals = []
+    if fmt == "mxfp8":
+        for c in range(256):
+            e, m = (c >> 3) & 15, c & 7
+            if (c & 0x7F) == 0x7F:
+                continue
+            v = m * 2.0 ** -9 if e == 0 else (1 + m / 8) * 2.0 ** (e - 7)
+            vals.append((-v if c & 0x80 else v, c))
+    else:
+        for c in range(16):
+            e, m = (c >> 1) & 3, c & 1
+            v = m * 0.5 if e == 0 else (1 + m / 2) * 2.0 ** (e - 1)
+            vals.append((-v if c & 8 else v, c))
+    return vals
+
+
+def _encode_by_search(x, fmt):
+    """Nearest representable value, ties to the even code (even mantissa),
+    saturating at the largest finite magnitude; zero keeps the sign."""
+    grid = _grid(fmt)
+    top = max(abs(v) for v, _ in grid)
+    sign_bit = 0x80 if fmt == "mxfp8" else 8
+    if abs(x) >= top:
+        return max((c for v, c in grid if abs(v) == top and (v < 0) == (x < 0)))
+    best = min(abs(v - x) for v, _ in grid)
+    cands = [(v, c) for v, c in grid if abs(v - x) == best]
+    if len(cands) > 1:  # a tie: the even mantissa
+        cands = [(v, c) for v, c in cands if (c & 1) == 0] or cands
+    v, c = cands[0]
+    if v == 0:  # both zeros are nearest: keep x's sign
+        c = (sign_bit if np.signbit(x) else 0)
+    return c
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "mxfp4"])
+def test_mx_encoders_agree_with_an_independent_search(fmt):
+    """The oracle's E4M3 / E2M1 encoders against a nearest-value search over
+    every representable value: random magnitudes across the formats' range,
+    exact ties and saturation."""
+    L = ora.lib()
+    enc = L.ora_f32_to_e4m3 if fmt == "mxfp8" else L.ora_f32_to_e2m1
+    rng = np.random.default_rng(11)
+    top = 448.0 if fmt == "mxfp8" else 6.0
+    xs = list((rng.standard_normal(3000) * np.exp(rng.uniform(-12, 6, 3000))).astype(np.float32))
+    grid = sorted(v for v, _ in _grid(fmt) if v >= 0)
+    xs += [np.float32((a + b) / 2) for a, b in zip(grid, grid[1:])]  # exact midpoints
+    xs += [np.float32(-x) for x in xs[-20:]] + [np.float32(top * 1.1), np.float32(-top * 3), np.float32(0.0)]
+    for x in xs:
+        assert enc(float(x)) == _encode_by_search(float(x), fmt), (fmt, float(x))
