@@ -54,8 +54,8 @@ GEMV_SOURCES = ("ferrite-strata_b200/csrc/k_gemv_mma.cu", "ferrite-strata_b200/c
 # epilogue (ncu: dram__bytes_read.sum + dram__bytes_write.sum of one launch,
 # cold cache, in a 2-layer decode step), keyed by (source digest, M, N, K).
 GEMV_TRAFFIC = {
-    ("5b752ad245761274", 8, 22016, 4096): 50817280 + 2816,
-    ("5b752ad245761274", 1, 22016, 4096): 50759936 + 9216,
+    ("c77fdfffe812c0b9", 8, 22016, 4096): 50817792 + 6656,
+    ("c77fdfffe812c0b9", 1, 22016, 4096): 50760192 + 11008,
 }
 
 

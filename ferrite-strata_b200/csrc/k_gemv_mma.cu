@@ -141,19 +141,19 @@ __device__ __forceinline__ void tile_epilogue(const Params& p, const TileRows& t
       const QkvExtra& e = p.qkv;
       const int hd = e.head_dim, half = hd / 2;
       const int head_in_job = nlo / hd, i = nlo % hd;  // i < half: the pair's first row
-      // The projection output is a bf16 value: round before the rotation.
-      double xlo = bf2f(f2bf(vlo)), xhi = bf2f(f2bf(vhi));
+      // The projection output is a bf16 value: round before the rotation,
+      // which runs in f32 as in rope_kernel.
+      float xlo = bf2f(f2bf(vlo)), xhi = bf2f(f2bf(vhi));
       const int pos = e.pos[m];
       if (jl < 2) {
         const double inv = e.inv_freq ? e.inv_freq[i] : pow(e.theta, -2.0 * double(i) / double(hd));
-        float snf, csf;
-        rope_cos_sin(pos, inv, csf, snf);
-        const double sn = snf, cs = csf;
-        const double a = xlo * cs - xhi * sn, b = xhi * cs + xlo * sn;
-        xlo = double(float(a));
-        xhi = double(float(b));
+        float sn, cs;
+        rope_cos_sin(pos, inv, cs, sn);
+        const float a = fmaf(xlo, cs, -xhi * sn), b = fmaf(xhi, cs, xlo * sn);
+        xlo = a;
+        xhi = b;
       }
-      const uint16_t olo = f2bf(float(xlo)), ohi = f2bf(float(xhi));
+      const uint16_t olo = f2bf(xlo), ohi = f2bf(xhi);
       if (jl == 0) {
         uint16_t* qo = e.q_out + int64_t(m) * e.hq * hd + head_in_job * hd;
         qo[i] = olo;
