@@ -88,19 +88,28 @@ class DecoderHandles:
     block_table: int = -1       # paged caches: I32 [batch, pages_per_seq], shared by every layer
 
 
-def ffn_shard(ffn: int, tp_world: int, tp_rank: int) -> tuple[int, int]:
+def ffn_unit(fmt: str) -> int:
+    """Features per FFN slice unit for weight format ``fmt``: 128 for the MX
+    formats (their GEMV stages four 32-code scale bytes of a row at a time,
+    so a down_proj shard's K is a multiple of 128), else 64 (two int4 groups,
+    the int4 GEMV's even group count)."""
+    return 128 if fmt in MX_CODES else 64
+
+
+def ffn_shard(ffn: int, tp_world: int, tp_rank: int, unit: int = 64) -> tuple[int, int]:
     """(first feature, features) of rank tp_rank's slice of the FFN.
 
-    Slices are whole units of 64 features (two int4 groups) where the FFN
-    allows it, so every rank's down_proj has an even number of 32-code
-    groups along K (the tensor-core GEMV's requirement); the first
-    (units % world) ranks take one unit more.  The 7B FFN of 11008 at 8
-    ranks splits as 4 x 1408 + 4 x 1344 instead of 8 x 1376 (43 groups).
-    Otherwise the FFN is split evenly."""
+    Slices are whole units of ``unit`` features (``ffn_unit`` of the weight
+    format) where the FFN allows it, so every rank's down_proj meets the
+    tensor-core GEMV's K rule; the first (units % world) ranks take one unit
+    more.  The 7B FFN of 11008 at 8 ranks splits as 4 x 1408 + 4 x 1344 in
+    64-feature units (instead of 8 x 1376, 43 int4 groups) and as
+    6 x 1408 + 2 x 1280 in 128-feature units.  Otherwise the FFN is split
+    evenly."""
     t, r = tp_world, tp_rank
-    if ffn % 64 == 0 and ffn // 64 >= t:
-        base, extra = divmod(ffn // 64, t)
-        return (r * base + min(r, extra)) * 64, (base + (1 if r < extra else 0)) * 64
+    if ffn % unit == 0 and ffn // unit >= t:
+        base, extra = divmod(ffn // unit, t)
+        return (r * base + min(r, extra)) * unit, (base + (1 if r < extra else 0)) * unit
     if ffn % t:
         raise ValueError("the ffn must divide by the tensor-parallel size")
     return r * (ffn // t), ffn // t
@@ -128,7 +137,7 @@ def weight_shapes(shape: DecoderShape, fmt: str, tp_world: int = 1, tp_rank: int
     t = tp_world
     if H % t or G % t:
         raise ValueError("heads and kv heads must divide by the tensor-parallel size")
-    Fr = ffn_shard(shape.ffn, t, tp_rank)[1]
+    Fr = ffn_shard(shape.ffn, t, tp_rank, ffn_unit(fmt))[1]
     act = F32 if fmt == "f32" else BF16
     mats = {"q": (H // t * d, D), "k": (G // t * d, D), "v": (G // t * d, D), "o": (D, H // t * d),
             "g": (Fr, D), "u": (Fr, D), "d": (D, Fr)}
@@ -235,7 +244,7 @@ def decoder_graph(shape: DecoderShape, *, batch: int, seq: int, max_len: int, fm
         h = b.node(Op.custom("fused::embed"), [hd.tokens, hd.embed_table], [(act, (R, D))], {}, "embed")[0]
     else:
         h = hd.tokens
-    Hl, Gl, Fl = H // t, G // t, ffn_shard(shape.ffn, t, tp_rank)[1]
+    Hl, Gl, Fl = H // t, G // t, ffn_shard(shape.ffn, t, tp_rank, ffn_unit(fmt))[1]
     for li, L in enumerate(hd.layers):
         W = L.ids
         p = f"l{li}."
@@ -299,15 +308,18 @@ def shard_layer(full: dict, shape: DecoderShape, fmt: str, rank: int, world: int
     ``full`` maps the names of ``weight_shapes(shape, fmt, 1)`` (and
     ``k_cache`` / ``v_cache``) to numpy arrays in the graph's layouts: int4
     codes [N, K/2] with bf16 scales [N, K/32], int8 codes [N, K] with f32
-    scales [N], or plain [N, K] weights.  Column-parallel matrices keep rows
+    scales [N], MX codes [N, K] (E4M3) or [N, K/2] (E2M1, two per byte) with
+    E8M0 scales [N, K/32], or plain [N, K] weights.  Column-parallel matrices keep rows
     [r*N/t, (r+1)*N/t); row-parallel ones keep columns [r*K/t, (r+1)*K/t) of
     the codes and the matching scale groups (per-channel int8 scales belong
     to the unsharded output rows and are kept whole).  The FFN dimension
-    (gate/up rows, down_proj columns) follows ``ffn_shard`` instead.  KV
-    caches keep their rank's kv heads.
+    (gate/up rows, down_proj columns) follows ``ffn_shard`` in the format's
+    ``ffn_unit`` instead.  KV caches, contiguous [batch, kv_heads, max_len,
+    head_dim] or page pools [pages, kv_heads, page_size, head_dim], keep
+    their rank's kv heads (the block table is the same on every rank).
     """
     t, r = world, rank
-    f0, fn = ffn_shard(shape.ffn, t, r)
+    f0, fn = ffn_shard(shape.ffn, t, r, ffn_unit(fmt))
     out = {}
     for name, arr in full.items():
         if name in ("attn_norm", "ffn_norm"):

@@ -18,7 +18,13 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, result_path):
+def _worker(rank, world, port, result_path, fmt="w4g32", page=0):
+    """One rank of a tensor-parallel decode step in weight format ``fmt``,
+    with page pools of ``page`` positions (contiguous caches when 0).  Every
+    rank also runs the unsharded step and checks its caches after the step
+    (read back through the block table when paged) against its kv heads of
+    the unsharded caches: exactly in layer 0, within the bf16 all-reduce
+    tolerance after it.  Rank 0 saves both steps' logits."""
     import sys
     for p in (ROOT, PKG):
         if p not in sys.path:
@@ -27,28 +33,41 @@ def _worker(rank, world, port, result_path):
     import torch.distributed as dist
     from oracle import graph_eval, oracle as ora
     from strata_host.blocks import DecoderShape, decoder_graph, shard_layer
-    from tests.helpers import seeded_graph_inputs
+    from tests.helpers import from_pages, page_table, seeded_graph_inputs, to_pages
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     shape = DecoderShape(256, 4, 2, 64, 512, 100, 2)
-    batch, max_len, fill = 2, 40, 30
-    full_g, full_hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt="w4g32", head="logits")
+    batch, max_len, fill = 2, 48, 30
+    full_g, full_hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt=fmt, head="logits")
     full = seeded_graph_inputs(full_g, cache_fill=fill)
     ids = ora.uniform_i32(2, batch, 0, shape.vocab)
     pos = np.array([fill, fill - 1], np.int32)
     full[full_hd.tokens], full[full_hd.pos] = ids, pos
 
-    g, hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt="w4g32", head="logits",
-                          tp_rank=rank, tp_world=world)
+    paged = {}
+    if page:
+        pps, npages = max_len // page, batch * (max_len // page) + 3
+        paged = {"kv_page": page, "kv_pages": npages}
+        table = page_table(batch, pps, npages, seed=9)
+    g, hd = decoder_graph(shape, batch=batch, seq=1, max_len=max_len, fmt=fmt, head="logits",
+                          tp_rank=rank, tp_world=world, **paged)
     inputs = {hd.tokens: ids, hd.pos: pos, hd.embed_table: full[full_hd.embed_table],
               hd.final_norm: full[full_hd.final_norm], hd.lm_w: full[full_hd.lm_w], hd.lm_s: full[full_hd.lm_s]}
+    if page:
+        inputs[hd.block_table] = table
     for li in range(shape.layers):
         layer_full = {k: full[v] for k, v in full_hd.layers[li].ids.items()}
-        shard = shard_layer(layer_full, shape, "w4g32", rank, world)
+        if page:
+            for c in ("k_cache", "v_cache"):
+                layer_full[c] = to_pages(layer_full[c], table, npages, fill_seed=21 + li)
+        shard = shard_layer(layer_full, shape, fmt, rank, world)
         for k, v in hd.layers[li].ids.items():
-            assert shard[k].shape == tuple(g.values[v].dims), (k, shard[k].shape, g.values[v].dims)
+            dims = tuple(g.values[v].dims)
+            if g.values[v].dtype.element == graph_eval.F4E2M1_E:  # two codes per byte
+                dims = dims[:-1] + ((dims[-1] + 1) // 2,)
+            assert shard[k].shape == dims, (k, shard[k].shape, dims)
             inputs[v] = shard[k]
 
     def all_reduce(_name, x):
@@ -56,44 +75,73 @@ def _worker(rank, world, port, result_path):
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         return ora.round_bf16(t.numpy())
 
-    got = graph_eval.evaluate(g, inputs, all_reduce=all_reduce)[hd.out]
+    vals = graph_eval.evaluate(g, inputs, all_reduce=all_reduce)
+    ref = graph_eval.evaluate(full_g, {k: (v.copy() if isinstance(v, np.ndarray) else v) for k, v in full.items()})
+    gl = shape.kv_heads // world
+    for li in range(shape.layers):
+        for c in ("k_cache", "v_cache"):
+            mine = vals[hd.layers[li].ids[c]]
+            if page:
+                mine = from_pages(mine, table)
+            want = ref[full_hd.layers[li].ids[c]][:, rank * gl:(rank + 1) * gl]
+            if li == 0:  # same normed input, same rows of k/v_proj: exact
+                assert np.array_equal(mine, want), f"rank {rank} layer {li} {c} after the step"
+            else:  # the input went through the bf16 all-reduce of layer 0
+                err = float(np.max(np.abs(mine - want)) / np.max(np.abs(want)))
+                assert err <= 2e-2, f"rank {rank} layer {li} {c}: {err:.3e}"
     if rank == 0:
-        want = graph_eval.evaluate(full_g, full)[full_hd.out]
-        np.save(result_path, np.stack([got, want]))
+        np.save(result_path, np.stack([vals[hd.out], ref[full_hd.out]]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_two_rank_tensor_parallel_step_matches_unsharded(tmp_path):
+@pytest.mark.parametrize("fmt,page", [("w4g32", 0), ("w4g32", 16), ("mxfp8", 0), ("mxfp4", 16)])
+def test_two_rank_tensor_parallel_step_matches_unsharded(tmp_path, fmt, page):
+    """Column-parallel q/k/v/gate/up, row-parallel o/down with a sum over the
+    ranks, for int4 and MX weights (codes and E8M0 scale groups sliced along
+    K) and for page pools sliced by kv head under one block table."""
     path = str(tmp_path / "tp.npy")
-    mp.start_processes(_worker, args=(2, _free_port(), path), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_worker, args=(2, _free_port(), path, fmt, page), nprocs=2, join=True,
+                       start_method="spawn")
     got, want = np.load(path)
     err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
     assert err <= 2e-2, f"tensor-parallel logits differ from unsharded by {err:.3e}"
 
 
+@pytest.mark.parametrize("fmt", ["w4g32", "mxfp8", "mxfp4"])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_ffn_shards_cover_the_ffn_with_even_group_counts(world):
-    """The 7B FFN (11008) at 8 ranks splits 4 x 1408 + 4 x 1344 (even int4 group counts for every
-    down_proj shard), and the shards of gate/up rows and down_proj codes / scales concatenate
-    back to the full matrices."""
+def test_ffn_shards_cover_the_ffn_in_whole_units(world, fmt):
+    """The 7B FFN (11008) at 8 ranks splits 4 x 1408 + 4 x 1344 for int4
+    (even int4 group counts for every down_proj shard) and 6 x 1408 +
+    2 x 1280 for MX (K a multiple of 128 for every down_proj shard), and the
+    shards of gate/up rows and down_proj codes / scales concatenate back to
+    the full matrices."""
     import numpy as np
 
-    from strata_host.blocks import LLAMA_7B, DecoderShape, ffn_shard, shard_layer, weight_shapes
+    from strata_host.blocks import LLAMA_7B, DecoderShape, ffn_shard, ffn_unit, shard_layer, weight_shapes
     shape = DecoderShape(256, 8, 8, 32, 11008, 0, 1)
+    unit = ffn_unit(fmt)
+    assert unit == (64 if fmt == "w4g32" else 128)
     full = {}
-    for name, (dt, dims) in weight_shapes(shape, "w4g32").items():
+    for name, (dt, dims) in weight_shapes(shape, fmt).items():
+        dims = tuple(dims)
+        if fmt == "mxfp4" and name[0] == "w":  # E2M1 codes are stored two per byte
+            dims = dims[:-1] + (dims[-1] // 2,)
         full[name] = np.arange(int(np.prod(dims)), dtype=np.int64).reshape(dims)
-    shards = [shard_layer(full, shape, "w4g32", r, world) for r in range(world)]
+    shards = [shard_layer(full, shape, fmt, r, world) for r in range(world)]
     for r in range(world):
-        f0, fn = ffn_shard(shape.ffn, world, r)
-        assert fn % 64 == 0 and (fn // 32) % 2 == 0
-        ws = weight_shapes(shape, "w4g32", world, r)
+        f0, fn = ffn_shard(shape.ffn, world, r, unit)
+        assert fn % unit == 0
+        ws = weight_shapes(shape, fmt, world, r)
         for name in ("wg", "sg", "wu", "su", "wd", "sd"):
-            assert shards[r][name].shape == ws[name][1], (name, r)
+            want = tuple(ws[name][1])
+            if fmt == "mxfp4" and name[0] == "w":
+                want = want[:-1] + (want[-1] // 2,)
+            assert shards[r][name].shape == want, (name, r)
     for name, axis in (("wg", 0), ("sg", 0), ("wu", 0), ("su", 0), ("wd", 1), ("sd", 1)):
         assert np.array_equal(np.concatenate([s[name] for s in shards], axis=axis), full[name]), name
-    assert [ffn_shard(LLAMA_7B.ffn, 8, r)[1] for r in range(8)] == [1408] * 4 + [1344] * 4
+    want7b = [1408] * 4 + [1344] * 4 if unit == 64 else [1408] * 6 + [1280] * 2
+    assert [ffn_shard(LLAMA_7B.ffn, 8, r, unit)[1] for r in range(8)] == want7b
 
 
 def _worker_argmax(rank, world, port, result_path):
