@@ -3,10 +3,12 @@
 #include "k_elem.cuh"
 #include "k_gemv_mma.cuh"
 
+#include <algorithm>
 #include <cstdlib>
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 namespace sb {
 std::atomic<uint64_t> g_launches{0};
@@ -26,22 +28,35 @@ static inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s)
 
 // Weight-expansion scratch of the linear entry points: one grow-only device
 // buffer per (device, stream).  Work on one stream runs in order, so a buffer
-// is never used by two launches at once; one that must grow is released with
-// cudaFreeAsync on its stream (after the work already queued there) and
-// replaced.  The buffers live until the process exits.
+// is never used by two launches at once.  A buffer that must grow is
+// replaced by one of at least twice its size and the old one is kept, never
+// freed: a CUDA graph captured from an earlier call may still name it (the
+// kept buffers add up to less than the live one).  Allocation is a plain
+// cudaMalloc in the relaxed capture mode, so a call made while its stream is
+// being captured gets ordinary device memory, valid outside the graph too,
+// rather than a graph-owned allocation.  The buffers live until the process
+// exits.
 static void* linear_scratch(cudaStream_t st, size_t bytes) {
   static std::mutex mu;
   static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> bufs;
+  static std::vector<void*> kept;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
   std::lock_guard<std::mutex> lk(mu);
   auto& e = bufs[{dev, st}];
   if (e.first && e.second >= bytes) return e.first;
-  if (e.first) cudaFreeAsync(e.first, st);
-  e = {nullptr, 0};
+  const size_t want = std::max(bytes, 2 * e.second);
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  cudaThreadExchangeStreamCaptureMode(&mode);
   void* p = nullptr;
-  if (cudaMallocAsync(&p, bytes, st) != cudaSuccess) return nullptr;
-  e = {p, bytes};
+  const cudaError_t rc = cudaMalloc(&p, want);
+  cudaThreadExchangeStreamCaptureMode(&mode);
+  if (rc != cudaSuccess) {
+    cudaGetLastError();  // leave no sticky error for the caller's next check
+    return nullptr;
+  }
+  if (e.first) kept.push_back(e.first);
+  e = {p, want};
   return p;
 }
 

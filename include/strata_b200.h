@@ -132,8 +132,11 @@ int32_t strata_b200_linear_mxfp4(const uint16_t *x, int64_t m, int64_t k,
  * bf16 weights [n, k]: the reference's f32 `linear` (crates/ferrite-strata-cpu/
  * src/backend.rs:607-637) in bf16 storage with f32 accumulation.  k must be a
  * multiple of 8.  Batches of more than 64 rows run on the tcgen05 tensor cores
- * (so do the int4 and int8 entry points above, after expanding the weights
- * into a stream-ordered temporary). */
+ * (so do the int4, int8 and MX entry points, after expanding the weights into
+ * a bf16 scratch buffer the library keeps per device and stream; a call that
+ * needs a larger one than it has allocates it with cudaMalloc, also while the
+ * stream is being captured, and the smaller one stays allocated for graphs
+ * that name it). */
 int32_t strata_b200_linear_bf16(const uint16_t *x, int64_t m, int64_t k,
                                 const uint16_t *w, int64_t n,
                                 const uint16_t *residual, uint16_t *y,
