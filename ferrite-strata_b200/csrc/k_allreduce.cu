@@ -289,23 +289,35 @@ __global__ void __launch_bounds__(kAmThreads)
   pdl_trigger();
   pdl_wait();  // the logits come from the preceding kernel
   const int b = blockIdx.x, tid = threadIdx.x;
-  const int nmine = rows > b ? int((rows - b + kAmBlocks - 1) / kAmBlocks) : 0;
-  for (int j = 0; j < nmine; ++j) {
+  const int64_t nmine = rows > b ? (rows - b + kAmBlocks - 1) / kAmBlocks : 0;
+  if (world <= 1 || keys_out) {
+    // No exchange: each row's key (or id) goes straight to global memory,
+    // so any number of rows fits.
+    for (int64_t j = 0; j < nmine; ++j) {
+      const int64_t row = b + j * kAmBlocks;
+      const uint64_t k = am_row_key(x + row * cols, cols, offset, red);
+      if (tid == 0) {
+        if (keys_out)
+          keys_out[row] = k;
+        else
+          out[row] = am_id(k);
+      }
+    }
+    return;
+  }
+  // The exchange stages this block's keys in s_key; the launcher refuses
+  // more than kAmMaxRows rows, and every rank sees the same row count, so
+  // all ranks leave here together if that check was bypassed.
+  if (nmine > kAmMaxRows / kAmBlocks) {
+    if (tid == 0 && err) atomicExch(err, 1);
+    return;
+  }
+  for (int j = 0; j < int(nmine); ++j) {
     const int64_t row = b + int64_t(j) * kAmBlocks;
     const uint64_t k = am_row_key(x + row * cols, cols, offset, red);
     if (tid == 0) s_key[j] = k;
   }
   __syncthreads();
-  if (world <= 1 || keys_out) {
-    for (int j = tid; j < nmine; j += blockDim.x) {
-      const int64_t row = b + int64_t(j) * kAmBlocks;
-      if (keys_out)
-        keys_out[row] = s_key[j];
-      else
-        out[row] = am_id(s_key[j]);
-    }
-    return;
-  }
   const int fb = kAmFlag0 + b;
   if (tid == 0) {
     s_gen = counters[fb] + 1;

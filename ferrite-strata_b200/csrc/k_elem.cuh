@@ -147,7 +147,8 @@ int launch_allreduce_add_norm_bf16(const uint16_t* x, const uint16_t* r, const u
 // over all ranks' columns with the replicated argmax's rules (NaN skipped,
 // lowest id on ties, 0 for a row of NaNs).  world == 1 needs no peers.  With
 // keys set, the rank's 64-bit keys go there instead (for a u64 max all-reduce
-// by NCCL, then launch_vocab_argmax_decode).
+// by NCCL, then launch_vocab_argmax_decode).  The peer exchange (world > 1,
+// no keys) takes at most kAmMaxRows rows; the other two forms take any.
 constexpr int kAmMaxRows = 4096;  // rows of one exchange
 template <typename T>
 int launch_vocab_argmax(const T* x, int64_t rows, int64_t cols, int64_t offset, int rank, int world,

@@ -372,11 +372,13 @@ def test_device_quantize_node_is_bit_exact(cuda, plugin):
 
 
 @pytest.mark.parametrize("dtype", [BF16, F32])
-@pytest.mark.parametrize("rows,cols,offset", [(1, 4000, 0), (37, 1000, 64000), (300, 16, 31984)])
+@pytest.mark.parametrize("rows,cols,offset", [(1, 4000, 0), (37, 1000, 64000), (300, 16, 31984), (5000, 16, 0)])
 def test_vocab_argmax_node_on_one_rank(cuda, plugin, dtype, rows, cols, offset):
     """fused::vocab_argmax outside a tensor-parallel group: the argmax of the
     shard plus its first vocabulary id, with the replicated argmax's rules --
-    NaN skipped, the lowest id on ties (-0 and +0 tie), 0 for a row of NaNs."""
+    NaN skipped, the lowest id on ties (-0 and +0 tie), 0 for a row of NaNs.
+    5000 rows is more than one peer exchange takes; without an exchange any
+    row count is served."""
     b = GraphBuilder("vargmax")
     x = b.input(dtype, (rows, cols), "logits")
     out = b.node(Op.custom("fused::vocab_argmax"), [x], [(I32, (rows,))], {"vocab_offset": offset}, "va")[0]
