@@ -519,13 +519,24 @@ template <int FMT, int NT, int MODE, int W>
 int launch_w(Params p, bool scale16_ok, bool pdl, cudaStream_t st) {
   auto kern = gemv_mma_kernel<FMT, NT, MODE, W>;
   const size_t smem = W * warp_smem_bytes(FMT);
-  static int per_sm = 0;
-  if (per_sm == 0) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
-      return SB_INTERNAL;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, W * 32, smem) != cudaSuccess || per_sm < 1)
-      per_sm = 1;
-  }
+  // The shared-memory limit is a per-device setting: raise it on every
+  // device that launches this instance.  Resident blocks per SM are the same
+  // on every B200.
+  static PerDeviceOnce configured;
+  static std::atomic<int> resident{1};
+  if (!configured.run([&] {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+          return false;
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, W * 32, smem) != cudaSuccess || n < 1) {
+          cudaGetLastError();
+          n = 1;
+        }
+        resident.store(n, std::memory_order_relaxed);
+        return true;
+      }))
+    return SB_INTERNAL;
+  const int per_sm = resident.load(std::memory_order_relaxed);
   p.gpw = (p.groups + W - 1) / W;
   p.gpw += p.gpw & 1;  // even slice starts keep the bf16 scale pairs 4-byte aligned
   if (FMT >= 2) p.gpw = (p.gpw + 3) & ~3;  // E8M0 scales are copied 4 bytes (groups) at a time
