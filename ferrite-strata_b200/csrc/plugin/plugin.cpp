@@ -97,21 +97,32 @@ int env_int(const char* name, int dflt) {
 
 bool graphs_enabled() { return env_int("STRATA_B200_CUDA_GRAPHS", 1) != 0 && !step_times_enabled(); }
 
-// Cache of device allocations by rounded size, so per-run buffers (the
-// reference host allocates one per value per run) do not hit cudaMalloc.
+// Cache of device allocations by (device, rounded size), so per-run buffers
+// (the reference host allocates one per value per run) do not hit
+// cudaMalloc.  Every context of the process shares it, so it has its own
+// lock, and a buffer is only handed out again on the device it was made on.
 struct Pool {
-  std::multimap<uint64_t, void*> free_;
-  void* get(uint64_t bytes) {
-    auto it = free_.find(bytes);
+  std::mutex mu;
+  std::multimap<std::pair<int, uint64_t>, void*> free_;
+  void* get(int dev, uint64_t bytes) {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = free_.find({dev, bytes});
     if (it == free_.end()) return nullptr;
     void* p = it->second;
     free_.erase(it);
     return p;
   }
-  void put(uint64_t bytes, void* p) { free_.emplace(bytes, p); }
-  void drain() {
-    for (auto& kv : free_) cudaFree(kv.second);
-    free_.clear();
+  void put(int dev, uint64_t bytes, void* p) {
+    std::lock_guard<std::mutex> lk(mu);
+    free_.emplace(std::make_pair(dev, bytes), p);
+  }
+  // Frees device dev's cached buffers; the caller has that device current.
+  void drain(int dev) {
+    std::lock_guard<std::mutex> lk(mu);
+    for (auto it = free_.lower_bound({dev, 0}); it != free_.end() && it->first.first == dev;) {
+      cudaFree(it->second);
+      it = free_.erase(it);
+    }
   }
 };
 Pool g_pool;
@@ -120,21 +131,20 @@ uint64_t round_bytes(uint64_t b) { return (std::max<uint64_t>(b, 1) + 255) & ~ui
 
 void* device_alloc(Ctx& c, uint64_t bytes) {
   const uint64_t rb = round_bytes(bytes);
-  if (void* p = g_pool.get(rb)) return p;
+  if (void* p = g_pool.get(c.device, rb)) return p;
   void* p = nullptr;
   cudaError_t e = cudaMalloc(&p, rb);
   if (e == cudaErrorMemoryAllocation) {
     cudaGetLastError();
-    g_pool.drain();
+    g_pool.drain(c.device);
     e = cudaMalloc(&p, rb);
   }
   cuda_check(e, "cudaMalloc");
-  (void)c;
   return p;
 }
 
-void device_free(uint64_t bytes, void* p) {
-  if (p) g_pool.put(round_bytes(bytes), p);
+void device_free(Ctx& c, uint64_t bytes, void* p) {
+  if (p) g_pool.put(c.device, round_bytes(bytes), p);
 }
 
 }  // namespace
@@ -547,7 +557,7 @@ static int32_t sb_buffer_release(void* ctx, StrataBuffer* b) {
   if (b->b.owned && b->b.ptr) {
     // The stream may still be reading it; release only after queued work.
     if (c->device_ready) cudaStreamSynchronize(c->stream);
-    device_free(b->b.bytes, b->b.ptr);
+    device_free(*c, b->b.bytes, b->b.ptr);
   }
   delete b;
   return STRATA_OK;
@@ -825,7 +835,7 @@ static void sb_plugin_free(void* ctx) {
     cudaStreamSynchronize(c->stream);
     c->teardown_allreduce();
     if (c->comm) c->nccl.comm_destroy(c->comm);
-    g_pool.drain();
+    g_pool.drain(c->device);
     cudaFree(c->d_err);
     cudaStreamDestroy(c->stream);
   }
