@@ -444,7 +444,7 @@ class Executable:
             for idx in g.outputs:
                 v = g.values[idx]
                 if idx in kept:
-                    arena[idx] = Device(kept[idx])
+                    arena[idx] = Device(kept.pop(idx))
                     continue
                 entry = arena.get(idx)
                 buf_handle = refs[idx].buffer
@@ -454,6 +454,8 @@ class Executable:
                 arena[idx] = _decode_host(b.read(v.nbytes), v.dtype, v.dims)
         finally:
             for b in temp:
+                b.release()
+            for b in kept.values():  # device-resident outputs that never reached the arena
                 b.release()
         return arena
 
